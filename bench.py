@@ -1,0 +1,501 @@
+#!/usr/bin/env python
+"""Benchmark of the 4-bit affine group-64 quantized matmul hot path.
+
+Headline (BASELINE metric "4-bit qmatmul HBM GB/s & % peak at M=1/16; 27B
+linear-stack tok/s"): decode tokens/s of the 64-layer Qwen 27B linear stack at
+M=1 (q|k|v 5120->8192, o 6144->5120, gate|up 5120->34816, down 17408->5120 per
+layer, then lm_head 5120->151936), synthetic seeded weights quantized on the
+GPU by the library's own quantizer.  One step = one token through the stack.
+
+  value   device-resident inputs, the step captured once as a CUDA graph of
+          the library's launches (programmatic dependent launch between them)
+  e2e     the same step through the public C ABI call by call (qw_quantized_matmul
+          via ctypes), x copied from pinned host memory before and the logits
+          read back after, every step
+Extra keys report the single-matrix qmv (M=1) and verify qmm (M=16) GB/s with
+L2 defeated by rotating weight copies, and the M=16 stack.
+
+With torchrun (N > 1) the stack is tensor-parallel: q/k/v/gate/up/lm_head
+column-sharded, o/down row-sharded with an fp32 NCCL allreduce.  Rank 0 prints
+one JSON line.  `--impl reference` times the reference's CPU path (the oracle
+restatement of MLX's affine quantized_matmul; the reference itself cannot be
+built here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from qw_b200 import synth, tp  # noqa: E402
+
+METRIC = "4-bit qmatmul HBM GB/s & % peak at M=1/16; 27B linear-stack tok/s"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profile_traffic(key):
+    """DRAM bytes per launch from a committed ncu summary (profiles/traffic.txt)."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == key:
+                return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = str(index)
+        self.proc = None
+        try:  # nvidia-smi numbers GPUs differently from CUDA_VISIBLE_DEVICES; use the UUID
+            import torch
+            u = str(torch.cuda.get_device_properties(int(index)).uuid)
+            self.index = u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            pass
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.index, f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------ the GPU arm
+def make_weights(torch, qw, N, K, seed, dev):
+    """N x K fp16 ~ N(0, 0.02), quantized on the GPU; returns (wq, scales, biases)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    wq = torch.empty(N, K // 8, dtype=torch.int32, device=dev)
+    s = torch.empty(N, K // 64, dtype=torch.float16, device=dev)
+    b = torch.empty(N, K // 64, dtype=torch.float16, device=dev)
+    rows = max(1, (1 << 27) // K)  # quantize in slabs of ~256 MB of fp16
+    for r0 in range(0, N, rows):
+        r1 = min(N, r0 + rows)
+        w = (torch.randn(r1 - r0, K, generator=g, device=dev, dtype=torch.float32) * 0.02).half()
+        wq_s, s_s, b_s = qw.quantize_weights(w)
+        wq[r0:r1].copy_(wq_s)
+        s[r0:r1].copy_(s_s)
+        b[r0:r1].copy_(b_s)
+        del w, wq_s, s_s, b_s
+    return wq, s, b
+
+
+def build_stack(torch, qw, P, rank, layers, dev):
+    ws = []
+    for l in range(layers):
+        d = {}
+        for lin in synth.layer_linears():
+            N, K = tp.shard_shape(lin, P)
+            d[lin.name] = make_weights(torch, qw, N, K, seed=(l * 16 + lin.tid) * 64 + rank, dev=dev)
+        ws.append(d)
+    N, K = tp.shard_shape(synth.LM_HEAD, P)
+    lm = make_weights(torch, qw, N, K, seed=(99 * 16 + 9) * 64 + rank, dev=dev)
+    return ws, lm
+
+
+class StackRunner:
+    """Fixed buffers + the per-step launch sequence, for graph capture and eager e2e."""
+
+    def __init__(self, torch, qw, ws, lm, M, P, group):
+        self.torch, self.qw, self.ws, self.lm, self.M, self.P, self.group = torch, qw, ws, lm, M, P, group
+        dev = lm[0].device
+        H = synth.HIDDEN
+        f16, f32 = torch.float16, torch.float32
+        self.h = torch.randn(M, H, device=dev).half()
+        nq = tp.shard_shape(synth.layer_linears()[0], P)[0]
+        ngu = tp.shard_shape(synth.layer_linears()[2], P)[0]
+        self.qkv = torch.empty(M, nq, dtype=f16, device=dev)
+        self.attn = torch.empty(M, synth.Q_OUT // P, dtype=f16, device=dev)
+        self.gu = torch.empty(M, ngu, dtype=f16, device=dev)
+        self.gate = torch.empty(M, synth.INTER // P, dtype=f16, device=dev)
+        self.part = torch.empty(M, H, dtype=f32, device=dev)
+        self.o = torch.empty(M, H, dtype=f16, device=dev)
+        self.logits = torch.empty(M, lm[0].shape[0], dtype=f16, device=dev)
+        self.launches_per_step = 4 * len(ws) + 1
+
+    def _mm(self, x, w, out):
+        self.qw.quantized_matmul(x, w[0], w[1], w[2], out=out)
+
+    def _rowpar(self, x, w, out16):
+        if self.P == 1:
+            self._mm(x, w, out16)
+            return
+        self._mm(x, w, self.part)
+        self.torch.distributed.all_reduce(self.part, group=self.group)
+        out16.copy_(self.part)
+
+    def step(self):
+        M = self.M
+        for w in self.ws:
+            self._mm(self.h, w["qkv"], self.qkv)
+            if M == 1:
+                attn = self.qkv[:, : self.attn.shape[1]]
+            else:
+                self.attn.copy_(self.qkv[:, : self.attn.shape[1]])
+                attn = self.attn
+            self._rowpar(attn, w["o"], self.o)
+            self._mm(self.o, w["gate_up"], self.gu)
+            if M == 1:
+                gate = self.gu[:, : self.gate.shape[1]]
+            else:
+                self.gate.copy_(self.gu[:, : self.gate.shape[1]])
+                gate = self.gate
+            self._rowpar(gate, w["down"], self.h)
+        self._mm(self.h, self.lm, self.logits)
+
+
+def timed_graph(torch, runner, steps, warmup, stream, dist_on, sampler_index):
+    """Capture one step as a CUDA graph and time `steps` replays (max over ranks)."""
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            runner.step()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        runner.step()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            g.replay()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(sampler_index) as cs:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    ms = e0.elapsed_time(e1) / steps
+    ms = reduce_max(torch, ms, dist_on)
+    del g
+    return ms, cs.summary()
+
+
+def timed_e2e(torch, runner, steps, warmup, stream, dist_on):
+    """Eager C-ABI calls; h2d of x from pinned memory and d2h of logits every step."""
+    M = runner.M
+    x_host = torch.randn(M, synth.HIDDEN).half().pin_memory()
+    y_host = torch.empty(runner.logits.shape, dtype=torch.float16).pin_memory()
+
+    def one():
+        runner.h.copy_(x_host, non_blocking=True)
+        runner.step()
+        y_host.copy_(runner.logits, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            one()
+    stream.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            one()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = reduce_max(torch, e0.elapsed_time(e1) / steps, dist_on)
+    return ms, x_host.numel() * 2, y_host.numel() * 2
+
+
+def reduce_max(torch, v, dist_on):
+    if not dist_on:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50):
+    """One quantized matmul, rotating `copies` weight sets (> L2) between launches."""
+    sets = [make_weights(torch, qw, N, K, seed=7000 + i, dev=dev) for i in range(copies)]
+    x = torch.randn(M, K, device=dev).half()
+    y = torch.empty(M, N, dtype=torch.float16, device=dev)
+    s = torch.cuda.Stream(dev)
+    with torch.cuda.stream(s):
+        for i in range(copies * 2):
+            w = sets[i % copies]
+            qw.quantized_matmul(x, w[0], w[1], w[2], out=y)
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(copies):
+            w = sets[i % copies]
+            qw.quantized_matmul(x, w[0], w[1], w[2], out=y)
+    with torch.cuda.stream(s):
+        g.replay()
+    s.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(iters):
+            g.replay()
+        e1.record(s)
+    s.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (iters * copies)
+    nbytes = synth.algorithmic_bytes(M, N, K)
+    del g, sets
+    torch.cuda.empty_cache()
+    return us, nbytes / (us * 1e-6) / 1e9
+
+
+def cpu_sample_rate(ws_host, threads):
+    """Oracle over one layer's host copy of the GPU's quantized weights: GB/s."""
+    import oracle
+    M = 1
+    t_total, b_total = 0.0, 0
+    for name, (wq, s, b) in ws_host.items():
+        N, K = wq.shape[0], wq.shape[1] * 8
+        x = synth.activations(M, K, seed=1)
+        oracle.quantized_matmul(x, wq[:64], s[:64], b[:64], nthreads=threads)  # warm
+        t0 = time.perf_counter()
+        oracle.quantized_matmul(x, wq, s, b, nthreads=threads)
+        t_total += time.perf_counter() - t0
+        b_total += synth.algorithmic_bytes(M, N, K)
+    return b_total / t_total / 1e9, t_total
+
+
+def run_ours(args):
+    import torch
+    import qw_b200 as qw
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist_on = world > 1
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if dist_on:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+        group = torch.distributed.group.WORLD
+    P = world
+    hbm_peak, tf_peak, peak_src = peaks()
+
+    ws, lm = build_stack(torch, qw, P, rank, args.layers, dev)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(dev)
+
+    runner = StackRunner(torch, qw, ws, lm, 1, P, group)
+    ms, clocks = timed_graph(torch, runner, args.steps, args.warmup, stream, dist_on, local)
+    step_bytes = synth.stack_bytes(1, layers=args.layers) // P if P > 1 else synth.stack_bytes(1, layers=args.layers)
+    tok_s = 1000.0 / ms
+    launches = runner.launches_per_step
+
+    e2e_ms, h2d, d2h = timed_e2e(torch, runner, args.steps, args.warmup, stream, dist_on)
+
+    extra = {}
+    if not args.skip_extra:
+        runner16 = StackRunner(torch, qw, ws, lm, 16, P, group)
+        ms16, _ = timed_graph(torch, runner16, max(10, args.steps // 4), args.warmup, stream, dist_on, local)
+        b16 = synth.stack_bytes(16, layers=args.layers) // P
+        extra["stack_m16"] = {"tok_s": round(16 * 1000.0 / ms16, 1), "ms_per_step": round(ms16, 4),
+                              "GBps_per_gpu": round(b16 / (ms16 * 1e-3) / 1e9, 1),
+                              "frac_hbm": round(b16 / (ms16 * 1e-3) / 1e9 / hbm_peak, 4)}
+        del runner16
+        if rank == 0 and P == 1:
+            for M in (1, 4, 16):
+                us, gbs = kernel_microbench(torch, qw, M, 17408, 5120, dev)
+                extra[f"qmm_17408x5120_m{M}"] = {"us": round(us, 2), "GBps": round(gbs, 1),
+                                                 "frac_hbm": round(gbs / hbm_peak, 4),
+                                                 "frac_8TBps": round(gbs / 8000.0, 4)}
+
+    result = {
+        "metric": METRIC,
+        "value": round(tok_s, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 5),
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
+        "dtype": "f16 activations, u4 weights, f32 accumulate",
+        "data": "synthetic: x~N(0,1), W~N(0,0.02) fp16 quantized on GPU (affine, 4-bit, group 64)",
+        "config": {"workload": f"decode linear stack M=1, {args.layers} layers (qkv/o/gate_up/down) + lm_head",
+                   "M": 1, "layers": args.layers, "hidden": synth.HIDDEN, "vocab": synth.VOCAB,
+                   "parallelism": f"tp{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (weights %.2f GB per step)" % (synth.stack_bytes(1, args.layers) / 1e9),
+                   "graph": "one CUDA graph per step, programmatic dependent launch"},
+        "GBps_per_gpu": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+        "roofline": None,
+        "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
+                "path": "qw_quantized_matmul per layer via ctypes, eager, pinned host x in / logits out"},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks,
+        "extra": extra,
+    }
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    traffic = profile_traffic("qmm_skinny_m1_stack_step")
+    result["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                          "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
+                          "kernel": "qmm_skinny_kernel (every launch of the step)",
+                          "traffic": traffic}
+
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        ws_host = {n: tuple(t.cpu().numpy().view(np.uint32) if i == 0 else t.cpu().numpy()
+                            for i, t in enumerate(ws[0][n])) for n in ws[0]}
+        threads = os.cpu_count() or 1
+        gbs, secs = cpu_sample_rate(ws_host, threads)
+        result["cpu_baseline"] = {
+            "value": round(gbs * 1e9 / synth.stack_bytes(1, args.layers), 4), "unit": "tok/s", "cores": threads,
+            "kind": "port", "GBps": round(gbs, 3),
+            "sample": f"one decoder layer (4 matmuls, M=1, {secs:.2f} s) through the C oracle with OpenMP; "
+                      f"tok/s = GB/s / {synth.stack_bytes(1, args.layers)} bytes per token"}
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def run_reference(args):
+    """The reference's CPU path (oracle restatement) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import oracle
+    threads = os.cpu_count() or 1
+    # Per step: a slab of rows of one decoder layer, sized so warmup + steps
+    # finish in about two minutes on this host.
+    budget_s = 120.0 / max(1, args.steps + args.warmup)
+    lins = synth.layer_linears()
+    mats = {}
+    for lin in lins:
+        w = synth.weight_fp16(512, lin.K, seed=lin.tid)
+        mats[lin.name] = oracle.quantize(w)
+    x = {lin.K: synth.activations(1, lin.K, seed=2) for lin in lins}
+    # rate probe
+    t0 = time.perf_counter()
+    for lin in lins:
+        wq, s, b = mats[lin.name]
+        oracle.quantized_matmul(x[lin.K], wq, s, b, nthreads=threads)
+    probe = time.perf_counter() - t0
+    rows = int(max(16, min(512, 512 * budget_s / max(probe, 1e-6))))
+    rows -= rows % 16
+    rows = max(16, rows)
+    for _ in range(args.warmup):
+        for lin in lins:
+            wq, s, b = mats[lin.name]
+            oracle.quantized_matmul(x[lin.K], wq[:rows], s[:rows], b[:rows], nthreads=threads)
+    t0 = time.perf_counter()
+    nbytes = 0
+    for _ in range(args.steps):
+        for lin in lins:
+            wq, s, b = mats[lin.name]
+            oracle.quantized_matmul(x[lin.K], wq[:rows], s[:rows], b[:rows], nthreads=threads)
+            nbytes += synth.algorithmic_bytes(1, rows, lin.K)
+    dt = time.perf_counter() - t0
+    gbs = nbytes / dt / 1e9
+    tok_s = gbs * 1e9 / synth.stack_bytes(1, args.layers)
+    sample = (f"{rows} rows of each of qkv/o/gate_up/down per step through the C oracle (OpenMP, {threads} threads); "
+              f"tok/s = GB/s / {synth.stack_bytes(1, args.layers)} bytes per token")
+    out = {
+        "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1000 / args.steps, 4),
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "f16 activations, u4 weights, f32 accumulate", "data": "synthetic (seeded)",
+        "config": {"workload": f"decode linear stack M=1, {args.layers} layers + lm_head", "M": 1,
+                   "layers": args.layers, "parallelism": "host cores"},
+        "GBps": round(gbs, 3),
+        "cpu_baseline": {"value": round(tok_s, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(tok_s, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "MLX (the reference's arithmetic) is not installable here; this is the oracle restatement",
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=synth.LAYERS)
+    ap.add_argument("--skip-extra", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,122 @@
+/*
+ * qw_qmm.h -- C ABI of the B200 affine group-quantized matmul library
+ * (libqwqmm.so).  Drop-in for the quantized-linear operator surface that
+ * cr0sh/qw's mlxcel-core exposes to its runtime crate: every entry point
+ * below replaces one cxx bridge function, cited as
+ *   crates/mlxcel-core/src/lib.rs:<line>             (Rust declaration)
+ *   crates/mlxcel-core/cpp/mlx_cxx_bridge.cpp:<line> (C++ shim)
+ *
+ * Conventions
+ *  - All tensors are device memory owned by the caller, described by
+ *    qw_array (row-contiguous; leading dimensions of x / y are flattened, as
+ *    MLX does).  Outputs are preallocated by the caller.
+ *  - Every launch is stream-ordered on `stream` (a cudaStream_t; NULL = the
+ *    legacy default stream).  Calls on distinct streams may run concurrently.
+ *  - Errors are returned as qw_status codes and never abort; the message of
+ *    the last failing call on this host thread is qw_last_error().  The
+ *    reference has no error channel at this boundary (an MLX throw crosses the
+ *    cxx bridge as std::terminate, crates/mlxcel-core/src/layers.rs:1255-1285),
+ *    so the checks it performs at load time (layers.rs:1286-1318, :1409-1440,
+ *    :1783-1868) are performed here on every call instead.
+ *  - Supported quantization: mode "affine", bits 4, group_size 64, activations
+ *    and scales/biases fp16 (the Qwen 27B checkpoint, crates/runtime/src/
+ *    qwen3_5.rs:208-211).  Other combinations MLX accepts return
+ *    QW_EUNSUPPORTED.
+ */
+#ifndef QW_QMM_H
+#define QW_QMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QW_ABI_VERSION 1
+
+typedef enum qw_status {
+  QW_OK = 0,
+  QW_EINVAL = 1,       /* shapes, dtypes or parameters inconsistent */
+  QW_EUNSUPPORTED = 2, /* valid for MLX, not implemented here (bits, group size, mode, dtype) */
+  QW_ECUDA = 3,        /* a CUDA runtime call failed */
+  QW_ETIMEOUT = 4,     /* a kernel gave up on a bounded wait (see qw_device_status) */
+  QW_ENOMEM = 5        /* scratch allocation failed */
+} qw_status;
+
+typedef enum qw_dtype {
+  QW_U32 = 1,
+  QW_F16 = 2,
+  QW_BF16 = 3,
+  QW_F32 = 4
+} qw_dtype;
+
+/* A device array: the role of MlxArray (crates/mlxcel-core/cpp/mlx_cxx_bridge.h:16-22)
+ * at this boundary.  strides are in elements; a stride array of all zeros is
+ * read as row-contiguous. */
+typedef struct qw_array {
+  void* data;
+  int32_t dtype; /* qw_dtype */
+  int32_t ndim;  /* 1..4 */
+  int64_t shape[4];
+  int64_t strides[4];
+} qw_array;
+
+/* y = x @ dequantize(w, scales, biases).T  (transpose != 0)
+ * x: f16 [..., K]; w: u32 [N, K*bits/32]; scales, biases: f16 [N, K/group_size];
+ * y: f16 [..., N], or f32 [..., N] to receive the fp32 accumulators unrounded
+ * (the row-parallel partial sums of a tensor-parallel shard).
+ * transpose == 0 (y = x @ dequantize(w)) returns QW_EUNSUPPORTED.
+ * Replaces: quantized_matmul, lib.rs:1134-1143, mlx_cxx_bridge.cpp:2991-3017. */
+int qw_quantized_matmul(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
+                        int transpose, int group_size, int bits, const char* mode, qw_array* y, void* stream);
+
+/* y = x @ dequantize(w).T (+ linear_bias), linear_bias nullable f16 [N].
+ * Replaces: quantized_linear_forward, lib.rs:591-601, mlx_cxx_bridge.cpp:1099-1133. */
+int qw_quantized_linear_forward(const qw_array* x, const qw_array* w, const qw_array* scales,
+                                const qw_array* biases, const qw_array* linear_bias, int group_size, int bits,
+                                const char* mode, qw_array* y, void* stream);
+
+/* y = fp16(fp16(x @ dequantize(w).T) * global_scale) (+ linear_bias).
+ * global_scale nullable, f32 scalar in device memory.
+ * Replaces: quantized_linear_forward_global_scale, lib.rs:604-615,
+ * mlx_cxx_bridge.cpp:1135-1170. */
+int qw_quantized_linear_forward_global_scale(const qw_array* x, const qw_array* w, const qw_array* scales,
+                                             const qw_array* biases, const qw_array* global_scale,
+                                             const qw_array* linear_bias, int group_size, int bits,
+                                             const char* mode, qw_array* y, void* stream);
+
+/* out f16 [N, K] = scales * q + biases, each product and sum rounded to fp16
+ * (the fp16 op-by-op evaluation of MLX's CPU backend).
+ * Replaces: dequantize, lib.rs:1152-1159, mlx_cxx_bridge.cpp:3019-3069. */
+int qw_dequantize(const qw_array* w, const qw_array* scales, const qw_array* biases, int group_size, int bits,
+                  const char* mode, qw_array* out, void* stream);
+
+/* As qw_dequantize with an explicit rounding: 0 = two roundings (default
+ * above), 1 = s*q + b rounded once (fused multiply-add in fp16). */
+int qw_dequantize_rounding(const qw_array* w, const qw_array* scales, const qw_array* biases, int group_size,
+                           int bits, const char* mode, int rounding, qw_array* out, void* stream);
+
+/* Affine-quantize w f16 [N, K] into (wq u32, scales f16, biases f16):
+ * s = max((max-min)/(2^bits-1), 1e-7) rounded to fp16, b = fp16(min),
+ * q = clamp(rint((w - b) / s), 0, 2^bits-1) per group.
+ * Replaces: quantize_weights{,_w,_scales,_biases}, lib.rs:2707-2742,
+ * mlx_cxx_bridge.cpp:6347-6393. */
+int qw_quantize(const qw_array* w, int group_size, int bits, const char* mode, qw_array* wq, qw_array* scales,
+                qw_array* biases, void* stream);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* qw_last_error(void);
+
+/* Reads (and, if clear != 0, resets) the device-side status word that a
+ * kernel sets when one of its bounded waits runs out (0 = none).  Synchronises
+ * the device. */
+int qw_device_status(int device, unsigned int* status, int clear);
+
+/* QW_ABI_VERSION of the loaded library. */
+int qw_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

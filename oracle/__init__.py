@@ -1,0 +1,122 @@
+"""CPU oracle for the affine group-quantized matmul (TEST INFRASTRUCTURE).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU legs of ``bench.py``
+(``cpu_baseline`` and ``--impl reference``) may import this package.  The
+product library never calls it: it is the checker, not the thing measured.
+
+The arithmetic lives in ``qw_oracle.c`` (see its header for the reference
+citations).  ``np_ref`` holds an independent float64 numpy restatement used to
+cross-check the C code.
+
+Parity status: unpinned by the reference.  cr0sh/qw has no golden vectors for
+this path and its MLX dependency cannot be built in this environment; the
+oracle is pinned instead by hand-derived known answers, by the reference's own
+layout-commutation test (crates/mlxcel-core/src/ffi_tests.rs:3792-3850) and by
+the committed fixtures under tests/golden/.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libqworacle.so")
+_lib = None
+
+ROUND_TWICE = 0
+ROUND_ONCE = 1
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        p = ctypes.c_void_p
+        i64 = ctypes.c_int64
+        i32 = ctypes.c_int
+        L.qwo_quantize.argtypes = [p, i64, i64, i32, i32, p, p, p]
+        L.qwo_dequantize.argtypes = [p, p, p, i64, i64, i32, i32, i32, p]
+        L.qwo_quantized_matmul.argtypes = [p, p, p, p, i64, i64, i64, i32, i32, p, p, i32]
+        L.qwo_f32_to_f16.argtypes = [ctypes.c_float]
+        L.qwo_f32_to_f16.restype = ctypes.c_uint16
+        L.qwo_f64_to_f16.argtypes = [ctypes.c_double]
+        L.qwo_f64_to_f16.restype = ctypes.c_uint16
+        L.qwo_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.qwo_f16_to_f32.restype = ctypes.c_float
+        L.qwo_max_threads.restype = i32
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"], "oracle inputs must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise ValueError(f"oracle {what} rejected its arguments (status {rc})")
+
+
+def quantize(w: np.ndarray, group_size: int = 64, bits: int = 4):
+    """Affine-quantize fp16 w [N, K] -> (wq uint32 [N, K*bits/32], scales, biases fp16 [N, K/gs])."""
+    w = np.ascontiguousarray(w, dtype=np.float16)
+    N, K = w.shape
+    wq = np.zeros((N, K * bits // 32), dtype=np.uint32)
+    s = np.zeros((N, K // group_size), dtype=np.float16)
+    b = np.zeros((N, K // group_size), dtype=np.float16)
+    _check(lib().qwo_quantize(_ptr(w), N, K, group_size, bits, _ptr(wq), _ptr(s), _ptr(b)), "quantize")
+    return wq, s, b
+
+
+def dequantize(wq, scales, biases, group_size: int = 64, bits: int = 4, rounding: int = ROUND_TWICE):
+    wq = np.ascontiguousarray(wq, dtype=np.uint32)
+    scales = np.ascontiguousarray(scales, dtype=np.float16)
+    biases = np.ascontiguousarray(biases, dtype=np.float16)
+    N = wq.shape[0]
+    K = wq.shape[1] * 32 // bits
+    out = np.zeros((N, K), dtype=np.float16)
+    _check(lib().qwo_dequantize(_ptr(wq), _ptr(scales), _ptr(biases), N, K, group_size, bits,
+                                rounding, _ptr(out)), "dequantize")
+    return out
+
+
+def quantized_matmul(x, wq, scales, biases, group_size: int = 64, bits: int = 4,
+                     nthreads: int = 0, want_f32: bool = False):
+    """y = x . dequantize(w)^T with fp32 accumulation; x fp16 [..., K]."""
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    lead = x.shape[:-1]
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    wq = np.ascontiguousarray(wq, dtype=np.uint32)
+    scales = np.ascontiguousarray(scales, dtype=np.float16)
+    biases = np.ascontiguousarray(biases, dtype=np.float16)
+    N = wq.shape[0]
+    if wq.shape[1] * 32 // bits != K:
+        raise ValueError("packed width does not match x's K")
+    y = np.zeros((M, N), dtype=np.float16)
+    y32 = np.zeros((M, N), dtype=np.float32) if want_f32 else None
+    _check(lib().qwo_quantized_matmul(_ptr(x2), _ptr(wq), _ptr(scales), _ptr(biases), M, N, K,
+                                      group_size, bits, _ptr(y),
+                                      _ptr(y32) if y32 is not None else None, nthreads),
+           "quantized_matmul")
+    y = y.reshape(*lead, N)
+    if want_f32:
+        return y, y32.reshape(*lead, N)
+    return y
+
+
+def max_threads() -> int:
+    return int(lib().qwo_max_threads())

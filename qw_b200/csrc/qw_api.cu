@@ -1,0 +1,450 @@
+// qw_api.cu -- the C ABI (include/qw_qmm.h): argument validation mirroring
+// the reference's load-time checks, dispatch to the kernels, per-stream
+// scratch, TMA descriptor encoding and error reporting.
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+
+#include "../../include/qw_qmm.h"
+#include "qw_internal.h"
+
+namespace qw {
+
+// ------------------------------------------------------------------ errors
+namespace {
+thread_local std::string t_last_error;
+}
+void set_error(const std::string& msg) { t_last_error = msg; }
+const char* last_error() { return t_last_error.c_str(); }
+
+// ----------------------------------------------------------- device queries
+const DeviceInfo& device_info(int device) {
+  static std::mutex mu;
+  static std::map<int, DeviceInfo> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(device);
+  if (it != cache.end()) return it->second;
+  DeviceInfo d;
+  d.device = device;
+  cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, device);
+  cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  return cache.emplace(device, d).first->second;
+}
+
+// ------------------------------------------------------------ TMA encoding
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+}  // namespace
+
+bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
+                    uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle,
+                    std::string* err) {
+  auto fn = get_encode_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled is not available from the driver";
+    return false;
+  }
+  const cuuint64_t dims[2] = {dim0, dim1};
+  const cuuint64_t strides[1] = {stride1_bytes};
+  const cuuint32_t box[2] = {box0, box1};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ") for dims " + std::to_string(dim0) +
+           "x" + std::to_string(dim1) + " stride " + std::to_string(stride1_bytes);
+    return false;
+  }
+  return true;
+}
+
+// ------------------------------------------------- per-device resources
+namespace {
+
+struct DeviceRes {
+  unsigned int* status = nullptr;
+};
+
+std::mutex g_res_mu;
+std::map<int, DeviceRes> g_dev_res;
+std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
+
+bool device_res(int device, DeviceRes** out, std::string* err) {
+  std::lock_guard<std::mutex> lock(g_res_mu);
+  auto it = g_dev_res.find(device);
+  if (it == g_dev_res.end()) {
+    DeviceRes r;
+    if (cudaMalloc(&r.status, 256) != cudaSuccess || cudaMemset(r.status, 0, 256) != cudaSuccess) {
+      *err = "could not allocate the device status word";
+      return false;
+    }
+    it = g_dev_res.emplace(device, r).first;
+  }
+  *out = &it->second;
+  return true;
+}
+
+// Scratch keyed by (device, stream): launches on one stream are ordered, so
+// they can share it; launches on different streams never do.  Grows on
+// demand; freshly allocated scratch is zeroed (the split-tile counters must
+// start at zero and every kernel leaves them at zero).
+bool scratch_for(int device, cudaStream_t stream, size_t bytes, Scratch* out, std::string* err) {
+  std::lock_guard<std::mutex> lock(g_res_mu);
+  Scratch& s = g_scratch[{device, stream}];
+  if (s.bytes < bytes) {
+    if (s.base) {
+      cudaStreamSynchronize(stream);
+      cudaFree(s.base);
+      s = Scratch{};
+    }
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    void* p = nullptr;
+    if (cudaMalloc(&p, want) != cudaSuccess) {
+      cudaGetLastError();
+      *err = "scratch allocation of " + std::to_string(want) + " bytes failed";
+      return false;
+    }
+    if (cudaMemset(p, 0, want) != cudaSuccess) {
+      cudaFree(p);
+      *err = "scratch initialisation failed";
+      return false;
+    }
+    s.base = p;
+    s.bytes = want;
+  }
+  *out = s;
+  return true;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("QW_DISABLE_PDL");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
+
+// ------------------------------------------------------------- validation
+int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+int64_t numel(const qw_array* a) {
+  int64_t n = 1;
+  for (int i = 0; i < a->ndim; ++i) n *= a->shape[i];
+  return n;
+}
+
+bool contiguous(const qw_array* a) {
+  bool all_zero = true;
+  for (int i = 0; i < a->ndim; ++i) all_zero = all_zero && a->strides[i] == 0;
+  if (all_zero) return true;
+  int64_t expect = 1;
+  for (int i = a->ndim - 1; i >= 0; --i) {
+    if (a->shape[i] != 1 && a->strides[i] != expect) return false;
+    expect *= a->shape[i];
+  }
+  return true;
+}
+
+const char* dtype_name(int d) {
+  switch (d) {
+    case QW_U32: return "uint32";
+    case QW_F16: return "float16";
+    case QW_BF16: return "bfloat16";
+    case QW_F32: return "float32";
+    default: return "unknown";
+  }
+}
+
+int check_array(const qw_array* a, const char* what) {
+  if (!a) return fail(QW_EINVAL, std::string(what) + " is null");
+  if (a->ndim < 1 || a->ndim > 4) return fail(QW_EINVAL, std::string(what) + " must have 1 to 4 dimensions");
+  for (int i = 0; i < a->ndim; ++i)
+    if (a->shape[i] < 0) return fail(QW_EINVAL, std::string(what) + " has a negative dimension");
+  if (!contiguous(a)) return fail(QW_EINVAL, std::string(what) + " must be row-contiguous");
+  if (numel(a) > 0 && a->data == nullptr) return fail(QW_EINVAL, std::string(what) + " has a null data pointer");
+  return QW_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Mode / bits / group checks in the order of the reference's validators:
+// mode allowlist (layers.rs:1367-1380), biases presence (layers.rs:1409-1440),
+// bits and group bounds (layers.rs:1286-1318).
+int check_quant_params(const char* mode, bool has_biases, int group_size, int bits) {
+  if (!mode) return fail(QW_EINVAL, "mode is null");
+  const bool affine = std::strcmp(mode, "affine") == 0;
+  const bool blockfloat =
+      std::strcmp(mode, "mxfp4") == 0 || std::strcmp(mode, "mxfp8") == 0 || std::strcmp(mode, "nvfp4") == 0;
+  if (!affine && !blockfloat)
+    return fail(QW_EINVAL, std::string("quantization mode \"") + mode +
+                               "\" must be one of affine, mxfp4, mxfp8, nvfp4");
+  if (affine && !has_biases) return fail(QW_EINVAL, "affine quantization requires biases");
+  if (!affine && has_biases)
+    return fail(QW_EINVAL, std::string("biases must be null for quantization mode \"") + mode + "\"");
+  if (bits < 1 || bits > 32) return fail(QW_EINVAL, "bits must be between 1 and 32");
+  if (group_size < 1 || group_size > (1 << 20)) return fail(QW_EINVAL, "group_size must be between 1 and 2^20");
+  if (!affine) return fail(QW_EUNSUPPORTED, std::string("quantization mode \"") + mode + "\" is not supported");
+  if (bits != 4 || group_size != 64)
+    return fail(QW_EUNSUPPORTED, "only bits=4, group_size=64 affine quantization is supported (got bits=" +
+                                     std::to_string(bits) + ", group_size=" + std::to_string(group_size) + ")");
+  return QW_OK;
+}
+
+struct WeightDims {
+  int64_t N, K, G;
+};
+
+// Packed-weight invariants (layers.rs:1568-1570, :1783-1868).
+int check_weights(const qw_array* w, const qw_array* scales, const qw_array* biases, int group_size, int bits,
+                  WeightDims* d) {
+  int rc;
+  if ((rc = check_array(w, "w")) || (rc = check_array(scales, "scales")) ||
+      (biases && (rc = check_array(biases, "biases"))))
+    return rc;
+  if (w->dtype != QW_U32) return fail(QW_EINVAL, std::string("w must be uint32, got ") + dtype_name(w->dtype));
+  if (w->ndim != 2) return fail(QW_EUNSUPPORTED, "w must be 2-D [N, K*bits/32]");
+  if (scales->ndim != 2 || scales->shape[0] != w->shape[0])
+    return fail(QW_EINVAL, "scales must be 2-D with the same row count as w");
+  if (biases && (biases->ndim != scales->ndim || biases->shape[0] != scales->shape[0] ||
+                 biases->shape[1] != scales->shape[1]))
+    return fail(QW_EINVAL, "biases must have the same shape as scales");
+  if (scales->dtype != QW_F16 || (biases && biases->dtype != QW_F16))
+    return fail(QW_EUNSUPPORTED, std::string("scales/biases must be float16, got ") + dtype_name(scales->dtype));
+  const int64_t packed_in = w->shape[1];
+  const int64_t groups = scales->shape[1];
+  if (packed_in * 32 != (int64_t)bits * groups * group_size)
+    return fail(QW_EINVAL, "packed width " + std::to_string(packed_in) + " at " + std::to_string(bits) +
+                               "-bit does not match " + std::to_string(groups) + " groups of " +
+                               std::to_string(group_size));
+  d->N = w->shape[0];
+  d->K = packed_in * 32 / bits;
+  d->G = groups;
+  if (d->N > (int64_t)1 << 30 || d->K > (int64_t)1 << 28)
+    return fail(QW_EUNSUPPORTED, "matrix dimensions beyond the supported range");
+  if (!aligned(w->data, 16) || !aligned(scales->data, 16) || (biases && !aligned(biases->data, 16)))
+    return fail(QW_EINVAL, "w, scales and biases must be 16-byte aligned");
+  return QW_OK;
+}
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(QW_ECUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+// Core of the matmul entry points.  y may be f16 or f32.
+int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases, int transpose,
+            int group_size, int bits, const char* mode, qw_array* y, void* stream_v) {
+  int rc;
+  if ((rc = check_quant_params(mode, biases != nullptr, group_size, bits))) return rc;
+  if (!transpose) return fail(QW_EUNSUPPORTED, "transpose=false is not supported");
+  WeightDims d;
+  if ((rc = check_weights(w, scales, biases, group_size, bits, &d))) return rc;
+  if ((rc = check_array(x, "x")) || (rc = check_array(y, "y"))) return rc;
+  if (x->dtype != QW_F16) return fail(QW_EUNSUPPORTED, std::string("x must be float16, got ") + dtype_name(x->dtype));
+  if (x->shape[x->ndim - 1] != d.K)
+    return fail(QW_EINVAL, "x's last dimension " + std::to_string(x->shape[x->ndim - 1]) +
+                               " does not match the weights' input width " + std::to_string(d.K));
+  const int64_t M = numel(x) / (d.K ? d.K : 1);
+  if (y->dtype != QW_F16 && y->dtype != QW_F32)
+    return fail(QW_EINVAL, std::string("y must be float16 or float32, got ") + dtype_name(y->dtype));
+  if (y->shape[y->ndim - 1] != d.N || numel(y) != M * d.N)
+    return fail(QW_EINVAL, "y must have shape [..., N] with the leading dimensions of x");
+  if (M == 0 || d.N == 0) return QW_OK;
+  if (!aligned(x->data, 16)) return fail(QW_EINVAL, "x must be 16-byte aligned");
+  if (!aligned(y->data, y->dtype == QW_F32 ? 4 : 2)) return fail(QW_EINVAL, "y is misaligned");
+
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  DeviceRes* res = nullptr;
+  std::string err;
+  if (!device_res(dev, &res, &err)) return fail(QW_ENOMEM, err);
+  cudaStream_t stream = as_stream(stream_v);
+  const bool y32 = y->dtype == QW_F32;
+  const size_t ysz = y32 ? 4 : 2;
+
+  if (M > 16 && prefill_available()) {
+    PrefillArgs pa{x->data, (const uint32_t*)w->data, scales->data, biases->data, y->data, y32, M, d.N, d.K,
+                   res->status};
+    ce = launch_prefill(pa, stream, pdl_enabled(), &err);
+    if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "prefill launch") : fail(QW_ECUDA, err);
+    return QW_OK;
+  }
+  // Skinny path, 16 rows of x per launch.
+  for (int64_t m0 = 0; m0 < M; m0 += 16) {
+    const int64_t mb = (M - m0) < 16 ? (M - m0) : 16;
+    SkinnyArgs sa{};
+    sa.x = static_cast<const uint8_t*>(x->data) + m0 * d.K * 2;
+    sa.w = (const uint32_t*)w->data;
+    sa.scales = scales->data;
+    sa.biases = biases->data;
+    sa.y = static_cast<uint8_t*>(y->data) + m0 * d.N * ysz;
+    sa.y_f32 = y32;
+    sa.M = mb;
+    sa.N = d.N;
+    sa.K = d.K;
+    sa.max_ctas = 0;
+    sa.status = res->status;
+    Scratch sc;
+    if (!scratch_for(dev, stream, skinny_scratch_bytes(sa, dev), &sc, &err)) return fail(QW_ENOMEM, err);
+    ce = launch_skinny(sa, sc, stream, pdl_enabled(), &err);
+    if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "skinny launch") : fail(QW_ECUDA, err);
+  }
+  return QW_OK;
+}
+
+}  // namespace
+}  // namespace qw
+
+using namespace qw;
+
+extern "C" {
+
+int qw_quantized_matmul(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
+                        int transpose, int group_size, int bits, const char* mode, qw_array* y, void* stream) {
+  set_error("");
+  return run_qmm(x, w, scales, biases, transpose, group_size, bits, mode, y, stream);
+}
+
+static int linear_common(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
+                         const qw_array* global_scale, const qw_array* linear_bias, int group_size, int bits,
+                         const char* mode, qw_array* y, void* stream) {
+  set_error("");
+  int rc;
+  if (y && y->dtype != QW_F16) return fail(QW_EINVAL, "linear forward output must be float16");
+  if (global_scale) {
+    if ((rc = check_array(global_scale, "global_scale"))) return rc;
+    if (global_scale->dtype != QW_F32 || numel(global_scale) != 1)
+      return fail(QW_EINVAL, "global_scale must be a float32 scalar");
+  }
+  if (linear_bias) {
+    if ((rc = check_array(linear_bias, "linear_bias"))) return rc;
+    if (linear_bias->dtype != QW_F16 || numel(linear_bias) != w->shape[0])
+      return fail(QW_EINVAL, "linear_bias must be float16 with N elements");
+  }
+  if ((rc = run_qmm(x, w, scales, biases, 1, group_size, bits, mode, y, stream))) return rc;
+  const int64_t N = w->shape[0];
+  const int64_t M = N ? numel(y) / N : 0;
+  cudaError_t ce = launch_affine_epilogue(y->data, linear_bias ? linear_bias->data : nullptr,
+                                          global_scale ? (const float*)global_scale->data : nullptr, M, N,
+                                          as_stream(stream));
+  if (ce != cudaSuccess) return cuda_fail(ce, "epilogue launch");
+  return QW_OK;
+}
+
+int qw_quantized_linear_forward(const qw_array* x, const qw_array* w, const qw_array* scales,
+                                const qw_array* biases, const qw_array* linear_bias, int group_size, int bits,
+                                const char* mode, qw_array* y, void* stream) {
+  return linear_common(x, w, scales, biases, nullptr, linear_bias, group_size, bits, mode, y, stream);
+}
+
+int qw_quantized_linear_forward_global_scale(const qw_array* x, const qw_array* w, const qw_array* scales,
+                                             const qw_array* biases, const qw_array* global_scale,
+                                             const qw_array* linear_bias, int group_size, int bits,
+                                             const char* mode, qw_array* y, void* stream) {
+  return linear_common(x, w, scales, biases, global_scale, linear_bias, group_size, bits, mode, y, stream);
+}
+
+int qw_dequantize_rounding(const qw_array* w, const qw_array* scales, const qw_array* biases, int group_size,
+                           int bits, const char* mode, int rounding, qw_array* out, void* stream) {
+  set_error("");
+  int rc;
+  if ((rc = check_quant_params(mode, biases != nullptr, group_size, bits))) return rc;
+  if (rounding != 0 && rounding != 1) return fail(QW_EINVAL, "rounding must be 0 or 1");
+  WeightDims d;
+  if ((rc = check_weights(w, scales, biases, group_size, bits, &d))) return rc;
+  if ((rc = check_array(out, "out"))) return rc;
+  if (out->dtype != QW_F16 || out->ndim != 2 || out->shape[0] != d.N || out->shape[1] != d.K)
+    return fail(QW_EINVAL, "out must be float16 [N, K]");
+  if (!aligned(out->data, 16)) return fail(QW_EINVAL, "out must be 16-byte aligned");
+  cudaError_t ce = launch_dequantize((const uint32_t*)w->data, scales->data, biases->data, out->data, d.N, d.K,
+                                     group_size, bits, rounding, as_stream(stream));
+  if (ce != cudaSuccess) return cuda_fail(ce, "dequantize launch");
+  return QW_OK;
+}
+
+int qw_dequantize(const qw_array* w, const qw_array* scales, const qw_array* biases, int group_size, int bits,
+                  const char* mode, qw_array* out, void* stream) {
+  return qw_dequantize_rounding(w, scales, biases, group_size, bits, mode, 0, out, stream);
+}
+
+int qw_quantize(const qw_array* w, int group_size, int bits, const char* mode, qw_array* wq, qw_array* scales,
+                qw_array* biases, void* stream) {
+  set_error("");
+  int rc;
+  if ((rc = check_quant_params(mode, biases != nullptr, group_size, bits))) return rc;
+  if ((rc = check_array(w, "w")) || (rc = check_array(wq, "wq")) || (rc = check_array(scales, "scales")) ||
+      (rc = check_array(biases, "biases")))
+    return rc;
+  if (w->dtype != QW_F16 || w->ndim != 2) return fail(QW_EUNSUPPORTED, "w must be float16 [N, K]");
+  const int64_t N = w->shape[0], K = w->shape[1];
+  if (K % group_size != 0) return fail(QW_EINVAL, "K must be a multiple of group_size");
+  if (wq->dtype != QW_U32 || wq->ndim != 2 || wq->shape[0] != N || wq->shape[1] != K * bits / 32)
+    return fail(QW_EINVAL, "wq must be uint32 [N, K*bits/32]");
+  if (scales->dtype != QW_F16 || scales->ndim != 2 || scales->shape[0] != N || scales->shape[1] != K / group_size ||
+      biases->dtype != QW_F16 || biases->ndim != 2 || biases->shape[0] != N || biases->shape[1] != K / group_size)
+    return fail(QW_EINVAL, "scales and biases must be float16 [N, K/group_size]");
+  if (!aligned(w->data, 16) || !aligned(wq->data, 16))
+    return fail(QW_EINVAL, "w and wq must be 16-byte aligned");
+  cudaError_t ce = launch_quantize(w->data, (uint32_t*)wq->data, scales->data, biases->data, N, K, group_size,
+                                   bits, as_stream(stream));
+  if (ce != cudaSuccess) return cuda_fail(ce, "quantize launch");
+  return QW_OK;
+}
+
+const char* qw_last_error(void) { return qw::last_error(); }
+
+int qw_device_status(int device, unsigned int* status, int clear) {
+  set_error("");
+  if (!status) return fail(QW_EINVAL, "status is null");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t ce = cudaSetDevice(device);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaSetDevice");
+  DeviceRes* res = nullptr;
+  std::string err;
+  if (!device_res(device, &res, &err)) {
+    cudaSetDevice(prev);
+    return fail(QW_ENOMEM, err);
+  }
+  ce = cudaDeviceSynchronize();
+  unsigned int v = 0;
+  if (ce == cudaSuccess) ce = cudaMemcpy(&v, res->status, sizeof v, cudaMemcpyDeviceToHost);
+  if (ce == cudaSuccess && clear && v != 0) {
+    ce = cudaMemset(res->status, 0, sizeof v);
+    // A kernel that gave up may have left split-tile counters raised.
+    std::lock_guard<std::mutex> lock(g_res_mu);
+    for (auto& kv : g_scratch)
+      if (kv.first.first == device && kv.second.base) cudaMemset(kv.second.base, 0, kv.second.bytes);
+  }
+  cudaSetDevice(prev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "reading the device status");
+  *status = v;
+  return v ? QW_ETIMEOUT : QW_OK;
+}
+
+int qw_abi_version(void) { return QW_ABI_VERSION; }
+
+}  // extern "C"

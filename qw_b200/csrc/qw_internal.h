@@ -1,0 +1,77 @@
+// qw_internal.h -- declarations shared by the C-ABI layer and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace qw {
+
+// Error reporting: the C-ABI stores a message in a thread-local string.
+void set_error(const std::string& msg);
+const char* last_error();
+
+// TMA descriptor encoding through the driver entry point (no -lcuda).
+bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
+                    uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle,
+                    std::string* err);
+
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+};
+const DeviceInfo& device_info(int device);
+
+// Scratch memory for a launch: either the library's own per-device buffer or
+// caller-supplied memory.  `bytes` is the capacity of `base`.
+struct Scratch {
+  void* base = nullptr;
+  size_t bytes = 0;
+};
+
+// Skinny path (M <= 16): stream-K over (row tile, 512-wide k chunk) units.
+struct SkinnyArgs {
+  const void* x;         // fp16 [M][K]
+  const uint32_t* w;     // [N][K/8]
+  const void* scales;    // fp16 [N][K/64]
+  const void* biases;    // fp16 [N][K/64]
+  void* y;               // fp16 or fp32 [M][N]
+  bool y_f32;
+  int64_t M, N, K;
+  int max_ctas;          // 0 = occupancy-derived
+  unsigned int* status;  // device status word
+};
+// Scratch bytes the skinny path needs for a shape (0 when it runs unsplit).
+size_t skinny_scratch_bytes(const SkinnyArgs& a, int device);
+cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
+                          std::string* err);
+
+// Prefill path (tcgen05, M >= 17).
+struct PrefillArgs {
+  const void* x;
+  const uint32_t* w;
+  const void* scales;
+  const void* biases;
+  void* y;
+  bool y_f32;
+  int64_t M, N, K;
+  unsigned int* status;
+};
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err);
+bool prefill_available();
+
+// Quantize / dequantize kernels (affine, 4-bit, group 64 for now).
+cudaError_t launch_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N,
+                              int64_t K, int group_size, int bits, int rounding, cudaStream_t stream);
+cudaError_t launch_quantize(const void* w, uint32_t* wq, void* scales, void* biases, int64_t N, int64_t K,
+                            int group_size, int bits, cudaStream_t stream);
+
+// Elementwise epilogues used by the linear-forward entry points.
+cudaError_t launch_affine_epilogue(void* y, const void* linear_bias, const float* global_scale, int64_t M,
+                                   int64_t N, cudaStream_t stream);
+cudaError_t launch_f32_to_f16(const float* src, void* dst, int64_t n, cudaStream_t stream);
+
+}  // namespace qw

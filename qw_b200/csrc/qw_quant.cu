@@ -1,0 +1,150 @@
+// qw_quant.cu -- affine 4-bit group-64 dequantize / quantize kernels and the
+// small elementwise epilogues of the linear-forward entry points.
+//
+// dequantize is bit-exact with the oracle under both roundings: every fp16
+// product and sum goes through an explicitly rounded (.rn) f16x2 instruction.
+// quantize is bit-exact with the oracle's quantizer: every fp32 step uses an
+// explicitly rounded intrinsic so nothing is contracted into an fma.
+#include <cuda_fp16.h>
+
+#include "qw_internal.h"
+#include "qw_ptx.cuh"
+
+namespace qw {
+
+namespace {
+
+// One thread per packed word: 8 outputs (16 bytes) per thread.
+template <bool kRoundOnce>
+__global__ void dequantize_kernel(const uint32_t* __restrict__ w, const __half* __restrict__ scales,
+                                  const __half* __restrict__ biases, uint4* __restrict__ out, int64_t N,
+                                  int64_t words_per_row, int64_t groups) {
+  const int64_t total = N * words_per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / words_per_row;
+    const int64_t kw = i - n * words_per_row;
+    const int64_t g = kw / 8;  // 8 words per group of 64
+    const __half s = scales[n * groups + g];
+    const __half b = biases[n * groups + g];
+    const uint32_t s2 = (uint32_t)__half_as_ushort(s) * 0x10001u;
+    const uint32_t b2 = (uint32_t)__half_as_ushort(b) * 0x10001u;
+    out[i] = dequant_word<kRoundOnce>(__ldg(w + i), s2, b2);
+  }
+}
+
+// One thread per group of 64 weights.
+__global__ void quantize_kernel(const uint4* __restrict__ w, uint4* __restrict__ wq, __half* __restrict__ scales,
+                                __half* __restrict__ biases, int64_t ngroups) {
+  for (int64_t gidx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; gidx < ngroups;
+       gidx += (int64_t)gridDim.x * blockDim.x) {
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __ldg(w + gidx * 8 + i);
+    const __half* h = reinterpret_cast<const __half*>(v);
+    float mn = __int_as_float(0x7f800000), mx = -__int_as_float(0x7f800000);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float f = __half2float(h[i]);
+      if (f < mn) mn = f;
+      if (f > mx) mx = f;
+    }
+    float scale = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+    if (!(scale >= 1e-7f)) scale = 1e-7f;
+    const __half sh = __float2half_rn(scale);
+    const __half bh = __float2half_rn(mn);
+    const float sf = __half2float(sh);
+    const float bf = __half2float(bh);
+    scales[gidx] = sh;
+    biases[gidx] = bh;
+    uint32_t words[8];
+#pragma unroll
+    for (int wi = 0; wi < 8; ++wi) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        const float f = __half2float(h[wi * 8 + p]);
+        float r = rintf(__fdiv_rn(__fsub_rn(f, bf), sf));
+        r = fminf(fmaxf(r, 0.0f), 15.0f);
+        word |= ((uint32_t)r) << (4 * p);
+      }
+      words[wi] = word;
+    }
+    wq[gidx * 2] = make_uint4(words[0], words[1], words[2], words[3]);
+    wq[gidx * 2 + 1] = make_uint4(words[4], words[5], words[6], words[7]);
+  }
+}
+
+// y[m][n] = fp16(fp16 y * global_scale) then fp16 add of linear_bias[n].
+__global__ void affine_epilogue_kernel(__half* __restrict__ y, const __half* __restrict__ bias,
+                                       const float* __restrict__ gscale, int64_t M, int64_t N) {
+  const int64_t total = M * N;
+  const float gs = gscale ? *gscale : 1.0f;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    __half v = y[i];
+    if (gscale) v = __float2half_rn(__fmul_rn(__half2float(v), gs));
+    if (bias) v = __hadd_rn(v, bias[i % N]);
+    y[i] = v;
+  }
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ src, __half* __restrict__ dst, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = __float2half_rn(src[i]);
+}
+
+int grid_for(int64_t work, int threads) {
+  int64_t blocks = (work + threads - 1) / threads;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+}  // namespace
+
+cudaError_t launch_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N,
+                              int64_t K, int group_size, int bits, int rounding, cudaStream_t stream) {
+  if (group_size != 64 || bits != 4) return cudaErrorInvalidValue;
+  const int64_t wpr = K / 8;
+  const int64_t total = N * wpr;
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  const int blocks = grid_for(total, threads);
+  if (rounding == 1)
+    dequantize_kernel<true><<<blocks, threads, 0, stream>>>(w, (const __half*)scales, (const __half*)biases,
+                                                            (uint4*)out, N, wpr, K / 64);
+  else
+    dequantize_kernel<false><<<blocks, threads, 0, stream>>>(w, (const __half*)scales, (const __half*)biases,
+                                                             (uint4*)out, N, wpr, K / 64);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize(const void* w, uint32_t* wq, void* scales, void* biases, int64_t N, int64_t K,
+                            int group_size, int bits, cudaStream_t stream) {
+  if (group_size != 64 || bits != 4) return cudaErrorInvalidValue;
+  const int64_t ngroups = N * (K / 64);
+  if (ngroups == 0) return cudaSuccess;
+  const int threads = 128;
+  quantize_kernel<<<grid_for(ngroups, threads), threads, 0, stream>>>((const uint4*)w, (uint4*)wq,
+                                                                       (__half*)scales, (__half*)biases, ngroups);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_affine_epilogue(void* y, const void* linear_bias, const float* global_scale, int64_t M,
+                                   int64_t N, cudaStream_t stream) {
+  if (M * N == 0 || (!linear_bias && !global_scale)) return cudaSuccess;
+  const int threads = 256;
+  affine_epilogue_kernel<<<grid_for(M * N, threads), threads, 0, stream>>>(
+      (__half*)y, (const __half*)linear_bias, global_scale, M, N);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f32_to_f16(const float* src, void* dst, int64_t n, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const int threads = 256;
+  f32_to_f16_kernel<<<grid_for(n, threads), threads, 0, stream>>>(src, (__half*)dst, n);
+  return cudaGetLastError();
+}
+
+}  // namespace qw

@@ -1,0 +1,156 @@
+"""Host-side mirror of mlxcel-core's quantized-linear operator surface.
+
+Each function keeps the name, argument meaning and error behaviour of the
+cxx bridge function it stands in for (crates/mlxcel-core/src/lib.rs), with
+torch CUDA tensors in place of MlxArray and a raise in place of the bridge's
+uncatchable abort.  The work happens in libqwqmm.so through its C ABI; torch
+supplies device memory and the current stream only.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_DT = {
+    torch.float16: _lib.QW_F16,
+    torch.bfloat16: _lib.QW_BF16,
+    torch.float32: _lib.QW_F32,
+    torch.int32: _lib.QW_U32,   # MLX's uint32 packing, viewed as int32 by torch
+    torch.uint32: _lib.QW_U32,
+}
+
+
+def _arr(t: Optional[torch.Tensor]):
+    """torch tensor -> pointer to a qw_array (None -> NULL)."""
+    if t is None:
+        return None
+    if t.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    if t.dim() < 1 or t.dim() > 4:
+        raise ValueError("qw arrays have 1 to 4 dimensions")
+    a = _lib.QwArray()
+    a.data = t.data_ptr() if t.numel() else 0
+    a.dtype = _DT[t.dtype]
+    a.ndim = t.dim()
+    for i, (s, st) in enumerate(zip(t.shape, t.stride())):
+        a.shape[i] = s
+        a.strides[i] = st
+    return ctypes.pointer(a)
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _mode(mode: str) -> bytes:
+    return mode.encode()
+
+
+def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: Optional[torch.Tensor],
+                     transpose: bool = True, group_size: int = 64, bits: int = 4, mode: str = "affine",
+                     out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """y = x @ dequantize(w, scales, biases).T  (lib.rs:1134-1143).
+
+    ``out_dtype=torch.float32`` returns the fp32 accumulators unrounded (the
+    partial sums of a row-parallel tensor-parallel shard)."""
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=out_dtype, device=x.device)
+    L = _lib.load()
+    _lib.check(L.qw_quantized_matmul(_arr(x), _arr(w), _arr(scales), _arr(biases), int(bool(transpose)),
+                                     group_size, bits, _mode(mode), _arr(out), _stream(x)))
+    return out
+
+
+def quantized_linear_forward(x, w, scales, biases, linear_bias=None, group_size: int = 64, bits: int = 4,
+                             mode: str = "affine", out=None) -> torch.Tensor:
+    """Quantized linear layer forward (lib.rs:591-601)."""
+    if out is None:
+        out = torch.empty(*x.shape[:-1], w.shape[0], dtype=torch.float16, device=x.device)
+    L = _lib.load()
+    _lib.check(L.qw_quantized_linear_forward(_arr(x), _arr(w), _arr(scales), _arr(biases), _arr(linear_bias),
+                                             group_size, bits, _mode(mode), _arr(out), _stream(x)))
+    return out
+
+
+def quantized_linear_forward_global_scale(x, w, scales, biases, global_scale=None, linear_bias=None,
+                                          group_size: int = 64, bits: int = 4, mode: str = "affine",
+                                          out=None) -> torch.Tensor:
+    """Quantized linear forward with a post-qmm global scale (lib.rs:604-615)."""
+    if out is None:
+        out = torch.empty(*x.shape[:-1], w.shape[0], dtype=torch.float16, device=x.device)
+    L = _lib.load()
+    _lib.check(L.qw_quantized_linear_forward_global_scale(
+        _arr(x), _arr(w), _arr(scales), _arr(biases), _arr(global_scale), _arr(linear_bias), group_size, bits,
+        _mode(mode), _arr(out), _stream(x)))
+    return out
+
+
+def dequantize(w, scales, biases, group_size: int = 64, bits: int = 4, mode: str = "affine",
+               rounding: int = 0, out=None) -> torch.Tensor:
+    """Full-precision weights from the quantized triple (lib.rs:1152-1159).
+
+    rounding 0: fp16(fp16(s*q) + b); rounding 1: fp16(s*q + b) rounded once."""
+    K = w.shape[1] * 32 // bits
+    if out is None:
+        out = torch.empty(w.shape[0], K, dtype=torch.float16, device=w.device)
+    L = _lib.load()
+    _lib.check(L.qw_dequantize_rounding(_arr(w), _arr(scales), _arr(biases), group_size, bits, _mode(mode),
+                                        rounding, _arr(out), _stream(w)))
+    return out
+
+
+def quantize_weights(w: torch.Tensor, group_size: int = 64, bits: int = 4,
+                     mode: str = "affine") -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Quantize once and return the (w, scales, biases) triple (lib.rs:2707-2742)."""
+    N, K = w.shape
+    wq = torch.empty(N, K * bits // 32, dtype=torch.int32, device=w.device)
+    s = torch.empty(N, K // group_size, dtype=torch.float16, device=w.device)
+    b = torch.empty(N, K // group_size, dtype=torch.float16, device=w.device)
+    L = _lib.load()
+    _lib.check(L.qw_quantize(_arr(w), group_size, bits, _mode(mode), _arr(wq), _arr(s), _arr(b), _stream(w)))
+    return wq, s, b
+
+
+def device_status(device: int = 0, clear: bool = True) -> int:
+    """Device-side status word left by a kernel whose bounded wait ran out (0 = none)."""
+    v = ctypes.c_uint(0)
+    rc = _lib.load().qw_device_status(device, ctypes.byref(v), int(clear))
+    if rc not in (_lib.QW_OK, _lib.QW_ETIMEOUT):
+        _lib.check(rc)
+    return int(v.value)
+
+
+class QuantizedLinear:
+    """A quantized weight triple and its forward, after mlxcel-core's
+    ``QuantizedWeight`` (layers.rs:35-174) and the quantized arm of
+    ``UnifiedLinear::forward`` (layers.rs:2023-2093)."""
+
+    def __init__(self, w, scales, biases, group_size: int = 64, bits: int = 4, mode: str = "affine",
+                 bias: Optional[torch.Tensor] = None, global_scale: Optional[torch.Tensor] = None):
+        self.weight, self.scales, self.biases = w, scales, biases
+        self.group_size, self.bits, self.mode = group_size, bits, mode
+        self.bias = bias
+        self.global_scale = global_scale
+
+    @property
+    def out_features(self) -> int:
+        return self.weight.shape[0]
+
+    @property
+    def in_features(self) -> int:
+        return self.weight.shape[1] * 32 // self.bits
+
+    def forward(self, x: torch.Tensor, out=None) -> torch.Tensor:
+        if self.global_scale is not None:
+            return quantized_linear_forward_global_scale(x, self.weight, self.scales, self.biases,
+                                                         self.global_scale, self.bias, self.group_size,
+                                                         self.bits, self.mode, out=out)
+        return quantized_linear_forward(x, self.weight, self.scales, self.biases, self.bias, self.group_size,
+                                        self.bits, self.mode, out=out)
+
+    __call__ = forward

@@ -1,0 +1,179 @@
+"""GPU parity: libqwqmm.so (through its C ABI) against the CPU oracle.
+
+Bars: quantize and dequantize bit-exact; matmul outputs within
+max|y - y_ref| <= 1e-2 * rms(y_ref) (TOL), fp32 outputs within 1e-3.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import qw_b200
+from qw_b200 import synth
+from tests.conftest import TOL, golden_cases, load_golden, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def dev_u32(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int32)).cuda()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    return t.cpu().numpy()
+
+
+def quantized(N, K, seed=0):
+    w = synth.weight_fp16(N, K, seed=seed)
+    return oracle.quantize(w)
+
+
+def run_qmm(x, wq, s, b, out_dtype=torch.float16):
+    y = qw_b200.quantized_matmul(dev(x), dev_u32(wq), dev(s), dev(b), out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    return host(y)
+
+
+@pytest.fixture(autouse=True)
+def _clean_status(cuda_dev):
+    yield
+    assert qw_b200.device_status(0) == 0, "a kernel gave up on a bounded wait"
+
+
+# ---------------------------------------------------------------- golden
+@pytest.mark.parametrize("name", golden_cases())
+def test_golden_quantize_bit_exact(name):
+    from tests.golden.gen_golden import CASES
+    M, N, K, seed = CASES[name]
+    w = synth.weight_fp16(N, K, seed=seed, layer=0, tid=0)
+    g = load_golden(name)
+    wq, s, b = qw_b200.quantize_weights(dev(w))
+    np.testing.assert_array_equal(host(wq).view(np.uint32), g["wq"])
+    np.testing.assert_array_equal(host(s).view(np.uint16), g["scales"].view(np.uint16))
+    np.testing.assert_array_equal(host(b).view(np.uint16), g["biases"].view(np.uint16))
+
+
+@pytest.mark.parametrize("name", golden_cases())
+@pytest.mark.parametrize("rounding,key", [(0, "deq_twice"), (1, "deq_once")])
+def test_golden_dequantize_bit_exact(name, rounding, key):
+    g = load_golden(name)
+    d = qw_b200.dequantize(dev_u32(g["wq"]), dev(g["scales"]), dev(g["biases"]), rounding=rounding)
+    np.testing.assert_array_equal(host(d).view(np.uint16), g[key].view(np.uint16))
+
+
+@pytest.mark.parametrize("name", golden_cases())
+def test_golden_matmul(name):
+    g = load_golden(name)
+    y = run_qmm(g["x"], g["wq"], g["scales"], g["biases"])
+    assert rel_err(y, g["y32"]) <= TOL
+    y32 = run_qmm(g["x"], g["wq"], g["scales"], g["biases"], out_dtype=torch.float32)
+    assert rel_err(y32, g["y32"]) <= 1e-3
+
+
+# ------------------------------------------------------------- sweeps
+@pytest.mark.parametrize("M", list(range(1, 17)))
+def test_every_small_m(M):
+    wq, s, b = quantized(384, 1024, seed=M)
+    x = synth.activations(M, 1024, seed=M)
+    _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL
+
+
+@pytest.mark.parametrize("N,K", [(1, 64), (129, 64), (130, 576), (1000, 2048), (17, 4160), (512, 5120)])
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_ragged_shapes(M, N, K):
+    wq, s, b = quantized(N, K, seed=N + K)
+    x = synth.activations(M, K, seed=N)
+    _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_single_config_full_size(M):
+    """BASELINE config: W [17408, 5120] 4-bit group 64, x ~ N(0, 1)."""
+    wq, s, b = quantized(17408, 5120, seed=0)
+    x = synth.activations(M, 5120, seed=0)
+    _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    y = run_qmm(x, wq, s, b)
+    assert rel_err(y, y_ref) <= TOL
+    y32 = run_qmm(x, wq, s, b, out_dtype=torch.float32)
+    assert rel_err(y32, y_ref) <= 1e-3
+
+
+@pytest.mark.parametrize("lin", synth.layer_linears() + [synth.LM_HEAD], ids=lambda l: l.name)
+def test_stack_shapes_m1(lin):
+    wq, s, b = quantized(lin.N, lin.K, seed=lin.tid)
+    x = synth.activations(1, lin.K, seed=lin.tid)
+    _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL
+
+
+def test_deterministic_across_calls():
+    wq, s, b = quantized(5120, 17408, seed=3)   # down-projection shape: tiles split across CTAs
+    x = synth.activations(3, 17408, seed=3)
+    y1 = run_qmm(x, wq, s, b, out_dtype=torch.float32)
+    y2 = run_qmm(x, wq, s, b, out_dtype=torch.float32)
+    np.testing.assert_array_equal(y1, y2)
+
+
+def test_large_m_runs_in_blocks():
+    wq, s, b = quantized(256, 1024, seed=9)
+    x = synth.activations(40, 1024, seed=9)
+    _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL
+
+
+def test_leading_batch_dims():
+    wq, s, b = quantized(200, 512, seed=4)
+    x = synth.activations(6, 512, seed=4).reshape(2, 3, 512)
+    y = qw_b200.quantized_matmul(dev(x), dev_u32(wq), dev(s), dev(b))
+    assert tuple(y.shape) == (2, 3, 200)
+    _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    assert rel_err(host(y), y_ref) <= TOL
+
+
+# -------------------------------------------------------------- edge codes
+@pytest.mark.parametrize("fill", [0x00000000, 0xFFFFFFFF, 0x0F0F0F0F])
+def test_constant_codes(fill):
+    N, K = 300, 1536
+    wq = np.full((N, K // 8), fill, dtype=np.uint32)
+    rng = np.random.default_rng(fill & 0xFF)
+    s = (rng.random((N, K // 64)) * 0.01).astype(np.float16)
+    b = (-rng.random((N, K // 64)) * 0.05).astype(np.float16)
+    x = synth.activations(2, K, seed=1)
+    _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL
+
+
+def test_empty_inputs():
+    wq, s, b = quantized(64, 128)
+    x = torch.empty(0, 128, dtype=torch.float16, device="cuda")
+    y = qw_b200.quantized_matmul(x, dev_u32(wq), dev(s), dev(b))
+    assert tuple(y.shape) == (0, 64)
+
+
+# ------------------------------------------------------- linear forwards
+def test_linear_forward_bias_and_global_scale():
+    N, K = 320, 1024
+    wq, s, b = quantized(N, K, seed=12)
+    x = synth.activations(3, K, seed=12)
+    bias = (np.random.default_rng(1).standard_normal(N) * 0.1).astype(np.float16)
+    gs = np.array([0.75], dtype=np.float32)
+    y_ref = oracle.quantized_matmul(x, wq, s, b)  # fp16 output of the qmm
+    lin = qw_b200.QuantizedLinear(dev_u32(wq), dev(s), dev(b), bias=dev(bias))
+    y = host(lin(dev(x)))
+    assert rel_err(y, (y_ref + bias).astype(np.float32)) <= TOL
+    lin_gs = qw_b200.QuantizedLinear(dev_u32(wq), dev(s), dev(b), bias=dev(bias), global_scale=dev(gs))
+    y2 = host(lin_gs(dev(x)))
+    expect = (y_ref.astype(np.float32) * gs[0]).astype(np.float16) + bias
+    assert rel_err(y2, expect) <= TOL
+
+
+def test_invalid_call_raises_with_message():
+    wq, s, b = quantized(64, 128)
+    with pytest.raises(qw_b200._lib.QwError, match="bits=8"):
+        qw_b200.quantized_matmul(dev(synth.activations(1, 128)), dev_u32(wq), dev(s), dev(b), bits=8)

@@ -1,0 +1,187 @@
+"""CPU tests of the oracle: hand-derived known answers, the reference's own
+layout test restated, the committed golden fixtures, and agreement with the
+independent numpy restatement.  No GPU."""
+import numpy as np
+import pytest
+
+import oracle
+from oracle import np_ref
+from qw_b200 import synth
+from tests.conftest import golden_cases, load_golden, rel_err
+
+
+def f16(*v):
+    return np.array(v, dtype=np.float16)
+
+
+# ---------------------------------------------------------------- fp16 helpers
+def test_f16_conversion_matches_numpy_on_every_pattern():
+    L = oracle.lib()
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    ref = bits.view(np.float16).astype(np.float32)
+    ours = np.array([L.qwo_f16_to_f32(int(b)) for b in bits[::97]], dtype=np.float32)
+    np.testing.assert_array_equal(np.isnan(ours), np.isnan(ref[::97]))
+    ok = ~np.isnan(ref[::97])
+    np.testing.assert_array_equal(ours[ok], ref[::97][ok])
+
+
+def test_f32_to_f16_round_to_nearest_even():
+    L = oracle.lib()
+    rng = np.random.default_rng(7)
+    vals = np.concatenate([
+        rng.standard_normal(4000).astype(np.float32) * 10,
+        rng.standard_normal(1000).astype(np.float32) * 1e-6,   # subnormal range
+        np.array([65504, 65519.99, 65520, 1e9, -1e9, 2.0 ** -25, 2.0 ** -24, 3 * 2.0 ** -26, 0.0, -0.0],
+                 dtype=np.float32),
+    ])
+    ours = np.array([L.qwo_f32_to_f16(float(v)) for v in vals], dtype=np.uint16)
+    with np.errstate(over="ignore"):
+        ref = vals.astype(np.float16).view(np.uint16)
+    np.testing.assert_array_equal(ours, ref)
+    # float64 path: compare against numpy's direct double -> half conversion
+    d = rng.standard_normal(3000) * 3.0
+    ours64 = np.array([L.qwo_f64_to_f16(float(v)) for v in d], dtype=np.uint16)
+    np.testing.assert_array_equal(ours64, d.astype(np.float16).view(np.uint16))
+
+
+# ------------------------------------------------------------ known answers
+def test_nibble_order_known_answer():
+    """Element k of a row is bits 4*(k%8).. of word k/8, low nibble first."""
+    K = 64
+    words = np.array([[0x76543210, 0xFEDCBA98] * 4], dtype=np.uint32)  # codes 0..15, 0..15, ...
+    s = f16(0.5).reshape(1, 1)
+    b = f16(-1.0).reshape(1, 1)
+    deq = oracle.dequantize(words, s, b)
+    expect = (np.tile(np.arange(16), 4) * 0.5 - 1.0).astype(np.float16).reshape(1, K)
+    np.testing.assert_array_equal(deq, expect)
+    # x = e_k picks out column k exactly
+    for k in (0, 1, 7, 8, 15, 63):
+        x = np.zeros((1, K), dtype=np.float16)
+        x[0, k] = 1.0
+        y = oracle.quantized_matmul(x, words, s, b)
+        assert float(y[0, 0]) == float(expect[0, k])
+
+
+def test_all_zero_and_all_fifteen_codes():
+    K, N = 128, 3
+    s = np.full((N, K // 64), 0.25, dtype=np.float16)
+    b = np.full((N, K // 64), 0.125, dtype=np.float16)
+    zeros = np.zeros((N, K // 8), dtype=np.uint32)
+    full = np.full((N, K // 8), 0xFFFFFFFF, dtype=np.uint32)
+    np.testing.assert_array_equal(oracle.dequantize(zeros, s, b), np.full((N, K), 0.125, np.float16))
+    np.testing.assert_array_equal(oracle.dequantize(full, s, b), np.full((N, K), 3.875, np.float16))
+    x = np.ones((2, K), dtype=np.float16)
+    np.testing.assert_array_equal(oracle.quantized_matmul(x, full, s, b), np.full((2, N), 496.0, np.float16))
+
+
+def test_roundings_differ_only_where_expected():
+    """Rounded-once and rounded-twice dequantisation agree on exactly
+    representable cases and otherwise differ by at most the first rounding
+    (half an ulp of s*q) plus one ulp of the result."""
+    rng = np.random.default_rng(3)
+    N, K = 64, 256
+    wq = rng.integers(0, 2 ** 32, size=(N, K // 8), dtype=np.uint64).astype(np.uint32)
+    s = (rng.random((N, K // 64)) * 0.01).astype(np.float16)
+    b = (-rng.random((N, K // 64)) * 0.08).astype(np.float16)
+    d0 = oracle.dequantize(wq, s, b, rounding=oracle.ROUND_TWICE).astype(np.float64)
+    d1 = oracle.dequantize(wq, s, b, rounding=oracle.ROUND_ONCE).astype(np.float64)
+    sq = np.repeat(s, 64, axis=1).astype(np.float64) * np_ref.unpack(wq).astype(np.float64)
+    bound = 0.5 * np.spacing(np.abs(sq).astype(np.float16)).astype(np.float64) + \
+        np.spacing(np.abs(d1).astype(np.float16)).astype(np.float64)
+    assert np.all(np.abs(d0 - d1) <= bound * 1.0001)
+    assert np.mean(d0 != d1) > 0.05  # the two conventions really differ
+    pow2 = np.full_like(s, 0.25)
+    np.testing.assert_array_equal(oracle.dequantize(wq, pow2, f16(0).reshape(1, 1).repeat(N, 0).repeat(K // 64, 1)),
+                                  oracle.dequantize(wq, pow2, np.zeros_like(b), rounding=oracle.ROUND_ONCE))
+
+
+def test_dequantize_commutes_with_output_axis_slice():
+    """The reference's one deterministic dequantize test
+    (crates/mlxcel-core/src/ffi_tests.rs:3792-3850), restated with its hand-made
+    word patterns: dequantize(slice(w)) == slice(dequantize(w)) bit for bit.
+    The reference uses group 32 and f32 scales; here group 64 / fp16 scales,
+    which the same property covers."""
+    experts, rows, K = 2, 8, 128
+    packed = K // 8
+    groups = K // 64
+    w = np.zeros((experts * rows, packed), dtype=np.uint32)
+    s = np.zeros((experts * rows, groups), dtype=np.float16)
+    b = np.zeros((experts * rows, groups), dtype=np.float16)
+    for e in range(experts):
+        for r in range(rows):
+            for c in range(packed):
+                w[e * rows + r, c] = (0x12345678 + e * 131 + r * 17 + c) & 0xFFFFFFFF
+            for g in range(groups):
+                s[e * rows + r, g] = 0.05 + 0.01 * e + 0.001 * r + 0.0003 * g
+                b[e * rows + r, g] = -0.2 + 0.02 * e - 0.003 * r + 0.0007 * g
+    full = oracle.dequantize(w, s, b)
+    half = rows // 2
+    for e in range(experts):
+        for lo, hi in ((0, half), (half, rows)):
+            sl = slice(e * rows + lo, e * rows + hi)
+            part = oracle.dequantize(np.ascontiguousarray(w[sl]), np.ascontiguousarray(s[sl]),
+                                     np.ascontiguousarray(b[sl]))
+            np.testing.assert_array_equal(part.view(np.uint16), full[sl].view(np.uint16))
+
+
+def test_packing_invariant_is_enforced():
+    """packed_in * 32 == bits * groups * group_size (layers.rs:1568-1570)."""
+    with pytest.raises(ValueError):
+        oracle.quantized_matmul(np.zeros((1, 128), np.float16), np.zeros((2, 8), np.uint32),
+                                np.zeros((2, 2), np.float16), np.zeros((2, 2), np.float16))
+
+
+# ------------------------------------------------------------- restatements
+@pytest.mark.parametrize("N,K", [(8, 64), (33, 256), (100, 640), (17, 1024)])
+def test_c_and_numpy_restatements_agree(N, K):
+    w = synth.weight_fp16(N, K, seed=11)
+    wq, s, b = oracle.quantize(w)
+    wq2, s2, b2 = np_ref.quantize(w)
+    np.testing.assert_array_equal(wq, wq2)
+    np.testing.assert_array_equal(s.view(np.uint16), s2.view(np.uint16))
+    np.testing.assert_array_equal(b.view(np.uint16), b2.view(np.uint16))
+    for r, name in ((oracle.ROUND_TWICE, "twice"), (oracle.ROUND_ONCE, "once")):
+        np.testing.assert_array_equal(oracle.dequantize(wq, s, b, rounding=r).view(np.uint16),
+                                      np_ref.dequantize(wq, s, b, rounding=name).view(np.uint16))
+    x = synth.activations(5, K, seed=11)
+    y, y32 = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    y64 = np_ref.quantized_matmul(x, wq, s, b)
+    assert rel_err(y32, y64) < 1e-5
+    assert rel_err(y, y64) < 1e-3
+
+
+def test_quantizer_reconstruction_error_is_bounded():
+    w = synth.weight_fp16(64, 512, seed=5)
+    wq, s, b = oracle.quantize(w)
+    d = oracle.dequantize(wq, s, b).astype(np.float32)
+    err = np.abs(d - w.astype(np.float32))
+    smax = np.repeat(s.astype(np.float32), 64, axis=1)
+    assert np.all(err <= 0.5 * smax + 2e-3)
+
+
+# ---------------------------------------------------------------- fixtures
+@pytest.mark.parametrize("name", golden_cases())
+def test_golden_fixture_reproduces(name):
+    g = load_golden(name)
+    M, K = g["x"].shape
+    N = g["wq"].shape[0]
+    wq, s, b = g["wq"], g["scales"], g["biases"]
+    np.testing.assert_array_equal(oracle.dequantize(wq, s, b).view(np.uint16), g["deq_twice"].view(np.uint16))
+    np.testing.assert_array_equal(oracle.dequantize(wq, s, b, rounding=1).view(np.uint16),
+                                  g["deq_once"].view(np.uint16))
+    y, y32 = oracle.quantized_matmul(g["x"], wq, s, b, want_f32=True)
+    np.testing.assert_array_equal(y.view(np.uint16), g["y"].view(np.uint16))
+    np.testing.assert_array_equal(y32, g["y32"])
+    assert rel_err(y32, np_ref.quantized_matmul(g["x"], wq, s, b)) < 1e-5
+    assert y.shape == (M, N) and K == wq.shape[1] * 8
+
+
+def test_golden_quantizer_inputs_regenerate():
+    from tests.golden.gen_golden import CASES
+    for name, (M, N, K, seed) in CASES.items():
+        g = load_golden(name)
+        w = synth.weight_fp16(N, K, seed=seed, layer=0, tid=0)
+        wq, s, b = oracle.quantize(w)
+        np.testing.assert_array_equal(wq, g["wq"])
+        np.testing.assert_array_equal(s.view(np.uint16), g["scales"].view(np.uint16))
+        np.testing.assert_array_equal(synth.activations(M, K, seed=seed), g["x"])
