@@ -479,6 +479,20 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_case(args):
+    """One quantized matmul shape, 4 rotating weight copies (> L2 for the
+    BASELINE shapes); prints one JSON line.  Used for ncu captures."""
+    import torch
+    import qw_b200 as qw
+    M, N, K = (int(v) for v in args.case.split(","))
+    dev = torch.device("cuda", 0)
+    us, gbs = kernel_microbench(torch, qw, M, N, K, dev, copies=4, iters=args.steps)
+    hbm_peak, _, src = peaks()
+    print(json.dumps({"case": [M, N, K], "us": round(us, 3), "GBps": round(gbs, 1),
+                      "frac_hbm": round(gbs / hbm_peak, 4), "peak_source": src,
+                      "TFLOPs": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 2)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -488,10 +502,14 @@ def main():
     ap.add_argument("--layers", type=int, default=synth.LAYERS)
     ap.add_argument("--skip-extra", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--case", default=None,
+                    help="M,N,K: time one quantized matmul shape only (small device footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

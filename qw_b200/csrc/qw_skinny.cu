@@ -40,6 +40,8 @@ namespace {
 
 constexpr int kGroup = 64;
 constexpr int kGroupsPerStage = 8;
+constexpr size_t kMaxCounters = 1u << 16;  // row tiles per launch (N <= 8M rows)
+constexpr size_t kCounterBytes = kMaxCounters * sizeof(unsigned int);
 constexpr int kChunkK = kGroup * kGroupsPerStage;  // 512
 
 template <int NT, int WARPS, int STAGES>
@@ -486,15 +488,21 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   p.y = a.y;
   p.scales = reinterpret_cast<const __half*>(a.scales);
   p.biases = reinterpret_cast<const __half*>(a.biases);
-  const size_t need = (size_t)p.G * 2 * Cfg::PART * sizeof(float) + (size_t)p.T * sizeof(unsigned int);
+  // Scratch layout: the split-tile counters at a fixed offset (they are zero
+  // between launches, whatever grid the previous launch used), then the
+  // partial slots, which need no initialisation.
+  if ((size_t)p.T > kMaxCounters) {
+    *err = "too many row tiles for the skinny path's counter block";
+    return cudaErrorInvalidValue;
+  }
+  const size_t need = kCounterBytes + (size_t)p.G * 2 * Cfg::PART * sizeof(float);
   if (scratch.bytes < need || scratch.base == nullptr) {
     *err = "scratch too small for the skinny path";
     return cudaErrorInvalidValue;
   }
   p.status = a.status;
-  p.part = reinterpret_cast<float*>(scratch.base);
-  p.counter = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(scratch.base) +
-                                              (size_t)p.G * 2 * Cfg::PART * sizeof(float));
+  p.counter = reinterpret_cast<unsigned int*>(scratch.base);
+  p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch.base) + kCounterBytes);
 
   CUtensorMap tw, ts, tb, tx;
   if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
@@ -539,8 +547,9 @@ size_t skinny_scratch_bytes(const SkinnyArgs& a, int device) {
   const int NT = a.M <= 8 ? 1 : 2;
   const int BN = kWarpsDefault * 16;
   const long long T = (a.N + BN - 1) / BN;
+  (void)T;
   const long long G = (long long)di.sm_count * 2;  // upper bound on resident CTAs
-  return (size_t)G * 2 * BN * 8 * NT * sizeof(float) + (size_t)T * sizeof(unsigned int);
+  return kCounterBytes + (size_t)G * 2 * BN * 8 * NT * sizeof(float);
 }
 
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,

@@ -177,3 +177,15 @@ def test_invalid_call_raises_with_message():
     wq, s, b = quantized(64, 128)
     with pytest.raises(qw_b200._lib.QwError, match="bits=8"):
         qw_b200.quantized_matmul(dev(synth.activations(1, 128)), dev_u32(wq), dev(s), dev(b), bits=8)
+
+
+def test_split_tiles_across_changing_grids():
+    """Launches whose grids differ in size share the per-stream scratch; the
+    split-tile counters must survive every sequence of shapes."""
+    shapes = [(136, 1024), (40, 576), (5120, 17408), (72, 1536), (1000, 2048), (40, 576)]
+    mats = [quantized(N, K, seed=i) for i, (N, K) in enumerate(shapes)]
+    for rep in range(2):
+        for (N, K), (wq, s, b) in zip(shapes, mats):
+            x = synth.activations(1, K, seed=rep)
+            _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+            assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL, (N, K, rep)
