@@ -18,6 +18,10 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* bas
                     uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle,
                     std::string* err);
 
+bool encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
+                    const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle,
+                    std::string* err);
+
 struct DeviceInfo {
   int device = -1;
   int sm_count = 0;

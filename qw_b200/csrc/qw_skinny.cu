@@ -3,32 +3,37 @@
 // weights are streamed once.
 //
 // Work decomposition ("stream-K"): the weight matrix is cut into row tiles of
-// BN rows and the K axis into 512-wide chunks (8 groups).  The T*C
+// BN = 128 rows and the K axis into 512-wide chunks (8 groups).  The T*C
 // (tile, chunk) units are dealt out as contiguous ranges to a persistent grid
-// of G CTAs, so every CTA streams the same number of bytes whatever N and K
-// are.  A tile whose chunks are split between CTAs is combined through fp32
-// partial slots in scratch memory: every contributor writes its slot, bumps
-// the tile's counter, and the last one to arrive adds the slots in CTA order
-// (deterministic) and writes y.
+// of one CTA per SM, so every CTA streams the same number of bytes whatever N
+// and K are.  A tile whose chunks are split between CTAs is combined through
+// fp32 partial slots in scratch memory: every contributor writes its slot,
+// bumps the tile's counter, and the last one to arrive adds the slots in CTA
+// order (deterministic) and writes y.
 //
-// CTA roles (warp-specialised):
-//   warp 0      TMA producer: packed W (two 128-byte SW128 boxes per stage),
-//               scales, biases, then the x boxes (issued only after
-//               griddepcontrol.wait, so the weight stream of this launch
-//               overlaps the tail of the previous kernel under PDL).
-//   warp 1      x-sum warp: X[g][m] = sum of the 64 x values of group g, in
-//               fp32, for the per-group fold below.
-//   warps 2..   consumers, 16 weight rows each.
+// CTA roles (warp-specialised), per pipeline stage of 128 rows x 512 k:
+//   warp 0        TMA producer: packed W (two 128-byte SW128 boxes, 32 KB),
+//                 scales and biases (one box each), and x (one 3-D box of
+//                 8 groups x M rows), the x box issued only after
+//                 griddepcontrol.wait, so the weight stream of this launch
+//                 overlaps the tail of the previous kernel under PDL.
+//   helper warps  turn the stage's x into the MMA B fragments every consumer
+//                 warp needs (permuted, odd k pre-scaled by 1/16) and the
+//                 per-group sums X and Z of the fold below.
+//   16 consumers  16 weight rows and half of the stage's 8 groups each; the
+//                 two halves of a row tile are added at the end of a tile.
 //
 // Consumer arithmetic (no per-element dequantisation): a packed word w holds
-// 8 nibbles; lop3((w >> 4j) & 0x000F000F | 0x64006400) is an fp16 pair
-// (1024 + q_j, 1024 + q_{j+4}), exact.  Those pairs feed mma.sync m16n8k16
-// directly as the A operand (16 weight rows), with x as B (one column per
-// token) permuted in registers to the same (k, k+4) pairing.  One group's four
-// MMAs give acc = sum_k x_k (1024 + q_k) in fp32; the group is folded into the
-// output as  y += s * acc + (b - 1024 s) * X,  which equals
-// sum_k x_k (s q_k + b) with the weight formed in fp32 (the reference
-// semantics) and fp32 accumulation.
+// nibbles q0..q7 (k ascending).  lop3(w & 0x000F000F | 0x64006400) is the fp16
+// pair (1024 + q0, 1024 + q4) and lop3(w & 0x00F000F0 | 0x64006400) is
+// (1024 + 16 q1, 1024 + 16 q5), both exact; the same on w >> 8 gives q2/q6 and
+// q3/q7.  These feed mma.sync m16n8k16 directly as the A operand (16 weight
+// rows) against x as B (one column per token, odd k scaled by 1/16), so one
+// group's four MMAs give d = 1024 X_even + 64 X_odd + sum_k x_k q_k in fp32.
+// The group is folded into the output as
+//     y += s * (d - Z) + b * X,   Z = 1024 X_even + 64 X_odd,
+// which is sum_k x_k (s q_k + b): the weight formed in fp32 and accumulated in
+// fp32 (the reference semantics).
 #include <cuda_fp16.h>
 
 #include "qw_internal.h"
@@ -40,31 +45,62 @@ namespace {
 
 constexpr int kGroup = 64;
 constexpr int kGroupsPerStage = 8;
-constexpr size_t kMaxCounters = 1u << 16;  // row tiles per launch (N <= 8M rows)
-constexpr size_t kCounterBytes = kMaxCounters * sizeof(unsigned int);
 constexpr int kChunkK = kGroup * kGroupsPerStage;  // 512
+constexpr size_t kMaxCounters = 1u << 16;  // row tiles per launch (N <= 16M rows)
+constexpr size_t kCounterBytes = kMaxCounters * sizeof(unsigned int);
 
-template <int NT, int WARPS, int STAGES>
+constexpr int align1k(int v) { return (v + 1023) / 1024 * 1024; }
+
+// MT: most tokens (rows of x) a launch of this configuration handles.
+//
+// Shared memory holds two rings:
+//   weight ring (WST stages): packed W (two SW128 boxes) + scales + biases of
+//     one unit.  Consumers copy what they need into registers (ldmatrix and
+//     the group's scale/bias pairs) and release the slot before computing, so
+//     a slot is busy only while its copy is in flight: the ring is the
+//     kernel's bytes-in-flight budget against HBM latency.
+//   small ring (SST stages): the unit's x box and what the helper warps derive
+//     from it (MMA B fragments, per-group X / Z sums).  x comes from L2.
+template <int MT>
 struct SkinnyCfg {
-  static constexpr int BN = WARPS * 16;
+  static constexpr int NT = (MT + 7) / 8;       // n8 MMA column tiles
+  static constexpr int MPAD_ = 8 * NT;
+  static constexpr int CW = 16;                 // consumer warps: 8 row tiles x 2 halves of each unit's groups
+  static constexpr int HW = MT == 1 ? 1 : (MT <= 8 ? 2 : 3);  // helper warps
+  static constexpr int BN = 128;                // rows per tile
+  static constexpr int WST = MT == 1 ? 5 : (MT <= 8 ? 4 : 3);
+  static constexpr int SST = MT == 1 ? 4 : (MT <= 8 ? 3 : 2);
   static constexpr int W_BOX = BN * 128;
-  static constexpr int W_BYTES = 2 * W_BOX;
   static constexpr int SB_BYTES = BN * 16;
-  static constexpr int XROWS = 8 * NT;
-  static constexpr int X_GROUP = XROWS * 128;
-  static constexpr int X_BYTES = kGroupsPerStage * X_GROUP;
-  static constexpr int XS_BYTES = kGroupsPerStage * XROWS * 4;
-  static constexpr int OFF_W = 0;
-  static constexpr int OFF_X = W_BYTES;  // multiple of 1024
-  static constexpr int OFF_S = OFF_X + X_BYTES;
-  static constexpr int OFF_B = OFF_S + SB_BYTES;
-  static constexpr int OFF_XS = OFF_B + SB_BYTES;
-  static constexpr int STAGE = ((OFF_XS + XS_BYTES) + 1023) / 1024 * 1024;
-  static constexpr int NBAR = 4 * STAGES;  // wfull, xfull, xready, empty
-  static constexpr int SMEM = STAGES * STAGE + NBAR * 8 + 16 + 1024;
-  static constexpr int THREADS = (WARPS + 2) * 32;
+  static constexpr int W_STAGE = 2 * W_BOX + 2 * SB_BYTES;  // W boxes, scales, biases
+  static constexpr int OFF_WS = 2 * W_BOX;
+  static constexpr int OFF_WB = OFF_WS + SB_BYTES;
+  static constexpr int X_BYTES = kGroupsPerStage * MT * 128;
+  static constexpr int BF_TOK = MT;
+  static constexpr int BF_BYTES = kGroupsPerStage * BF_TOK * 4 * 32;
+  static constexpr int XZ_COLS = 8 * NT;
+  static constexpr int XZ_BYTES = kGroupsPerStage * XZ_COLS * 8;
+  static constexpr int OFF_X = 0;  // within a small stage (1024-aligned for SW128)
+  static constexpr int OFF_BF = align1k(X_BYTES);
+  static constexpr int OFF_XZ = OFF_BF + BF_BYTES;
+  static constexpr int S_STAGE = align1k(OFF_XZ + XZ_BYTES);
+  static constexpr int OFF_WRING = 0;
+  static constexpr int OFF_SRING = WST * W_STAGE;
+  static constexpr int COMB_BYTES = 8 * 32 * 4 * NT * 4;  // k-half partner accumulators
+  static constexpr int OFF_COMB = OFF_SRING + SST * S_STAGE;
+  // Cluster split-K: the leader CTA of a tile receives the other CTAs'
+  // partials here (distributed shared memory).
+  static constexpr int SPLIT_MAX = MT <= 8 ? 4 : 2;
+  static constexpr int RECV_BYTES = (SPLIT_MAX - 1) * BN * MPAD_ * 4;
+  static constexpr int OFF_RECV = OFF_COMB + COMB_BYTES;
+  static constexpr int OFF_BAR = OFF_RECV + RECV_BYTES;
+  static constexpr int NBAR = 2 * WST + 3 * SST + 1;  // wfull, wempty | sfull, ready, sempty | recv
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static constexpr int THREADS = (2 + HW + CW) * 32;
   static constexpr int MPAD = 8 * NT;
   static constexpr int PART = BN * MPAD;  // floats per partial slot
+  static_assert(W_STAGE % 1024 == 0, "weight stages stay 1024-aligned");
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 struct SkinnyParams {
@@ -73,14 +109,14 @@ struct SkinnyParams {
   int T;          // row tiles
   long long U;    // T * C
   int G;          // CTAs
-  int xrows_box;  // rows of x in each x TMA box (min(M, XROWS))
   int sb_tma;     // scales/biases through TMA (needs K % 512 == 0)
+  int split;      // > 1: each tile is split over a cluster of `split` CTAs (G = T * split)
   int y_f32;
   void* y;
   const __half* scales;
   const __half* biases;
   float* part;            // [G][2][PART]
-  unsigned int* counter;  // [T]
+  unsigned int* counter;  // [T], zero between launches
   unsigned int* status;   // device status word
 };
 
@@ -95,151 +131,116 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
-
-__device__ __forceinline__ float sum8_f16(uint4 v) {
-  const __half2* h = reinterpret_cast<const __half2*>(&v);
-  float2 a = __half22float2(h[0]);
-  float2 b = __half22float2(h[1]);
-  float2 c = __half22float2(h[2]);
-  float2 d = __half22float2(h[3]);
-  return ((a.x + a.y) + (b.x + b.y)) + ((c.x + c.y) + (d.x + d.y));
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
 }
+__device__ __forceinline__ void sts_f32x2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ float4 lds_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t w, uint32_t mask) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "r"(mask), "r"(0x64006400u));
+  return r;
+}
+__device__ __forceinline__ float half_lo(uint32_t h2) { return __half2float(__ushort_as_half((uint16_t)(h2 & 0xffffu))); }
+__device__ __forceinline__ float half_hi(uint32_t h2) { return __half2float(__ushort_as_half((uint16_t)(h2 >> 16))); }
 
-template <int NT, int WARPS, int STAGES>
-__global__ void __launch_bounds__((WARPS + 2) * 32, 1)
+template <int MT>
+__global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
     qmm_skinny_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
                       const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_x,
                       const SkinnyParams p) {
-  using Cfg = SkinnyCfg<NT, WARPS, STAGES>;
+  using Cfg = SkinnyCfg<MT>;
+  constexpr int NT = Cfg::NT;
+  constexpr int WST = Cfg::WST;
+  constexpr int SST = Cfg::SST;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE);
+  // Align to 1024 bytes by pointer arithmetic on the shared array itself, so
+  // the compiler keeps treating every access through `smem` as shared memory.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
   uint64_t* wfull = bars;
-  uint64_t* xfull = bars + STAGES;
-  uint64_t* xready = bars + 2 * STAGES;
-  uint64_t* empty = bars + 3 * STAGES;
+  uint64_t* wempty = bars + WST;
+  uint64_t* sfull = bars + 2 * WST;
+  uint64_t* ready = sfull + SST;
+  uint64_t* sempty = ready + SST;
+  uint64_t* recv_bar = sempty + SST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + Cfg::NBAR);
-  volatile int* fin_flag = abort_flag + 1;
+  volatile int* fin_flag = abort_flag + 1;  // [2]: tile+1 to finish per partial slot, 0 = none
+  const uint32_t comb = smem_u32(smem + Cfg::OFF_COMB);
+  uint8_t* wring = smem + Cfg::OFF_WRING;
+  uint8_t* sring = smem + Cfg::OFF_SRING;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const long long u0 = unit_begin(blockIdx.x, p.U, p.G);
   const long long u1 = unit_begin(blockIdx.x + 1, p.U, p.G);
   const int nunits = (int)(u1 - u0);
+  const int first_tile = (int)(u0 / p.C);
+  const int first_chunk = (int)(u0 % p.C);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&wfull[s], 1);
-      mbar_init(&xfull[s], 1);
-      mbar_init(&xready[s], 1);
-      mbar_init(&empty[s], WARPS);
+    for (int i = 0; i < WST; ++i) {
+      mbar_init(&wfull[i], 1);
+      mbar_init(&wempty[i], Cfg::CW);
     }
+    for (int i = 0; i < SST; ++i) {
+      mbar_init(&sfull[i], 1);
+      mbar_init(&ready[i], Cfg::HW);
+      mbar_init(&sempty[i], Cfg::CW);
+    }
+    mbar_init(recv_bar, (p.split - 1) * Cfg::CW);
     *abort_flag = 0;
-    *fin_flag = 0;
+    fin_flag[0] = 0;
+    fin_flag[1] = 0;
     fence_barrier_init();
   }
-  __syncthreads();
+  if (p.split > 1) {
+    // every CTA's barriers are initialised before any remote arrival
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  } else {
+    __syncthreads();
+  }
   pdl_launch_dependents();
 
-  const uint32_t w_bytes = Cfg::W_BYTES + (p.sb_tma ? 2 * Cfg::SB_BYTES : 0);
-  const uint32_t x_bytes = kGroupsPerStage * 128 * p.xrows_box;
-
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ---------------------------------------------------- weight producer
+    // Weights, scales and biases are constants of the launch: this ring does
+    // not wait for the previous kernel at all.
+    const uint32_t w_bytes = 2 * Cfg::W_BOX + (p.sb_tma ? 2 * Cfg::SB_BYTES : 0);
+    const uint64_t pol_w = l2_policy_evict_first();
     if (lane == 0) {
       prefetch_tensormap(&tm_w);
-      prefetch_tensormap(&tm_x);
       if (p.sb_tma) {
         prefetch_tensormap(&tm_s);
         prefetch_tensormap(&tm_b);
       }
-      const uint64_t pol_w = l2_policy_evict_first();
-      auto issue_w = [&](int j) {
-        const long long u = u0 + j;
-        const int t = (int)(u / p.C), c = (int)(u % p.C);
-        const int slot = j % STAGES;
-        uint8_t* st = smem + slot * Cfg::STAGE;
-        mbar_arrive_expect_tx(&wfull[slot], w_bytes);
-        tma_load_2d_hint(st + Cfg::OFF_W, &tm_w, &wfull[slot], c * 256, t * Cfg::BN, pol_w);
-        tma_load_2d_hint(st + Cfg::OFF_W + Cfg::W_BOX, &tm_w, &wfull[slot], c * 256 + 128, t * Cfg::BN, pol_w);
-        if (p.sb_tma) {
-          tma_load_2d_hint(st + Cfg::OFF_S, &tm_s, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
-          tma_load_2d_hint(st + Cfg::OFF_B, &tm_b, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
-        }
-      };
-      auto issue_x = [&](int j) {
-        const long long u = u0 + j;
-        const int c = (int)(u % p.C);
-        const int slot = j % STAGES;
-        uint8_t* st = smem + slot * Cfg::STAGE;
-        mbar_arrive_expect_tx(&xfull[slot], x_bytes);
-        for (int gi = 0; gi < kGroupsPerStage; ++gi)
-          tma_load_2d(st + Cfg::OFF_X + gi * Cfg::X_GROUP, &tm_x, &xfull[slot], c * kChunkK + gi * kGroup, 0);
-      };
-      const int npre = nunits < STAGES ? nunits : STAGES;
-      // Weights do not depend on the previous kernel: start streaming them
-      // before waiting on it.
-      for (int j = 0; j < npre; ++j) issue_w(j);
-      pdl_wait();
-      for (int j = 0; j < npre; ++j) issue_x(j);
-      int issued = npre;
-      for (int j = npre; j < nunits; ++j) {
-        const int slot = j % STAGES;
-        const int round = j / STAGES;
-        if (!*abort_flag) {
-          if (!mbar_wait(&empty[slot], (round - 1) & 1, p.status, kDevTimeoutEmpty)) *abort_flag = 1;
-        }
-        if (*abort_flag) break;
-        issue_w(j);
-        issue_x(j);
-        issued = j + 1;
-      }
-      if (*abort_flag) {
-        // Let the copies already in flight land before the CTA retires.
-        const int first = issued > STAGES ? issued - STAGES : 0;
-        for (int j = first; j < issued; ++j) {
-          const int slot = j % STAGES;
-          mbar_wait(&wfull[slot], (j / STAGES) & 1, p.status, kDevTimeoutFull);
-          mbar_wait(&xfull[slot], (j / STAGES) & 1, p.status, kDevTimeoutFull);
-        }
-      }
     }
-    return;
-  }
-
-  if (warp == 1) {
-    // -------------------------------------------------------------- x sums
-    pdl_wait();
+    const int G = p.K / kGroup;
+    int t = first_tile, c = first_chunk, slot = 0;
+    uint32_t phase = 0;
     for (int j = 0; j < nunits; ++j) {
-      const long long u = u0 + j;
-      const int t = (int)(u / p.C), c = (int)(u % p.C);
-      const int slot = j % STAGES;
-      uint8_t* st = smem + slot * Cfg::STAGE;
-      if (!*abort_flag && !mbar_wait(&xfull[slot], (j / STAGES) & 1, p.status, kDevTimeoutFull)) *abort_flag = 1;
-      const uint32_t xbase = smem_u32(st + Cfg::OFF_X);
-      float* xs = reinterpret_cast<float*>(st + Cfg::OFF_XS);
-      const int ntask = kGroupsPerStage * p.M;
-      for (int t0 = 0; t0 < ntask; t0 += 4) {
-        const int task = t0 + lane / 8;
-        const int sub = lane % 8;
-        float v = 0.f;
-        int gi = 0, n = 0;
-        if (task < ntask) {
-          gi = task / p.M;
-          n = task - gi * p.M;
-          v = sum8_f16(lds128(xbase + gi * Cfg::X_GROUP + n * 128 + ((sub ^ (n & 7)) << 4)));
-        }
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        if (sub == 0 && task < ntask) xs[gi * Cfg::XROWS + n] = v;
+      if (j >= WST && !*abort_flag) {
+        if (!mbar_wait(&wempty[slot], phase ^ 1u, p.status, kDevTimeoutEmpty)) *abort_flag = 1;
       }
+      if (*abort_flag) break;
+      uint8_t* st = wring + slot * Cfg::W_STAGE;
       if (!p.sb_tma) {
         // Scales/biases rows are not 16-byte strided (K % 512 != 0): stage
         // them with plain loads, zero beyond the matrix edge.
-        __half* ss = reinterpret_cast<__half*>(st + Cfg::OFF_S);
-        __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_B);
-        const int G = p.K / kGroup;
+        __half* ss = reinterpret_cast<__half*>(st + Cfg::OFF_WS);
+        __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_WB);
         for (int e = lane; e < Cfg::BN * kGroupsPerStage; e += 32) {
           const int r = e / kGroupsPerStage, g = e % kGroupsPerStage;
           const int row = t * Cfg::BN + r, grp = c * kGroupsPerStage + g;
@@ -251,121 +252,342 @@ __global__ void __launch_bounds__((WARPS + 2) * 32, 1)
           ss[e] = sv;
           sb[e] = bv;
         }
+        __syncwarp();
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&wfull[slot], w_bytes);
+        tma_load_2d_hint(st, &tm_w, &wfull[slot], c * 256, t * Cfg::BN, pol_w);
+        tma_load_2d_hint(st + Cfg::W_BOX, &tm_w, &wfull[slot], c * 256 + 128, t * Cfg::BN, pol_w);
+        if (p.sb_tma) {
+          tma_load_2d_hint(st + Cfg::OFF_WS, &tm_s, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
+          tma_load_2d_hint(st + Cfg::OFF_WB, &tm_b, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
+        }
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&xready[slot]);
+      if (++slot == WST) {
+        slot = 0;
+        phase ^= 1u;
+      }
+      if (++c == p.C) {
+        c = 0;
+        ++t;
+      }
+    }
+    return;
+  }
+
+  if (warp == 1) {
+    // ------------------------------------------------------- x producer
+    if (lane == 0) {
+      prefetch_tensormap(&tm_x);
+      const uint32_t x_bytes = kGroupsPerStage * 128 * p.M;
+      pdl_wait();  // x is the previous kernel's output
+      int c = first_chunk, slot = 0;
+      uint32_t phase = 0;
+      for (int j = 0; j < nunits; ++j) {
+        if (j >= SST && !*abort_flag) {
+          if (!mbar_wait(&sempty[slot], phase ^ 1u, p.status, kDevTimeoutEmpty)) *abort_flag = 1;
+        }
+        if (*abort_flag) break;
+        mbar_arrive_expect_tx(&sfull[slot], x_bytes);
+        tma_load_3d(sring + slot * Cfg::S_STAGE + Cfg::OFF_X, &tm_x, &sfull[slot], 0, 0, c * kGroupsPerStage);
+        if (++slot == SST) {
+          slot = 0;
+          phase ^= 1u;
+        }
+        if (++c == p.C) c = 0;
+      }
+    }
+    return;
+  }
+
+  if (warp < 2 + Cfg::HW) {
+    // ------------------------------------------------------------- helpers
+    const int h = warp - 2;
+    pdl_wait();
+    // (X, Z) of token columns >= M stay zero for the whole launch.
+    for (int e = h * 32 + lane; e < SST * kGroupsPerStage * Cfg::XZ_COLS; e += Cfg::HW * 32) {
+      const int slot = e / (kGroupsPerStage * Cfg::XZ_COLS);
+      const int col = e % Cfg::XZ_COLS;
+      if (col >= p.M) {
+        const int gi = (e / Cfg::XZ_COLS) % kGroupsPerStage;
+        sts_f32x2(smem_u32(sring + slot * Cfg::S_STAGE + Cfg::OFF_XZ) + (gi * Cfg::XZ_COLS + col) * 8, 0.f, 0.f);
+      }
+    }
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int j = 0; j < nunits; ++j) {
+      if (!*abort_flag && !mbar_wait(&sfull[slot], phase, p.status, kDevTimeoutFull)) *abort_flag = 1;
+      uint8_t* st = sring + slot * Cfg::S_STAGE;
+      const uint32_t xbase = smem_u32(st + Cfg::OFF_X);
+      const uint32_t bf = smem_u32(st + Cfg::OFF_BF);
+      const uint32_t xz = smem_u32(st + Cfg::OFF_XZ);
+      // task = ((gi * M + n) * 4 + s): lanes 4k..4k+3 share one (group, token)
+      for (int base = h * 32; base < 32 * p.M; base += Cfg::HW * 32) {
+        const int task = base + lane;
+        const int s = task & 3;
+        const int gn = task >> 2;
+        const int gi = MT == 1 ? gn : gn / p.M;
+        const int n = MT == 1 ? 0 : gn - gi * p.M;
+        const int line = gn;  // box layout [group][token][64 halves]
+        const uint4 xv0 = lds128(xbase + line * 128 + ((s ^ (line & 7)) << 4));
+        const uint4 xv1 = lds128(xbase + line * 128 + (((4 + s) ^ (line & 7)) << 4));
+        // B fragment of MMA jj: (x[8s+jj], x[8s+jj+4]) and the same 32 further
+        // on; odd jj scaled by 1/16 to match the in-place odd nibbles.
+        uint4 f0, f1;
+        f0.x = prmt(xv0.x, xv0.z, 0x5410);
+        f0.y = prmt(xv1.x, xv1.z, 0x5410);
+        f0.z = hmul2_rn(prmt(xv0.x, xv0.z, 0x7632), 0x2C002C00u);
+        f0.w = hmul2_rn(prmt(xv1.x, xv1.z, 0x7632), 0x2C002C00u);
+        f1.x = prmt(xv0.y, xv0.w, 0x5410);
+        f1.y = prmt(xv1.y, xv1.w, 0x5410);
+        f1.z = hmul2_rn(prmt(xv0.y, xv0.w, 0x7632), 0x2C002C00u);
+        f1.w = hmul2_rn(prmt(xv1.y, xv1.w, 0x7632), 0x2C002C00u);
+        const uint32_t fa = bf + ((gi * Cfg::BF_TOK + n) * 4 + s) * 32;
+        sts128(fa, f0);
+        sts128(fa + 16, f1);
+        // sums over even and odd k of the 16 x values this lane holds
+        float xe = 0.f, xo = 0.f;
+        const uint32_t wv[8] = {xv0.x, xv0.y, xv0.z, xv0.w, xv1.x, xv1.y, xv1.z, xv1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[i]));
+          xe += f.x;
+          xo += f.y;
+        }
+        xe += __shfl_xor_sync(0xffffffffu, xe, 1);
+        xo += __shfl_xor_sync(0xffffffffu, xo, 1);
+        xe += __shfl_xor_sync(0xffffffffu, xe, 2);
+        xo += __shfl_xor_sync(0xffffffffu, xo, 2);
+        if (s == 0) sts_f32x2(xz + (gi * Cfg::XZ_COLS + n) * 8, xe + xo, 1024.f * xe + 64.f * xo);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[slot]);
+      if (++slot == SST) {
+        slot = 0;
+        phase ^= 1u;
+      }
     }
     return;
   }
 
   // ----------------------------------------------------------------- consumers
-  const int cw = warp - 2;
-  const int wrow = cw * 16;          // first row of this warp inside the tile
+  const int cw = warp - 2 - Cfg::HW;
+  const int rt = cw & 7;             // row tile of this warp
+  const int kh = cw >> 3;            // which half of each unit's 8 groups
+  const int wrow = rt * 16;          // first row of this warp inside the tile
   const int r = lane / 4, s4 = lane % 4;
   pdl_wait();
 
   float acc[NT][4];
 #pragma unroll
-  for (int t = 0; t < NT; ++t)
+  for (int q = 0; q < NT; ++q)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[t][e] = 0.f;
-
-  const int first_tile = (int)(u0 / p.C);
-  int seg_begin = (int)(u0 % p.C);
+    for (int e = 0; e < 4; ++e) acc[q][e] = 0.f;
 
   // ldmatrix lane addressing: matrix mi = lane/8 covers rows 8*(mi&1).. of
-  // chunk (mi>>1) of the group.
+  // chunk (mi>>1) of the group; per-lane offsets hoisted out of the loop.
   const int lm_mi = lane / 8;
   const int lm_row = wrow + (lane % 8) + 8 * (lm_mi & 1);
   const int lm_sw = lm_row & 7;
+  uint32_t lm_off[4];
+#pragma unroll
+  for (int g4 = 0; g4 < 4; ++g4)
+    lm_off[g4] = kh * Cfg::W_BOX + lm_row * 128 + (((g4 * 2 + (lm_mi >> 1)) ^ lm_sw) << 4);
+  // scale/bias rows r and r+8 of this warp, groups kh*4 .. kh*4+3 (8 bytes)
+  const uint32_t sb_off = (wrow + r) * 16 + kh * 8;
+  // B fragments: a lane whose token column is >= M reads token M-1's (a
+  // shared-memory broadcast).  MMA output columns depend only on their own B
+  // column, so those columns are never mixed into a written result.
+  uint32_t bf_off[NT];
+#pragma unroll
+  for (int tt = 0; tt < NT; ++tt) {
+    const int tok = (tt * 8 + r) < p.M ? (tt * 8 + r) : (p.M - 1);
+    bf_off[tt] = Cfg::OFF_BF + ((kh * 4 * Cfg::BF_TOK + tok) * 4 + s4) * 32;
+  }
+  const uint32_t xz_off = Cfg::OFF_XZ + 2 * s4 * 8 + kh * 4 * Cfg::XZ_COLS * 8;
+  const uint32_t wring_u = smem_u32(wring);
+  const uint32_t sring_u = smem_u32(sring);
 
+  int t = first_tile, c = first_chunk, wslot = 0, sslot = 0;
+  uint32_t wphase = 0, sphase = 0;
+  int seg_begin = first_chunk;
   for (int j = 0; j < nunits; ++j) {
-    const long long u = u0 + j;
-    const int t = (int)(u / p.C), c = (int)(u % p.C);
-    const int slot = j % STAGES;
-    const uint32_t parity = (j / STAGES) & 1;
-    uint8_t* st = smem + slot * Cfg::STAGE;
-    if (!*abort_flag) {
-      if (!mbar_wait(&wfull[slot], parity, p.status, kDevTimeoutFull)) *abort_flag = 1;
-      else if (!mbar_wait(&xready[slot], parity, p.status, kDevTimeoutFull)) *abort_flag = 1;
+    // 1) copy this warp's share of the unit's weights, scales and biases into
+    //    registers, then give the weight slot back to the producer.
+    uint32_t A[4][4];
+    uint2 sv_lo, sv_hi, bv_lo, bv_hi;
+    if (!*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
+    {
+      const uint32_t wb = wring_u + wslot * Cfg::W_STAGE;
+#pragma unroll
+      for (int g4 = 0; g4 < 4; ++g4) ldmatrix_x4(wb + lm_off[g4], A[g4][0], A[g4][1], A[g4][2], A[g4][3]);
+      sv_lo = lds64(wb + Cfg::OFF_WS + sb_off);
+      sv_hi = lds64(wb + Cfg::OFF_WS + sb_off + 8 * 16);
+      bv_lo = lds64(wb + Cfg::OFF_WB + sb_off);
+      bv_hi = lds64(wb + Cfg::OFF_WB + sb_off + 8 * 16);
     }
-    if (!*abort_flag) {
-      const uint32_t wbase = smem_u32(st + Cfg::OFF_W);
-      const uint32_t xbase = smem_u32(st + Cfg::OFF_X);
-      const uint4 sv_lo = *reinterpret_cast<const uint4*>(st + Cfg::OFF_S + (wrow + r) * 16);
-      const uint4 sv_hi = *reinterpret_cast<const uint4*>(st + Cfg::OFF_S + (wrow + r + 8) * 16);
-      const uint4 bv_lo = *reinterpret_cast<const uint4*>(st + Cfg::OFF_B + (wrow + r) * 16);
-      const uint4 bv_hi = *reinterpret_cast<const uint4*>(st + Cfg::OFF_B + (wrow + r + 8) * 16);
-      const float* xs = reinterpret_cast<const float*>(st + Cfg::OFF_XS);
-#pragma unroll
-      for (int gi = 0; gi < kGroupsPerStage; ++gi) {
-        const int box = gi / 4;
-        const int chunk = (gi % 4) * 2 + (lm_mi >> 1);
-        uint32_t A0, A1, A2, A3;
-        ldmatrix_x4(wbase + box * Cfg::W_BOX + lm_row * 128 + ((chunk ^ lm_sw) << 4), A0, A1, A2, A3);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&wempty[wslot]);
 
-        uint32_t bfr[NT][4][2];
+    // 2) compute against the unit's x fragments.
+    if (!*abort_flag && !mbar_wait(&ready[sslot], sphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
+    if (!*abort_flag) {
+      const uint8_t* stp = sring + sslot * Cfg::S_STAGE;
+      (void)sring_u;
+#pragma unroll
+      for (int g4 = 0; g4 < 4; ++g4) {
+        uint4 b0[NT], b1[NT];
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
-          const int n = tt * 8 + r;
-          uint4 xv0 = make_uint4(0, 0, 0, 0), xv1 = make_uint4(0, 0, 0, 0);
-          if (n < p.M) {
-            const uint32_t rowaddr = xbase + gi * Cfg::X_GROUP + n * 128;
-            xv0 = lds128(rowaddr + ((s4 ^ (n & 7)) << 4));
-            xv1 = lds128(rowaddr + (((4 + s4) ^ (n & 7)) << 4));
+          const uint4* fb = reinterpret_cast<const uint4*>(stp + bf_off[tt] + g4 * (Cfg::BF_TOK * 4 * 32));
+          b0[tt] = fb[0];
+          b1[tt] = fb[1];
+        }
+        // expanded A registers: e[jj][i] for word i
+        uint32_t e[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t w8 = A[g4][i] >> 8;
+          e[0][i] = lop3_and_or(A[g4][i], 0x000F000Fu);
+          e[1][i] = lop3_and_or(A[g4][i], 0x00F000F0u);
+          e[2][i] = lop3_and_or(w8, 0x000F000Fu);
+          e[3][i] = lop3_and_or(w8, 0x00F000F0u);
+        }
+        float dA[NT][4], dB[NT][4];
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt) {
+          mma_16816_zc(dA[tt], e[0][0], e[0][1], e[0][2], e[0][3], b0[tt].x, b0[tt].y);
+          mma_16816_zc(dB[tt], e[1][0], e[1][1], e[1][2], e[1][3], b0[tt].z, b0[tt].w);
+          mma_16816(dA[tt], e[2][0], e[2][1], e[2][2], e[2][3], b1[tt].x, b1[tt].y);
+          mma_16816(dB[tt], e[3][0], e[3][1], e[3][2], e[3][3], b1[tt].z, b1[tt].w);
+        }
+        // fold the group: y += s * (d - Z) + b * X
+        const uint32_t s_w_lo = (g4 < 2) ? sv_lo.x : sv_lo.y, s_w_hi = (g4 < 2) ? sv_hi.x : sv_hi.y;
+        const uint32_t b_w_lo = (g4 < 2) ? bv_lo.x : bv_lo.y, b_w_hi = (g4 < 2) ? bv_hi.x : bv_hi.y;
+        const float s_r = (g4 & 1) ? half_hi(s_w_lo) : half_lo(s_w_lo);
+        const float s_r8 = (g4 & 1) ? half_hi(s_w_hi) : half_lo(s_w_hi);
+        const float b_r = (g4 & 1) ? half_hi(b_w_lo) : half_lo(b_w_lo);
+        const float b_r8 = (g4 & 1) ? half_hi(b_w_hi) : half_lo(b_w_hi);
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt) {
+          const float4 v =
+              *reinterpret_cast<const float4*>(stp + xz_off + (g4 * Cfg::XZ_COLS + tt * 8) * 8);  // X0, Z0, X1, Z1
+          acc[tt][0] = fmaf(s_r, (dA[tt][0] + dB[tt][0]) - v.y, fmaf(b_r, v.x, acc[tt][0]));
+          acc[tt][2] = fmaf(s_r8, (dA[tt][2] + dB[tt][2]) - v.y, fmaf(b_r8, v.x, acc[tt][2]));
+          if (MT > 1) {  // a single token uses column 0 only
+            acc[tt][1] = fmaf(s_r, (dA[tt][1] + dB[tt][1]) - v.w, fmaf(b_r, v.z, acc[tt][1]));
+            acc[tt][3] = fmaf(s_r8, (dA[tt][3] + dB[tt][3]) - v.w, fmaf(b_r8, v.z, acc[tt][3]));
           }
-          bfr[tt][0][0] = prmt(xv0.x, xv0.z, 0x5410);
-          bfr[tt][1][0] = prmt(xv0.x, xv0.z, 0x7632);
-          bfr[tt][2][0] = prmt(xv0.y, xv0.w, 0x5410);
-          bfr[tt][3][0] = prmt(xv0.y, xv0.w, 0x7632);
-          bfr[tt][0][1] = prmt(xv1.x, xv1.z, 0x5410);
-          bfr[tt][1][1] = prmt(xv1.x, xv1.z, 0x7632);
-          bfr[tt][2][1] = prmt(xv1.y, xv1.w, 0x5410);
-          bfr[tt][3][1] = prmt(xv1.y, xv1.w, 0x7632);
-        }
-        float d[NT][4];
-#pragma unroll
-        for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) d[tt][e] = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const uint32_t a0 = lop3_expand(A0 >> (4 * jj));
-          const uint32_t a1 = lop3_expand(A1 >> (4 * jj));
-          const uint32_t a2 = lop3_expand(A2 >> (4 * jj));
-          const uint32_t a3 = lop3_expand(A3 >> (4 * jj));
-#pragma unroll
-          for (int tt = 0; tt < NT; ++tt) mma_16816(d[tt], a0, a1, a2, a3, bfr[tt][jj][0], bfr[tt][jj][1]);
-        }
-        // fold the group: y += s*acc + (b - 1024 s) * X
-        const __half* slo = reinterpret_cast<const __half*>(&sv_lo);
-        const __half* shi = reinterpret_cast<const __half*>(&sv_hi);
-        const __half* blo = reinterpret_cast<const __half*>(&bv_lo);
-        const __half* bhi = reinterpret_cast<const __half*>(&bv_hi);
-        const float s_r = __half2float(slo[gi]);
-        const float s_r8 = __half2float(shi[gi]);
-        const float c_r = __half2float(blo[gi]) - 1024.f * s_r;
-        const float c_r8 = __half2float(bhi[gi]) - 1024.f * s_r8;
-#pragma unroll
-        for (int tt = 0; tt < NT; ++tt) {
-          const float2 X = *reinterpret_cast<const float2*>(xs + gi * Cfg::XROWS + tt * 8 + 2 * s4);
-          acc[tt][0] += s_r * d[tt][0] + c_r * X.x;
-          acc[tt][1] += s_r * d[tt][1] + c_r * X.y;
-          acc[tt][2] += s_r8 * d[tt][2] + c_r8 * X.x;
-          acc[tt][3] += s_r8 * d[tt][3] + c_r8 * X.y;
         }
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (lane == 0) mbar_arrive(&sempty[sslot]);
 
     const bool seg_end = (c == p.C - 1) || (j == nunits - 1);
+    const int t_done = t;
+    if (++wslot == WST) {
+      wslot = 0;
+      wphase ^= 1u;
+    }
+    if (++sslot == SST) {
+      sslot = 0;
+      sphase ^= 1u;
+    }
+    if (++c == p.C) {
+      c = 0;
+      ++t;
+    }
     if (!seg_end) continue;
+    const bool whole = (seg_begin == 0) && (c == 0);
 
-    const int row0 = t * Cfg::BN + wrow + r;
-    const bool whole = (seg_begin == 0) && (c == p.C - 1);
-    if (whole) {
-      if (!*abort_flag) {
+    // Combine the two k-halves of each row tile: the second-half warp hands
+    // its accumulators to its partner through shared memory.
+    const uint32_t my_comb = comb + (rt * 32 + lane) * (16 * NT);
+    if (kh == 1) {
+#pragma unroll
+      for (int tt = 0; tt < NT; ++tt)
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(my_comb + tt * 16), "f"(acc[tt][0]),
+                     "f"(acc[tt][1]), "f"(acc[tt][2]), "f"(acc[tt][3])
+                     : "memory");
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+    if (kh == 0) {
+#pragma unroll
+      for (int tt = 0; tt < NT; ++tt) {
+        const float4 v = lds_f32x4(my_comb + tt * 16);
+        acc[tt][0] += v.x;
+        acc[tt][1] += v.y;
+        acc[tt][2] += v.z;
+        acc[tt][3] += v.w;
+      }
+    }
+    const int row0 = t_done * Cfg::BN + wrow + r;
+    if (p.split > 1) {
+      // Cluster split-K: this CTA's only segment.  Non-leaders store their
+      // partial into the leader's shared memory and arrive on its barrier;
+      // the leader adds them in rank order and writes y.
+      uint32_t rank;
+      asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+      const uint32_t recv = smem_u32(smem + Cfg::OFF_RECV);
+      if (rank != 0) {
+        if (kh == 0) {
+          const uint32_t lrecv = recv + (rank - 1) * (Cfg::BN * Cfg::MPAD * 4);
+          uint32_t rrecv;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rrecv) : "r"(lrecv));
+#pragma unroll
+          for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int rl = wrow + r + 8 * hh;
+              const uint32_t a = rrecv + (rl * Cfg::MPAD + tt * 8 + 2 * s4) * 4;
+              asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(acc[tt][2 * hh]),
+                           "f"(acc[tt][2 * hh + 1])
+                           : "memory");
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          uint32_t rbar;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rbar) : "r"(smem_u32(recv_bar)));
+          asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(rbar) : "memory");
+        }
+      } else {
+        if (!*abort_flag && !mbar_wait(recv_bar, 0, p.status, kDevTimeoutAccum)) *abort_flag = 1;
+        asm volatile("fence.acq_rel.cluster;" ::: "memory");
+        if (kh == 0 && !*abort_flag) {
+          for (int q = 1; q < p.split; ++q) {
+            const uint32_t lrecv = recv + (q - 1) * (Cfg::BN * Cfg::MPAD * 4);
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                const int rl = wrow + r + 8 * hh;
+                float2 v;
+                asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];"
+                             : "=f"(v.x), "=f"(v.y)
+                             : "r"(lrecv + (rl * Cfg::MPAD + tt * 8 + 2 * s4) * 4));
+                acc[tt][2 * hh] += v.x;
+                acc[tt][2 * hh + 1] += v.y;
+              }
+          }
+#pragma unroll
+          for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int n = tt * 8 + 2 * s4 + (e & 1);
+              const int row = row0 + ((e & 2) ? 8 : 0);
+              if (n < p.M && row < p.N) {
+                const size_t idx = (size_t)n * p.N + row;
+                if (p.y_f32) reinterpret_cast<float*>(p.y)[idx] = acc[tt][e];
+                else reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(acc[tt][e]);
+              }
+            }
+        }
+      }
+    } else if (whole) {
+      if (kh == 0 && !*abort_flag) {
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
@@ -380,33 +602,50 @@ __global__ void __launch_bounds__((WARPS + 2) * 32, 1)
           }
       }
     } else {
-      // split tile: publish this CTA's partial, last contributor reduces.
-      const int slot_idx = (t == first_tile) ? 0 : 1;
+      // Split tile: publish this CTA's partial; the last contributor to
+      // arrive adds the partials in CTA order.  A segment that is not this
+      // CTA's final one does not wait for its arrival's result: thread 0
+      // (consumer warp 0) fences and arrives while the other warps go on
+      // consuming, and a tile found complete there is finished after the
+      // final segment.
+      const int slot_idx = (t_done == first_tile) ? 0 : 1;
       float* mine = p.part + ((size_t)blockIdx.x * 2 + slot_idx) * Cfg::PART;
+      if (kh == 0) {
 #pragma unroll
-      for (int tt = 0; tt < NT; ++tt)
+        for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int n = tt * 8 + 2 * s4 + (e & 1);
-          const int rl = wrow + r + ((e & 2) ? 8 : 0);
-          mine[rl * Cfg::MPAD + n] = acc[tt][e];
-        }
-      __threadfence();
-      asm volatile("bar.sync 1, %0;" ::"r"(WARPS * 32) : "memory");
-      const long long tu0 = (long long)t * p.C;
-      const int i_first = cta_of_unit(tu0, p.U, p.G);
-      const int i_last = cta_of_unit(tu0 + p.C - 1, p.U, p.G);
-      if (cw == 0 && lane == 0) {
-        const unsigned int ncontrib = (unsigned int)(i_last - i_first + 1);
-        const unsigned int old = atomicAdd(&p.counter[t], 1u);
-        const int last = (old == ncontrib - 1) ? 1 : 0;
-        if (last) atomicExch(&p.counter[t], 0u);
-        *fin_flag = last;
+          for (int e = 0; e < 4; ++e) {
+            const int n = tt * 8 + 2 * s4 + (e & 1);
+            const int rl = wrow + r + ((e & 2) ? 8 : 0);
+            mine[rl * Cfg::MPAD + n] = acc[tt][e];
+          }
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(WARPS * 32) : "memory");
-      const int last = *fin_flag;
-      if (last) {
-        __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+      if (cw == 0 && lane == 0) {
+        // One release fence for the whole CTA's partial (ordered before it by
+        // the barrier), then the arrival; the last arrival acquires.
+        const long long tu0 = (long long)t_done * p.C;
+        const unsigned int ncontrib =
+            (unsigned int)(cta_of_unit(tu0 + p.C - 1, p.U, p.G) - cta_of_unit(tu0, p.U, p.G) + 1);
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        const unsigned int old = atomicAdd(&p.counter[t_done], 1u);
+        if (old == ncontrib - 1) {
+          atomicExch(&p.counter[t_done], 0u);
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
+          fin_flag[slot_idx] = t_done + 1;  // finish tile t_done after the final segment
+        }
+      }
+    }
+    if (j == nunits - 1) {
+      // Final segment: finish the split tiles this CTA completed.
+      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+#pragma unroll 1
+      for (int q = 0; q < 2; ++q) {
+        const int tf = fin_flag[q] - 1;
+        if (tf < 0 || kh != 0) continue;
+        const long long tu0 = (long long)tf * p.C;
+        const int i_first = cta_of_unit(tu0, p.U, p.G);
+        const int i_last = cta_of_unit(tu0 + p.C - 1, p.U, p.G);
         float tot[NT][4];
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt)
@@ -414,7 +653,7 @@ __global__ void __launch_bounds__((WARPS + 2) * 32, 1)
           for (int e = 0; e < 4; ++e) tot[tt][e] = 0.f;
         for (int i = i_first; i <= i_last; ++i) {
           const int ft = (int)(unit_begin(i, p.U, p.G) / p.C);
-          const float* src = p.part + ((size_t)i * 2 + (t == ft ? 0 : 1)) * Cfg::PART;
+          const float* src = p.part + ((size_t)i * 2 + (tf == ft ? 0 : 1)) * Cfg::PART;
 #pragma unroll
           for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
@@ -425,12 +664,13 @@ __global__ void __launch_bounds__((WARPS + 2) * 32, 1)
             }
         }
         if (!*abort_flag) {
+          const int rowf = tf * Cfg::BN + wrow + r;
 #pragma unroll
           for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int n = tt * 8 + 2 * s4 + (e & 1);
-              const int row = row0 + ((e & 2) ? 8 : 0);
+              const int row = rowf + ((e & 2) ? 8 : 0);
               if (n < p.M && row < p.N) {
                 const size_t idx = (size_t)n * p.N + row;
                 if (p.y_f32) reinterpret_cast<float*>(p.y)[idx] = tot[tt][e];
@@ -439,9 +679,9 @@ __global__ void __launch_bounds__((WARPS + 2) * 32, 1)
             }
         }
       }
-      // the flag is rewritten by the next split tile only after this barrier
-      asm volatile("bar.sync 1, %0;" ::"r"(WARPS * 32) : "memory");
     }
+    // the combine buffer and the flag are rewritten only after this barrier
+    asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
@@ -450,11 +690,11 @@ __global__ void __launch_bounds__((WARPS + 2) * 32, 1)
   }
 }
 
-template <int NT, int WARPS, int STAGES>
+template <int MT>
 cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                        std::string* err) {
-  using Cfg = SkinnyCfg<NT, WARPS, STAGES>;
-  auto kern = qmm_skinny_kernel<NT, WARPS, STAGES>;
+  using Cfg = SkinnyCfg<MT>;
+  auto kern = qmm_skinny_kernel<MT>;
   int dev = 0;
   cudaGetDevice(&dev);
   const DeviceInfo& di = device_info(dev);
@@ -472,17 +712,22 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   p.C = (int)((a.K + kChunkK - 1) / kChunkK);
   p.T = (int)((a.N + Cfg::BN - 1) / Cfg::BN);
   p.U = (long long)p.T * p.C;
-  static thread_local int occ_dev = -1, occ = 1;
-  if (occ_dev != dev) {
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, Cfg::THREADS, Cfg::SMEM);
-    if (occ < 1) occ = 1;
-    occ_dev = dev;
-  }
-  long long G = (long long)di.sm_count * occ;
+  // Schedule: with fewer row tiles than SMs, each tile gets `split` CTAs (a
+  // thread-block cluster reducing through distributed shared memory; one
+  // CTA per tile when split == 1).  Otherwise stream-K over all SMs.
+  long long G = (long long)di.sm_count;
   if (a.max_ctas > 0 && G > a.max_ctas) G = a.max_ctas;
+  p.split = 1;
+  if (p.T <= G) {
+    int split = (int)(G / p.T);
+    if (split > Cfg::SPLIT_MAX) split = Cfg::SPLIT_MAX;
+    if (split > p.C) split = p.C;
+    if (split < 1) split = 1;
+    p.split = split;
+    G = (long long)p.T * split;
+  }
   if (G > p.U) G = p.U;
   p.G = (int)G;
-  p.xrows_box = (int)(a.M < Cfg::XROWS ? a.M : Cfg::XROWS);
   p.sb_tma = (a.K % kChunkK == 0) ? 1 : 0;
   p.y_f32 = a.y_f32 ? 1 : 0;
   p.y = a.y;
@@ -508,9 +753,15 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
                       (uint64_t)(a.K / 2), 128, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_128B, err))
     return cudaErrorInvalidValue;
-  if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
-                      (uint64_t)a.K * 2, kGroup, (uint32_t)p.xrows_box, CU_TENSOR_MAP_SWIZZLE_128B, err))
-    return cudaErrorInvalidValue;
+  {
+    // x viewed as [K/64 groups][M tokens][64 halves]: one box = 8 groups x M tokens
+    const uint64_t dims[3] = {(uint64_t)kGroup, (uint64_t)a.M, (uint64_t)(a.K / kGroup)};
+    const uint64_t strides[2] = {(uint64_t)a.K * 2, (uint64_t)kGroup * 2};
+    const uint32_t box[3] = {(uint32_t)kGroup, (uint32_t)a.M, (uint32_t)kGroupsPerStage};
+    if (!encode_tmap_3d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                        err))
+      return cudaErrorInvalidValue;
+  }
   if (p.sb_tma) {
     const uint64_t G64 = (uint64_t)(a.K / kGroup);
     if (!encode_tmap_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.scales, G64, (uint64_t)a.N, G64 * 2,
@@ -529,33 +780,39 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   cfg.blockDim = dim3(Cfg::THREADS);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int nattr = 0;
+  if (pdl) {
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+  }
+  if (p.split > 1) {
+    attr[nattr].id = cudaLaunchAttributeClusterDimension;
+    attr[nattr].val.clusterDim.x = (unsigned)p.split;
+    attr[nattr].val.clusterDim.y = 1;
+    attr[nattr].val.clusterDim.z = 1;
+    ++nattr;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = nattr;
   return cudaLaunchKernelEx(&cfg, kern, tw, ts, tb, tx, p);
 }
-
-// Configuration table: (NT, consumer warps, stages).
-constexpr int kWarpsDefault = 8;
 
 }  // namespace
 
 size_t skinny_scratch_bytes(const SkinnyArgs& a, int device) {
   const DeviceInfo& di = device_info(device);
-  const int NT = a.M <= 8 ? 1 : 2;
-  const int BN = kWarpsDefault * 16;
-  const long long T = (a.N + BN - 1) / BN;
-  (void)T;
-  const long long G = (long long)di.sm_count * 2;  // upper bound on resident CTAs
-  return kCounterBytes + (size_t)G * 2 * BN * 8 * NT * sizeof(float);
+  const int mpad = a.M <= 8 ? 8 : 16;
+  const int BN = 128;
+  return kCounterBytes + (size_t)di.sm_count * 2 * BN * mpad * sizeof(float);
 }
 
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                           std::string* err) {
-  if (a.M <= 8) return launch_cfg<1, kWarpsDefault, 4>(a, scratch, stream, pdl, err);
-  return launch_cfg<2, kWarpsDefault, 3>(a, scratch, stream, pdl, err);
+  if (a.M == 1) return launch_cfg<1>(a, scratch, stream, pdl, err);
+  if (a.M <= 8) return launch_cfg<8>(a, scratch, stream, pdl, err);
+  return launch_cfg<16>(a, scratch, stream, pdl, err);
 }
 
 }  // namespace qw
