@@ -1,15 +1,354 @@
-// qw_prefill.cu -- prefill (M >= 17) affine 4-bit quantized matmul on the
-// 5th-generation tensor cores.  Placeholder until the tcgen05 kernel lands:
-// reports itself unavailable so the dispatcher uses the skinny path.
+// qw_prefill.cu -- affine 4-bit group-64 quantized matmul for prefill-sized
+// M (>= 17 rows of x) on the 5th-generation tensor cores.  Compute-bound.
+//
+// One CTA per SM walks output tiles of 128 weight rows x 256 tokens
+// (persistent, token tiles fastest so a weight tile is reused from L2):
+//
+//   warp 0      TMA producer, per 64-wide k group: the x box (256 tokens x
+//               64 halves, 128-byte swizzle, K-major: the UMMA B operand) and
+//               the packed weights of the group (128 rows x 32 bytes).
+//   warp 1      allocates TMEM and issues tcgen05.mma (one thread):
+//               D[128 x 256, fp32, TMEM] += A[128 x 64, TMEM] * x^T, four
+//               K=16 instructions per group, tcgen05.commit releasing stages.
+//   warps 2-5   dequantize: thread i owns weight row i of the tile (TMEM lane
+//               i), turns the group's 64 codes into fp16 weights and writes
+//               them to a TMEM A stage with tcgen05.st; after the last group
+//               of a tile they read D back (tcgen05.ld) and store y.
+//
+// The weights the MMA consumes are exactly qw_dequantize's (fp16(fp16(s*q)
+// + b)): pairs (1024 + q_even, 1024 + 16 q_odd) come from one prmt and one
+// and, fma.rn.f16x2 with (s, s/16) and (-1024 s, -64 s) gives fp16(s*q)
+// rounded once from the exact product, and add.rn.f16x2 adds b.  Scales too
+// small for s/16 to be exact, or too large for 1024 s, take an exact
+// per-element path.  Accumulation is fp32 in the tensor cores.
+#include <cuda_fp16.h>
+
 #include "qw_internal.h"
+#include "qw_ptx.cuh"
 
 namespace qw {
 
-bool prefill_available() { return false; }
+namespace {
 
-cudaError_t launch_prefill(const PrefillArgs&, cudaStream_t, bool, std::string* err) {
-  *err = "prefill kernel not built";
-  return cudaErrorNotSupported;
+constexpr int kGroup = 64;
+constexpr int BM = 128;       // weight rows per tile (UMMA M, TMEM lanes)
+constexpr int BT = 256;       // tokens per tile (UMMA N)
+constexpr int STAGES = 4;     // pipeline depth (x box, packed W, TMEM A)
+constexpr int X_STAGE = BT * 128;          // 32 KB
+constexpr int WP_STAGE = BM * 32;          // 4 KB
+constexpr int OFF_X = 0;
+constexpr int OFF_WP = STAGES * X_STAGE;
+constexpr int OFF_BAR = OFF_WP + STAGES * WP_STAGE;
+// barriers: xfull, xempty(unused), wpfull, wpempty, afull, aempty, dfull, dempty
+constexpr int NBAR = 6 * STAGES + 2;
+constexpr int SMEM = OFF_BAR + NBAR * 8 + 64 + 1024;
+constexpr int THREADS = 6 * 32;
+constexpr uint32_t TMEM_COLS = 512;  // D: 256 columns, A stages: 4 x 32
+constexpr uint32_t D_COL = 0;
+constexpr uint32_t A_COL = 256;
+
+struct PrefillParams {
+  int M, N, K;
+  int n_tiles, m_tiles, groups;
+  int y_f32;
+  void* y;
+  const __half* scales;
+  const __half* biases;
+  unsigned int* status;
+};
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  // K-major, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes apart.
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: D fp32, A/B fp16, both K-major, M x N.
+constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// Exact per-element dequantization, for scales outside the fast path's range.
+__device__ __noinline__ void dequant_group_slow(const uint32_t (&wd)[8], __half s, __half b, uint32_t (&out)[32]) {
+#pragma unroll 1
+  for (int i = 0; i < 8; ++i) {
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      const uint32_t q0 = (wd[i] >> (8 * pp)) & 0xFu, q1 = (wd[i] >> (8 * pp + 4)) & 0xFu;
+      const __half t0 = __hmul_rn(s, __uint2half_rn(q0));
+      const __half t1 = __hmul_rn(s, __uint2half_rn(q1));
+      out[4 * i + pp] = h2_bits(__halves2half2(__hadd_rn(t0, b), __hadd_rn(t1, b)));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    qmm_prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                       const PrefillParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* xfull = bars;
+  uint64_t* wpfull = bars + STAGES;
+  uint64_t* wpempty = bars + 2 * STAGES;
+  uint64_t* afull = bars + 3 * STAGES;
+  uint64_t* aempty = bars + 4 * STAGES;  // arrived by tcgen05.commit: x slot and A stage are free
+  uint64_t* xempty = bars + 5 * STAGES;  // unused alias kept for layout clarity
+  uint64_t* dfull = bars + 6 * STAGES;
+  uint64_t* dempty = dfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  (void)xempty;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int total_tiles = p.n_tiles * p.m_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&wpfull[s], 1);
+      mbar_init(&wpempty[s], 4);
+      mbar_init(&afull[s], 4);
+      mbar_init(&aempty[s], 1);
+    }
+    mbar_init(dfull, 1);
+    mbar_init(dempty, 4);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&tm_x);
+      prefetch_tensormap(&tm_w);
+      pdl_wait();
+      const uint64_t pol_w = l2_policy_evict_last();
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+        const int nt = tile / p.m_tiles, mt = tile % p.m_tiles;
+        for (int g = 0; g < p.groups; ++g, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (it >= STAGES) {
+            // x slot s is free once the MMAs that read it completed; the
+            // packed-weight slot once the dequant warps read it.
+            if (!mbar_wait(&aempty[s], ph ^ 1, p.status, kDevTimeoutEmpty) ||
+                !mbar_wait(&wpempty[s], ph ^ 1, p.status, kDevTimeoutEmpty)) {
+              *abort_flag = 1;
+              break;
+            }
+          }
+          mbar_arrive_expect_tx(&xfull[s], X_STAGE);
+          tma_load_2d(smem + OFF_X + s * X_STAGE, &tm_x, &xfull[s], g * kGroup, mt * BT);
+          mbar_arrive_expect_tx(&wpfull[s], WP_STAGE);
+          tma_load_2d_hint(smem + OFF_WP + s * WP_STAGE, &tm_w, &wpfull[s], g * 32, nt * BM, pol_w);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    constexpr uint32_t idesc = idesc_f16(BM, BT);
+    uint32_t it = 0, tile_count = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tile_count) {
+      // the epilogue has drained D from the previous tile
+      if (tile_count > 0 && !*abort_flag &&
+          !mbar_wait(dempty, (tile_count - 1) & 1, p.status, kDevTimeoutAccum))
+        *abort_flag = 1;
+      tc_fence_after();
+      for (int g = 0; g < p.groups; ++g, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!*abort_flag) {
+          if (!mbar_wait(&xfull[s], ph, p.status, kDevTimeoutFull) ||
+              !mbar_wait(&afull[s], ph, p.status, kDevTimeoutFull))
+            *abort_flag = 1;
+        }
+        tc_fence_after();
+        if (lane == 0 && !*abort_flag) {
+          const uint64_t bdesc = smem_desc_sw128(smem_u32(smem + OFF_X + s * X_STAGE));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            tc_mma_ts(tmem + D_COL, tmem + A_COL + s * 32 + kk * 8, bdesc + (uint64_t)(2 * kk), idesc,
+                      (g > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) tc_commit(&aempty[s]);  // frees x slot s and A stage s when these MMAs finish
+        __syncwarp();
+      }
+      if (lane == 0) tc_commit(dfull);
+      __syncwarp();
+    }
+  } else {
+    // ---------------------------------------------- dequant + epilogue
+    const int dw = warp - 2;                 // 0..3
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    (void)dw;
+    pdl_wait();
+    uint32_t it = 0, tile_count = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tile_count) {
+      const int nt = tile / p.m_tiles, mt = tile % p.m_tiles;
+      const int row = nt * BM + row_in_tile;
+      const bool row_ok = row < p.N;
+      const __half* srow = p.scales + (size_t)(row_ok ? row : 0) * p.groups;
+      const __half* brow = p.biases + (size_t)(row_ok ? row : 0) * p.groups;
+      __half s_next = row_ok ? srow[0] : __float2half(0.f);
+      __half b_next = row_ok ? brow[0] : __float2half(0.f);
+      for (int g = 0; g < p.groups; ++g, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        const __half sc = s_next, bi = b_next;
+        if (g + 1 < p.groups && row_ok) {  // prefetch the next group's scale/bias
+          s_next = srow[g + 1];
+          b_next = brow[g + 1];
+        }
+        if (!*abort_flag && !mbar_wait(&wpfull[s], ph, p.status, kDevTimeoutFull)) *abort_flag = 1;
+        uint32_t wd[8];
+        {
+          const uint4* src = reinterpret_cast<const uint4*>(smem + OFF_WP + s * WP_STAGE + row_in_tile * 32);
+          const uint4 a = src[0], b = src[1];
+          wd[0] = a.x; wd[1] = a.y; wd[2] = a.z; wd[3] = a.w;
+          wd[4] = b.x; wd[5] = b.y; wd[6] = b.z; wd[7] = b.w;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wpempty[s]);
+        // dequantize 64 codes into 32 fp16 pairs (k ascending)
+        uint32_t out[32];
+        const float sf = __half2float(sc);
+        const bool fast = fabsf(sf) >= 0.0009765625f && fabsf(sf) < 63.0f;  // s/16 exact, 1024 s finite
+        if (fast) {
+          const __half s16 = __float2half_rn(sf * 0.0625f);  // exact: s >= 2^-10
+          const uint32_t s2 = h2_bits(__halves2half2(sc, s16));
+          const uint32_t c2 = h2_bits(__halves2half2(__float2half_rn(-1024.f * sf), __float2half_rn(-64.f * sf)));
+          const uint32_t b2 = h2_bits(__halves2half2(bi, bi));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+#pragma unroll
+            for (int pp = 0; pp < 4; ++pp) {
+              const uint32_t t = prmt(wd[i], 0x64646464u, 0x4040u + 0x0101u * pp) & 0xFFF0FF0Fu;
+              out[4 * i + pp] = hadd2_rn(hfma2_rn(t, s2, c2), b2);
+            }
+          }
+        } else {
+          dequant_group_slow(wd, sc, bi, out);
+        }
+        // write A stage s once the MMAs that read it last have completed
+        if (it >= STAGES && !*abort_flag && !mbar_wait(&aempty[s], ph ^ 1, p.status, kDevTimeoutEmpty))
+          *abort_flag = 1;
+        tc_fence_after();
+        tmem_st_x32(tmem + lane_base + A_COL + s * 32, out);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[s]);
+      }
+      // ---------------------------------------------------------- epilogue
+      if (!*abort_flag && !mbar_wait(dfull, tile_count & 1, p.status, kDevTimeoutAccum)) *abort_flag = 1;
+      tc_fence_after();
+#pragma unroll 1
+      for (int cb = 0; cb < BT / 16; ++cb) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(tmem + lane_base + D_COL + cb * 16, v);
+        tmem_wait_ld();
+        if (!row_ok || *abort_flag) continue;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int tok = mt * BT + cb * 16 + q;
+          if (tok < p.M) {
+            const size_t idx = (size_t)tok * p.N + row;
+            const float f = __uint_as_float(v[q]);
+            if (p.y_f32) reinterpret_cast<float*>(p.y)[idx] = f;
+            else reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(f);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dempty);
+    }
+  }
+
+  // everyone: make sure all tcgen05 work is finished before freeing TMEM
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+bool prefill_available() { return true; }
+
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const DeviceInfo& di = device_info(dev);
+  static thread_local int configured_dev = -1;
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(qmm_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  PrefillParams p{};
+  p.M = (int)a.M;
+  p.N = (int)a.N;
+  p.K = (int)a.K;
+  p.groups = (int)(a.K / kGroup);
+  p.n_tiles = (int)((a.N + BM - 1) / BM);
+  p.m_tiles = (int)((a.M + BT - 1) / BT);
+  p.y_f32 = a.y_f32 ? 1 : 0;
+  p.y = a.y;
+  p.scales = reinterpret_cast<const __half*>(a.scales);
+  p.biases = reinterpret_cast<const __half*>(a.biases);
+  p.status = a.status;
+  CUtensorMap tx, tw;
+  if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2,
+                      kGroup, BT, CU_TENSOR_MAP_SWIZZLE_128B, err))
+    return cudaErrorInvalidValue;
+  if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
+                      (uint64_t)(a.K / 2), 32, BM, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+    return cudaErrorInvalidValue;
+  const int tiles = p.n_tiles * p.m_tiles;
+  int grid = di.sm_count < tiles ? di.sm_count : tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, qmm_prefill_kernel, tx, tw, p);
 }
 
 }  // namespace qw
