@@ -307,19 +307,25 @@ def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50):
     return us, nbytes / (us * 1e-6) / 1e9
 
 
-def cpu_sample_rate(ws_host, threads):
-    """Oracle over one layer's host copy of the GPU's quantized weights: GB/s."""
+def cpu_stack_rate(ws, lm, threads, passes=2):
+    """The oracle (C, OpenMP, `threads` threads) over the whole stack's
+    quantized weights copied to the host (the same bytes the GPU streams), M=1.
+    Returns (GB/s, seconds of CPU work)."""
     import oracle
-    M = 1
+
+    def host(w):
+        return (w[0].cpu().numpy().view(np.uint32), w[1].cpu().numpy(), w[2].cpu().numpy())
+
+    mats = [host(l[n]) for l in ws for n in l] + [host(lm)]
     t_total, b_total = 0.0, 0
-    for name, (wq, s, b) in ws_host.items():
-        N, K = wq.shape[0], wq.shape[1] * 8
-        x = synth.activations(M, K, seed=1)
-        oracle.quantized_matmul(x, wq[:64], s[:64], b[:64], nthreads=threads)  # warm
-        t0 = time.perf_counter()
-        oracle.quantized_matmul(x, wq, s, b, nthreads=threads)
-        t_total += time.perf_counter() - t0
-        b_total += synth.algorithmic_bytes(M, N, K)
+    for _ in range(passes):
+        for wq, s, b in mats:
+            N, K = wq.shape[0], wq.shape[1] * 8
+            x = synth.activations(1, K, seed=1)
+            t0 = time.perf_counter()
+            oracle.quantized_matmul(x, wq, s, b, nthreads=threads)
+            t_total += time.perf_counter() - t0
+            b_total += synth.algorithmic_bytes(1, N, K)
     return b_total / t_total / 1e9, t_total
 
 
@@ -356,13 +362,26 @@ def run_ours(args):
 
     extra = {}
     if not args.skip_extra:
-        runner16 = StackRunner(torch, qw, ws, lm, 16, P, group)
-        ms16, _ = timed_graph(torch, runner16, max(10, args.steps // 4), args.warmup, stream, dist_on, local)
-        b16 = synth.stack_bytes(16, layers=args.layers) // P
-        extra["stack_m16"] = {"tok_s": round(16 * 1000.0 / ms16, 1), "ms_per_step": round(ms16, 4),
-                              "GBps_per_gpu": round(b16 / (ms16 * 1e-3) / 1e9, 1),
-                              "frac_hbm": round(b16 / (ms16 * 1e-3) / 1e9 / hbm_peak, 4)}
-        del runner16
+        # verify-batch stacks (MTP M=4, DFlash2 block M=16): HBM-bound like M=1
+        for Mv in (4, 16):
+            rv = StackRunner(torch, qw, ws, lm, Mv, P, group)
+            msv, _ = timed_graph(torch, rv, max(10, args.steps // 4), args.warmup, stream, dist_on, local)
+            bv = synth.stack_bytes(Mv, layers=args.layers) // P
+            extra[f"stack_m{Mv}"] = {"tok_s": round(Mv * 1000.0 / msv, 1), "ms_per_step": round(msv, 4),
+                                     "GBps_per_gpu": round(bv / (msv * 1e-3) / 1e9, 1),
+                                     "frac_hbm": round(bv / (msv * 1e-3) / 1e9 / hbm_peak, 4),
+                                     "weight_reuse_vs_m1": Mv}
+            del rv
+        # prefill chunk (M=2048) through the same stack: tensor-bound (tcgen05)
+        rp = StackRunner(torch, qw, ws, lm, 2048, P, group)
+        msp, _ = timed_graph(torch, rp, 3, 3, stream, dist_on, local)
+        fl = synth.stack_flops(2048, layers=args.layers) / P
+        extra["stack_prefill_m2048"] = {"tok_s": round(2048 * 1000.0 / msp, 1), "ms_per_step": round(msp, 3),
+                                        "TFLOPs_per_gpu": round(fl / (msp * 1e-3) / 1e12, 1),
+                                        "frac_tensor_bf16_burst": round(fl / (msp * 1e-3) / 1e12 / tf_peak, 4),
+                                        "frac_2250TF_nominal": round(fl / (msp * 1e-3) / 1e12 / 2250.0, 4)}
+        del rp
+        torch.cuda.empty_cache()
         if rank == 0 and P == 1:
             for M in (1, 4, 16):
                 us, gbs = kernel_microbench(torch, qw, M, 17408, 5120, dev)
@@ -405,15 +424,13 @@ def run_ours(args):
                           "traffic": traffic}
 
     if rank == 0 and world == 1 and not args.skip_cpu:
-        ws_host = {n: tuple(t.cpu().numpy().view(np.uint32) if i == 0 else t.cpu().numpy()
-                            for i, t in enumerate(ws[0][n])) for n in ws[0]}
         threads = os.cpu_count() or 1
-        gbs, secs = cpu_sample_rate(ws_host, threads)
+        gbs, secs = cpu_stack_rate(ws, lm, threads)
         result["cpu_baseline"] = {
             "value": round(gbs * 1e9 / synth.stack_bytes(1, args.layers), 4), "unit": "tok/s", "cores": threads,
             "kind": "port", "GBps": round(gbs, 3),
-            "sample": f"one decoder layer (4 matmuls, M=1, {secs:.2f} s) through the C oracle with OpenMP; "
-                      f"tok/s = GB/s / {synth.stack_bytes(1, args.layers)} bytes per token"}
+            "sample": f"the whole {args.layers}-layer stack + lm_head at M=1, twice, through the C oracle with OpenMP "
+                      f"({secs:.1f} s of CPU work) on the GPU's quantized weights copied to the host"}
     if dist_on:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

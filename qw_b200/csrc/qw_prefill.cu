@@ -10,10 +10,11 @@
 //   warp 1      allocates TMEM and issues tcgen05.mma (one thread):
 //               D[128 x 256, fp32, TMEM] += A[128 x 64, TMEM] * x^T, four
 //               K=16 instructions per group, tcgen05.commit releasing stages.
-//   warps 2-5   dequantize: thread i owns weight row i of the tile (TMEM lane
-//               i), turns the group's 64 codes into fp16 weights and writes
-//               them to a TMEM A stage with tcgen05.st; after the last group
-//               of a tile they read D back (tcgen05.ld) and store y.
+//   warps 2-9   dequantize: the two warps of a TMEM lane quarter own its 32
+//               weight rows (one row per lane) and split each group's 64
+//               codes in halves; they write fp16 weights to a TMEM A stage
+//               with tcgen05.st.  After the last group of a tile they read D
+//               back (tcgen05.ld, half of the tokens each) and store y.
 //
 // The weights the MMA consumes are exactly qw_dequantize's (fp16(fp16(s*q)
 // + b)): pairs (1024 + q_even, 1024 + 16 q_odd) come from one prmt and one
@@ -39,10 +40,11 @@ constexpr int WP_STAGE = BM * 32;          // 4 KB
 constexpr int OFF_X = 0;
 constexpr int OFF_WP = STAGES * X_STAGE;
 constexpr int OFF_BAR = OFF_WP + STAGES * WP_STAGE;
-// barriers: xfull, xempty(unused), wpfull, wpempty, afull, aempty, dfull, dempty
-constexpr int NBAR = 6 * STAGES + 2;
+// barriers: xfull, wpfull, wpempty, afull, aempty (per stage), dfull, dempty
+constexpr int NBAR = 5 * STAGES + 2;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 64 + 1024;
-constexpr int THREADS = 6 * 32;
+constexpr int DQW = 8;             // dequant / epilogue warps: 2 per TMEM lane quarter
+constexpr int THREADS = (2 + DQW) * 32;
 constexpr uint32_t TMEM_COLS = 512;  // D: 256 columns, A stages: 4 x 32
 constexpr uint32_t D_COL = 0;
 constexpr uint32_t A_COL = 256;
@@ -68,23 +70,21 @@ constexpr uint32_t idesc_f16(int m, int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&v)[32]) {
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 // Exact per-element dequantization, for scales outside the fast path's range.
-__device__ __noinline__ void dequant_group_slow(const uint32_t (&wd)[8], __half s, __half b, uint32_t (&out)[32]) {
+__device__ __noinline__ void dequant_group_slow(const uint32_t (&wd)[4], __half s, __half b, uint32_t (&out)[16]) {
 #pragma unroll 1
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
 #pragma unroll
     for (int pp = 0; pp < 4; ++pp) {
       const uint32_t q0 = (wd[i] >> (8 * pp)) & 0xFu, q1 = (wd[i] >> (8 * pp + 4)) & 0xFu;
@@ -106,12 +106,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* wpempty = bars + 2 * STAGES;
   uint64_t* afull = bars + 3 * STAGES;
   uint64_t* aempty = bars + 4 * STAGES;  // arrived by tcgen05.commit: x slot and A stage are free
-  uint64_t* xempty = bars + 5 * STAGES;  // unused alias kept for layout clarity
-  uint64_t* dfull = bars + 6 * STAGES;
+  uint64_t* dfull = bars + 5 * STAGES;
   uint64_t* dempty = dfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  (void)xempty;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -121,12 +119,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&xfull[s], 1);
       mbar_init(&wpfull[s], 1);
-      mbar_init(&wpempty[s], 4);
-      mbar_init(&afull[s], 4);
+      mbar_init(&wpempty[s], DQW);
+      mbar_init(&afull[s], DQW);
       mbar_init(&aempty[s], 1);
     }
     mbar_init(dfull, 1);
-    mbar_init(dempty, 4);
+    mbar_init(dempty, DQW);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -205,11 +203,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---------------------------------------------- dequant + epilogue
-    const int dw = warp - 2;                 // 0..3
+    const int dw = warp - 2;                 // 0..7
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int khalf = dw >> 2;               // which 32 codes of each group / which 128 tokens
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    (void)dw;
     pdl_wait();
     uint32_t it = 0, tile_count = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tile_count) {
@@ -229,17 +227,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           b_next = brow[g + 1];
         }
         if (!*abort_flag && !mbar_wait(&wpfull[s], ph, p.status, kDevTimeoutFull)) *abort_flag = 1;
-        uint32_t wd[8];
+        uint32_t wd[4];
         {
-          const uint4* src = reinterpret_cast<const uint4*>(smem + OFF_WP + s * WP_STAGE + row_in_tile * 32);
-          const uint4 a = src[0], b = src[1];
+          const uint4 a = reinterpret_cast<const uint4*>(smem + OFF_WP + s * WP_STAGE + row_in_tile * 32)[khalf];
           wd[0] = a.x; wd[1] = a.y; wd[2] = a.z; wd[3] = a.w;
-          wd[4] = b.x; wd[5] = b.y; wd[6] = b.z; wd[7] = b.w;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&wpempty[s]);
-        // dequantize 64 codes into 32 fp16 pairs (k ascending)
-        uint32_t out[32];
+        // dequantize this half's 32 codes into 16 fp16 pairs (k ascending)
+        uint32_t out[16];
         const float sf = __half2float(sc);
         const bool fast = fabsf(sf) >= 0.0009765625f && fabsf(sf) < 63.0f;  // s/16 exact, 1024 s finite
         if (fast) {
@@ -248,7 +244,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t c2 = h2_bits(__halves2half2(__float2half_rn(-1024.f * sf), __float2half_rn(-64.f * sf)));
           const uint32_t b2 = h2_bits(__halves2half2(bi, bi));
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < 4; ++i) {
 #pragma unroll
             for (int pp = 0; pp < 4; ++pp) {
               const uint32_t t = prmt(wd[i], 0x64646464u, 0x4040u + 0x0101u * pp) & 0xFFF0FF0Fu;
@@ -262,7 +258,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (it >= STAGES && !*abort_flag && !mbar_wait(&aempty[s], ph ^ 1, p.status, kDevTimeoutEmpty))
           *abort_flag = 1;
         tc_fence_after();
-        tmem_st_x32(tmem + lane_base + A_COL + s * 32, out);
+        tmem_st_x16(tmem + lane_base + A_COL + s * 32 + khalf * 16, out);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -272,7 +268,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!*abort_flag && !mbar_wait(dfull, tile_count & 1, p.status, kDevTimeoutAccum)) *abort_flag = 1;
       tc_fence_after();
 #pragma unroll 1
-      for (int cb = 0; cb < BT / 16; ++cb) {
+      for (int cb = khalf * (BT / 32); cb < (khalf + 1) * (BT / 32); ++cb) {
         uint32_t v[16];
         tmem_ld_32x32b_x16(tmem + lane_base + D_COL + cb * 16, v);
         tmem_wait_ld();

@@ -4,31 +4,56 @@ The reference has no tensor parallelism (it is a single-device server); this
 is the partition BASELINE asks for, Megatron style:
 
 * column-parallel (no collective): q, k, v, gate, up and lm_head.  Each rank
-  holds rows [r*N/P, (r+1)*N/P) of every fused plane (q|k|v and gate|up are
-  sharded plane by plane, then re-fused per rank, so every rank holds N/P rows
-  of each plane), with their scales and biases;
+  holds rows [r*N/P, (r+1)*N/P) of every plane of a fused matrix (q|k|v and
+  gate|up are sharded plane by plane, then re-fused per rank), with their
+  scales and biases;
 * row-parallel (fp32 allreduce): o and down.  Each rank holds input columns
   [r*K/P, (r+1)*K/P) of the packed weight, on group boundaries so that every
   quantization group (and its scale/bias) lies wholly in one shard; the rank's
   matmul returns fp32 partial sums that an allreduce adds before the single
   fp16 rounding.
 
-Everything here is array slicing and works on numpy arrays or torch tensors.
+Everything here is slicing and works on numpy arrays or torch tensors.
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
 from typing import Callable, Dict, List, Sequence, Tuple
 
 from . import synth
 
 GROUP = synth.GROUP
-WORDS_PER_GROUP = GROUP * synth.BITS // 32
 
-# plane boundaries of the fused matrices (output features)
-PLANES = {
-    "qkv": (synth.Q_OUT, synth.KV_OUT, synth.KV_OUT),
-    "gate_up": (synth.INTER, synth.INTER),
-}
+
+@dataclass(frozen=True)
+class StackDims:
+    """Widths of one decoder layer's linears (defaults: the BASELINE 27B stack)."""
+    hidden: int = synth.HIDDEN
+    q_out: int = synth.Q_OUT
+    kv_out: int = synth.KV_OUT
+    inter: int = synth.INTER
+    vocab: int = synth.VOCAB
+
+    def linears(self) -> List[synth.Linear]:
+        return [
+            synth.Linear("qkv", self.q_out + 2 * self.kv_out, self.hidden, 0, False),
+            synth.Linear("o", self.hidden, self.q_out, 1, True),
+            synth.Linear("gate_up", 2 * self.inter, self.hidden, 2, False),
+            synth.Linear("down", self.hidden, self.inter, 3, True),
+        ]
+
+    def lm_head(self) -> synth.Linear:
+        return synth.Linear("lm_head", self.vocab, self.hidden, 9, False)
+
+    def planes(self, name: str, N: int) -> Tuple[int, ...]:
+        if name == "qkv":
+            return (self.q_out, self.kv_out, self.kv_out)
+        if name == "gate_up":
+            return (self.inter, self.inter)
+        return (N,)
+
+
+BASELINE = StackDims()
 
 
 def split_even(n: int, parts: int, rank: int, align: int = 1) -> Tuple[int, int]:
@@ -42,10 +67,10 @@ def split_even(n: int, parts: int, rank: int, align: int = 1) -> Tuple[int, int]
     return rank * per * align, (rank + 1) * per * align
 
 
-def column_shard_rows(name: str, N: int, P: int, rank: int) -> List[Tuple[int, int]]:
+def column_shard_rows(lin: synth.Linear, P: int, rank: int, dims: StackDims = BASELINE) -> List[Tuple[int, int]]:
     """Row ranges of the full matrix that rank r holds, plane by plane."""
-    planes = PLANES.get(name, (N,))
-    assert sum(planes) == N
+    planes = dims.planes(lin.name, lin.N)
+    assert sum(planes) == lin.N
     out, base = [], 0
     for n in planes:
         a, b = split_even(n, P, rank)
@@ -67,7 +92,7 @@ def _cat(parts):
     return np.ascontiguousarray(np.concatenate(parts, 0))
 
 
-def shard_linear(lin: synth.Linear, wq, scales, biases, P: int, rank: int):
+def shard_linear(lin: synth.Linear, wq, scales, biases, P: int, rank: int, dims: StackDims = BASELINE):
     """The rank's (wq, scales, biases) of a full quantized matrix."""
     if P == 1:
         return wq, scales, biases
@@ -76,7 +101,7 @@ def shard_linear(lin: synth.Linear, wq, scales, biases, P: int, rank: int):
         w0, w1 = k0 * synth.BITS // 32, k1 * synth.BITS // 32
         g0, g1 = k0 // GROUP, k1 // GROUP
         return (_cat([wq[:, w0:w1]]), _cat([scales[:, g0:g1]]), _cat([biases[:, g0:g1]]))
-    rows = column_shard_rows(lin.name, lin.N, P, rank)
+    rows = column_shard_rows(lin, P, rank, dims)
     return (_cat([wq[a:b] for a, b in rows]), _cat([scales[a:b] for a, b in rows]),
             _cat([biases[a:b] for a, b in rows]))
 
@@ -88,45 +113,38 @@ def shard_shape(lin: synth.Linear, P: int) -> Tuple[int, int]:
     return lin.N // P, lin.K
 
 
-def local_input_cols(lin: synth.Linear, P: int, rank: int) -> Tuple[int, int]:
-    """Columns of the full activation a row-parallel op consumes on this rank."""
-    return row_shard_cols(lin.K, P, rank) if lin.row_parallel else (0, lin.K)
-
-
 class LinearStack:
     """The decode linear stack on one rank: per layer qkv -> o -> gate_up ->
     down, then lm_head.  The stack keeps the data dependencies of a decoder
-    layer without its non-linear parts (attention, norms, SwiGLU are outside
-    this path): o consumes the q plane of the rank's qkv output, down consumes
-    the gate plane of its gate_up output, and each layer's down output is the
-    next layer's input.
+    layer without its non-linear parts (attention, norms and SwiGLU are outside
+    this path): o consumes the rank's q plane of its qkv output, down consumes
+    the rank's gate plane of its gate_up output, and each layer's down output
+    is the next layer's input.
 
     `matmul(x, (wq, s, b), out_f32)` runs one quantized matmul; `allreduce(t)`
-    sums an fp32 tensor over ranks in place; `to_half(t)` rounds fp32 to fp16.
+    sums an fp32 array over ranks and returns it; `to_half(t)` rounds fp32 to
+    fp16.  Row-parallel shards need every rank to run the same sequence of
+    collectives, which this fixed order guarantees.
     """
 
     def __init__(self, layers: Sequence[Dict[str, tuple]], lm_head: tuple, P: int, rank: int,
-                 matmul: Callable, allreduce: Callable, to_half: Callable):
+                 matmul: Callable, allreduce: Callable, to_half: Callable, dims: StackDims = BASELINE):
         self.layers, self.lm_head = layers, lm_head
-        self.P, self.rank = P, rank
+        self.P, self.rank, self.dims = P, rank, dims
         self.matmul, self.allreduce, self.to_half = matmul, allreduce, to_half
-        self.lin = {l.name: l for l in synth.layer_linears()}
+
+    def _rowpar(self, x, w):
+        if self.P == 1:
+            return self.matmul(x, w, False)
+        return self.to_half(self.allreduce(self.matmul(x, w, True)))
 
     def layer(self, h, w):
-        P = self.P
-        q_local = synth.Q_OUT // P
-        inter_local = synth.INTER // P
+        q_local = self.dims.q_out // self.P
+        inter_local = self.dims.inter // self.P
         qkv = self.matmul(h, w["qkv"], False)
-        attn = qkv[..., :q_local]
-        if P == 1:
-            o = self.matmul(_contig(attn), w["o"], False)
-        else:
-            o = self.to_half(self.allreduce(self.matmul(_contig(attn), w["o"], True)))
+        o = self._rowpar(_contig(qkv[..., :q_local]), w["o"])
         gu = self.matmul(o, w["gate_up"], False)
-        g = gu[..., :inter_local]
-        if P == 1:
-            return self.matmul(_contig(g), w["down"], False)
-        return self.to_half(self.allreduce(self.matmul(_contig(g), w["down"], True)))
+        return self._rowpar(_contig(gu[..., :inter_local]), w["down"])
 
     def forward(self, h):
         for w in self.layers:
@@ -139,3 +157,17 @@ def _contig(t):
         return t if t.is_contiguous() else t.contiguous()
     import numpy as np
     return np.ascontiguousarray(t)
+
+
+def gather_columns(shards: Sequence, lin: synth.Linear, dims: StackDims = BASELINE):
+    """Reassemble a column-parallel output [.., N] from every rank's [.., N/P]
+    (plane by plane), e.g. the full logits from the vocab shards."""
+    import numpy as np
+    P = len(shards)
+    planes = dims.planes(lin.name, lin.N)
+    out, base_local = [], 0
+    for n in planes:
+        per = n // P
+        out.extend(np.asarray(s)[..., base_local:base_local + per] for s in shards)
+        base_local += per
+    return np.concatenate(out, axis=-1)

@@ -1,0 +1,135 @@
+"""Tensor-parallel linear stack on P GPUs (NCCL fp32 allreduce for o/down).
+
+Checked two ways: against the same stack unsharded on one GPU (isolates the
+sharding and the allreduce: only fp32 summation order differs), and against
+the unsharded CPU oracle.  The oracle bound is per-op TOL scaled for the
+chain: 13 quantized matmuls feed each other through fp16 activations, and the
+prefill path (M >= 17) multiplies fp16-rounded dequantized weights, so the
+per-op differences accumulate along the chain.
+Needs at least 2 GPUs (skipped otherwise); one process per GPU, NVLS off,
+short process-group timeout."""
+import os
+import socket
+import time
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from qw_b200 import synth, tp
+from tests.conftest import TOL, rel_err
+
+pytestmark = pytest.mark.gpu
+
+DIMS = tp.StackDims(hidden=1024, q_out=1536, kv_out=256, inter=2048, vocab=4096)
+LAYERS = 3
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _weights():
+    layers = []
+    for l in range(LAYERS):
+        layers.append({lin.name: oracle.quantize(synth.weight_fp16(lin.N, lin.K, seed=3, layer=l, tid=lin.tid))
+                       for lin in DIMS.linears()})
+    lm = DIMS.lm_head()
+    return layers, oracle.quantize(synth.weight_fp16(lm.N, lm.K, seed=3, layer=99, tid=lm.tid))
+
+
+def _rank_main(rank, world, port, x, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    import torch.distributed as dist
+    import qw_b200
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        layers, lm_w = _weights()
+        lins = {l.name: l for l in DIMS.linears()}
+
+        def to_dev(w):
+            wq, s, b = w
+            return (torch.from_numpy(np.ascontiguousarray(wq).view(np.int32)).to(dev),
+                    torch.from_numpy(np.ascontiguousarray(s)).to(dev), torch.from_numpy(np.ascontiguousarray(b)).to(dev))
+
+        mine = [{n: to_dev(tp.shard_linear(lins[n], *w, world, rank, DIMS)) for n, w in d.items()} for d in layers]
+        lm_mine = to_dev(tp.shard_linear(DIMS.lm_head(), *lm_w, world, rank, DIMS))
+
+        def mm(xx, w, out_f32):
+            return qw_b200.quantized_matmul(xx, *w, out_dtype=torch.float32 if out_f32 else torch.float16)
+
+        def allreduce(t):
+            dist.all_reduce(t)
+            return t
+
+        stack = tp.LinearStack(mine, lm_mine, world, rank, mm, allreduce, lambda t: t.half(), DIMS)
+        for M in (1, 16, 64):
+            y = stack.forward(torch.from_numpy(x[:M]).to(dev))
+            torch.cuda.synchronize()
+            out_q.put((rank, M, "ok", y.cpu().numpy()))
+    except Exception as e:  # noqa: BLE001
+        out_q.put((rank, -1, "error", repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_stack_matches_oracle(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    x = synth.activations(64, DIMS.hidden, seed=9)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, x, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    deadline = time.time() + 300
+    while len(got) < 3 * world and time.time() < deadline:
+        try:
+            r, M, status, payload = q.get(timeout=10)
+        except Exception:
+            continue
+        assert status == "ok", payload
+        got[(r, M)] = payload
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert len(got) == 3 * world
+    layers, lm_w = _weights()
+
+    def omm(xx, w, out_f32):
+        y, y32 = oracle.quantized_matmul(xx, *w, want_f32=True)
+        return y32 if out_f32 else y
+
+    import qw_b200
+    dev = torch.device("cuda", 0)
+
+    def to_dev(w):
+        wq, s_, b_ = w
+        return (torch.from_numpy(np.ascontiguousarray(wq).view(np.int32)).to(dev),
+                torch.from_numpy(np.ascontiguousarray(s_)).to(dev), torch.from_numpy(np.ascontiguousarray(b_)).to(dev))
+
+    def gmm(xx, w, out_f32):
+        return qw_b200.quantized_matmul(xx, *w, out_dtype=torch.float32 if out_f32 else torch.float16)
+
+    one_gpu = tp.LinearStack([{n: to_dev(w) for n, w in d.items()} for d in layers], to_dev(lm_w), 1, 0, gmm,
+                             None, None, DIMS)
+    ref_stack = tp.LinearStack(layers, lm_w, 1, 0, omm, None, None, DIMS)
+    n_ops = 4 * LAYERS + 1
+    for M in (1, 16, 64):
+        full = tp.gather_columns([got[(r, M)] for r in range(world)], DIMS.lm_head(), DIMS).astype(np.float32)
+        single = one_gpu.forward(torch.from_numpy(x[:M]).to(dev)).float().cpu().numpy()
+        assert rel_err(full, single) <= TOL, (world, M)  # fp16 rounding flips from the partial-sum order
+        ref = ref_stack.forward(x[:M]).astype(np.float32)
+        assert rel_err(full, ref) <= TOL * np.sqrt(n_ops), (world, M)

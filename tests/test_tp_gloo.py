@@ -1,0 +1,154 @@
+"""Tensor-parallel stack logic on CPU: two gloo ranks, each running its shard
+of a (down-scaled) linear stack through the oracle, against the unsharded
+stack.  Also a host-side failure case: a rank that dies before the collective
+must not leave its peer hanging.  No GPU."""
+import os
+import socket
+import time
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from qw_b200 import synth, tp
+from tests.conftest import rel_err
+
+DIMS = tp.StackDims(hidden=256, q_out=384, kv_out=64, inter=512, vocab=1000)
+LAYERS = 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _weights():
+    layers = []
+    for l in range(LAYERS):
+        d = {}
+        for lin in DIMS.linears():
+            w = synth.weight_fp16(lin.N, lin.K, seed=7, layer=l, tid=lin.tid)
+            d[lin.name] = oracle.quantize(w)
+        layers.append(d)
+    lm = DIMS.lm_head()
+    lm_w = oracle.quantize(synth.weight_fp16(lm.N, lm.K, seed=7, layer=99, tid=lm.tid))
+    return layers, lm_w
+
+
+def _oracle_mm(x, w, out_f32):
+    y, y32 = oracle.quantized_matmul(x, *w, want_f32=True)
+    return y32 if out_f32 else y
+
+
+def _reference_logits(x):
+    layers, lm_w = _weights()
+    stack = tp.LinearStack(layers, lm_w, 1, 0, _oracle_mm, None, None, DIMS)
+    return stack.forward(x)
+
+
+def _rank_main(rank, world, port, x, out_q, fail_rank):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        layers, lm_w = _weights()
+        lins = {l.name: l for l in DIMS.linears()}
+        mine = [{n: tp.shard_linear(lins[n], *w, world, rank, DIMS) for n, w in d.items()} for d in layers]
+        lm_mine = tp.shard_linear(DIMS.lm_head(), *lm_w, world, rank, DIMS)
+
+        def allreduce(a):
+            if rank == fail_rank:
+                raise RuntimeError("injected rank failure")
+            t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32))
+            dist.all_reduce(t)
+            return t.numpy()
+
+        stack = tp.LinearStack(mine, lm_mine, world, rank, _oracle_mm, allreduce,
+                               lambda a: a.astype(np.float16), DIMS)
+        t0 = time.time()
+        out_q.put((rank, "ok", stack.forward(x), time.time() - t0))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        out_q.put((rank, "error", repr(e), 0.0))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run(world, fail_rank=-1):
+    x = synth.activations(3, DIMS.hidden, seed=5)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, x, q, fail_rank)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    deadline = time.time() + 120
+    while len(results) < world and time.time() < deadline:
+        try:
+            r, status, payload, dt = q.get(timeout=5)
+            results[r] = (status, payload)
+        except Exception:
+            pass
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return x, results
+
+
+def test_column_and_row_shards_reassemble():
+    lins = DIMS.linears()
+    for lin in lins:
+        w = synth.weight_fp16(lin.N, lin.K, seed=1)
+        wq, s, b = oracle.quantize(w)
+        shards = [tp.shard_linear(lin, wq, s, b, 2, r, DIMS) for r in range(2)]
+        for sh in shards:
+            assert sh[0].shape == (tp.shard_shape(lin, 2)[0], tp.shard_shape(lin, 2)[1] // 8)
+        x = synth.activations(2, lin.K, seed=2)
+        if lin.row_parallel:
+            k0, k1 = tp.row_shard_cols(lin.K, 2, 0)
+            parts = [oracle.quantized_matmul(x[:, slice(*tp.row_shard_cols(lin.K, 2, r))], *shards[r], want_f32=True)[1]
+                     for r in range(2)]
+            full = oracle.quantized_matmul(x, wq, s, b, want_f32=True)[1]
+            assert rel_err(parts[0] + parts[1], full) < 1e-5
+        else:
+            outs = [oracle.quantized_matmul(x, *shards[r]) for r in range(2)]
+            full = oracle.quantized_matmul(x, wq, s, b)
+            np.testing.assert_array_equal(tp.gather_columns(outs, lin, DIMS).view(np.uint16), full.view(np.uint16))
+
+
+def test_row_shards_keep_groups_whole():
+    with pytest.raises(ValueError):
+        tp.row_shard_cols(64 * 3, 2, 0)  # 3 groups do not split over 2 ranks
+    assert tp.row_shard_cols(17408, 8, 7) == (15232, 17408)
+
+
+def test_two_rank_stack_matches_unsharded():
+    x, results = _run(2)
+    assert set(results) == {0, 1}, results
+    ref = _reference_logits(x)
+    shards = []
+    for r in range(2):
+        status, payload = results[r]
+        assert status == "ok", payload
+        shards.append(payload)
+    full = tp.gather_columns(shards, DIMS.lm_head(), DIMS)
+    assert rel_err(full.astype(np.float32), ref.astype(np.float32)) <= 1e-2
+
+
+def test_failed_rank_does_not_hang_its_peer():
+    """Rank 1 raises before its first allreduce; rank 0's collective must end
+    with an error within the process-group timeout instead of waiting forever."""
+    t0 = time.time()
+    _, results = _run(2, fail_rank=1)
+    assert results.get(1, ("", ""))[0] == "error"
+    assert results.get(0, ("", ""))[0] == "error", results.get(0)
+    assert time.time() - t0 < 100
