@@ -65,7 +65,7 @@ template <int MT>
 struct SkinnyCfg {
   static constexpr int NT = (MT + 7) / 8;       // n8 MMA column tiles
   static constexpr int MPAD_ = 8 * NT;
-  static constexpr int CW = 16;                 // consumer warps: 8 row tiles x 2 halves of each unit's groups
+  static constexpr int CW = 8;                  // consumer warps: 16 rows x all 8 groups of a unit each
   static constexpr int HW = MT == 1 ? 1 : (MT <= 8 ? 2 : 3);  // helper warps
   static constexpr int BN = 128;                // rows per tile
   static constexpr int WST = MT == 1 ? 5 : (MT <= 8 ? 4 : 3);
@@ -86,8 +86,8 @@ struct SkinnyCfg {
   static constexpr int S_STAGE = align1k(OFF_XZ + XZ_BYTES);
   static constexpr int OFF_WRING = 0;
   static constexpr int OFF_SRING = WST * W_STAGE;
-  static constexpr int COMB_BYTES = 8 * 32 * 4 * NT * 4;  // k-half partner accumulators
   static constexpr int OFF_COMB = OFF_SRING + SST * S_STAGE;
+  static constexpr int COMB_BYTES = 0;
   // Cluster split-K: the leader CTA of a tile receives the other CTAs'
   // partials here (distributed shared memory).
   static constexpr int SPLIT_MAX = MT <= 8 ? 4 : 2;
@@ -97,6 +97,8 @@ struct SkinnyCfg {
   static constexpr int NBAR = 2 * WST + 3 * SST + 1;  // wfull, wempty | sfull, ready, sempty | recv
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static constexpr int THREADS = (2 + HW + CW) * 32;
+  // registers per thread: the whole register file over the CTA's warps
+  static constexpr int MAXREG = (65536 / THREADS) & ~7;
   static constexpr int MPAD = 8 * NT;
   static constexpr int PART = BN * MPAD;  // floats per partial slot
   static_assert(W_STAGE % 1024 == 0, "weight stages stay 1024-aligned");
@@ -138,16 +140,6 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
 __device__ __forceinline__ void sts_f32x2(uint32_t addr, float a, float b) {
   asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
 }
-__device__ __forceinline__ float4 lds_f32x4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
-}
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t w, uint32_t mask) {
   uint32_t r;
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "r"(mask), "r"(0x64006400u));
@@ -157,7 +149,7 @@ __device__ __forceinline__ float half_lo(uint32_t h2) { return __half2float(__us
 __device__ __forceinline__ float half_hi(uint32_t h2) { return __half2float(__ushort_as_half((uint16_t)(h2 >> 16))); }
 
 template <int MT>
-__global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
+__global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyCfg<MT>::MAXREG)
     qmm_skinny_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
                       const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_x,
                       const SkinnyParams p) {
@@ -178,7 +170,6 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
   uint64_t* recv_bar = sempty + SST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + Cfg::NBAR);
   volatile int* fin_flag = abort_flag + 1;  // [2]: tile+1 to finish per partial slot, 0 = none
-  const uint32_t comb = smem_u32(smem + Cfg::OFF_COMB);
   uint8_t* wring = smem + Cfg::OFF_WRING;
   uint8_t* sring = smem + Cfg::OFF_SRING;
 
@@ -373,9 +364,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
 
   // ----------------------------------------------------------------- consumers
   const int cw = warp - 2 - Cfg::HW;
-  const int rt = cw & 7;             // row tile of this warp
-  const int kh = cw >> 3;            // which half of each unit's 8 groups
-  const int wrow = rt * 16;          // first row of this warp inside the tile
+  const int wrow = cw * 16;          // first row of this warp inside the tile
   const int r = lane / 4, s4 = lane % 4;
   pdl_wait();
 
@@ -386,16 +375,16 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
     for (int e = 0; e < 4; ++e) acc[q][e] = 0.f;
 
   // ldmatrix lane addressing: matrix mi = lane/8 covers rows 8*(mi&1).. of
-  // chunk (mi>>1) of the group; per-lane offsets hoisted out of the loop.
+  // chunk (mi>>1) of the group; per-lane offsets (groups 0-3 of box 0; box 1
+  // adds W_BOX) hoisted out of the loop.
   const int lm_mi = lane / 8;
   const int lm_row = wrow + (lane % 8) + 8 * (lm_mi & 1);
   const int lm_sw = lm_row & 7;
   uint32_t lm_off[4];
 #pragma unroll
-  for (int g4 = 0; g4 < 4; ++g4)
-    lm_off[g4] = kh * Cfg::W_BOX + lm_row * 128 + (((g4 * 2 + (lm_mi >> 1)) ^ lm_sw) << 4);
-  // scale/bias rows r and r+8 of this warp, groups kh*4 .. kh*4+3 (8 bytes)
-  const uint32_t sb_off = (wrow + r) * 16 + kh * 8;
+  for (int g4 = 0; g4 < 4; ++g4) lm_off[g4] = lm_row * 128 + (((g4 * 2 + (lm_mi >> 1)) ^ lm_sw) << 4);
+  // scale/bias rows r and r+8 of this warp, all 8 groups (16 bytes each)
+  const uint32_t sb_off = (wrow + r) * 16;
   // B fragments: a lane whose token column is >= M reads token M-1's (a
   // shared-memory broadcast).  MMA output columns depend only on their own B
   // column, so those columns are never mixed into a written result.
@@ -403,11 +392,10 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
 #pragma unroll
   for (int tt = 0; tt < NT; ++tt) {
     const int tok = (tt * 8 + r) < p.M ? (tt * 8 + r) : (p.M - 1);
-    bf_off[tt] = Cfg::OFF_BF + ((kh * 4 * Cfg::BF_TOK + tok) * 4 + s4) * 32;
+    bf_off[tt] = Cfg::OFF_BF + (tok * 4 + s4) * 32;
   }
-  const uint32_t xz_off = Cfg::OFF_XZ + 2 * s4 * 8 + kh * 4 * Cfg::XZ_COLS * 8;
+  const uint32_t xz_off = Cfg::OFF_XZ + 2 * s4 * 8;
   const uint32_t wring_u = smem_u32(wring);
-  const uint32_t sring_u = smem_u32(sring);
 
   int t = first_tile, c = first_chunk, wslot = 0, sslot = 0;
   uint32_t wphase = 0, sphase = 0;
@@ -415,17 +403,18 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
   for (int j = 0; j < nunits; ++j) {
     // 1) copy this warp's share of the unit's weights, scales and biases into
     //    registers, then give the weight slot back to the producer.
-    uint32_t A[4][4];
-    uint2 sv_lo, sv_hi, bv_lo, bv_hi;
+    uint32_t A[8][4];
+    uint4 sv_lo, sv_hi, bv_lo, bv_hi;
     if (!*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
     {
       const uint32_t wb = wring_u + wslot * Cfg::W_STAGE;
 #pragma unroll
-      for (int g4 = 0; g4 < 4; ++g4) ldmatrix_x4(wb + lm_off[g4], A[g4][0], A[g4][1], A[g4][2], A[g4][3]);
-      sv_lo = lds64(wb + Cfg::OFF_WS + sb_off);
-      sv_hi = lds64(wb + Cfg::OFF_WS + sb_off + 8 * 16);
-      bv_lo = lds64(wb + Cfg::OFF_WB + sb_off);
-      bv_hi = lds64(wb + Cfg::OFF_WB + sb_off + 8 * 16);
+      for (int gi = 0; gi < 8; ++gi)
+        ldmatrix_x4(wb + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
+      sv_lo = lds128(wb + Cfg::OFF_WS + sb_off);
+      sv_hi = lds128(wb + Cfg::OFF_WS + sb_off + 8 * 16);
+      bv_lo = lds128(wb + Cfg::OFF_WB + sb_off);
+      bv_hi = lds128(wb + Cfg::OFF_WB + sb_off + 8 * 16);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&wempty[wslot]);
@@ -434,13 +423,14 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
     if (!*abort_flag && !mbar_wait(&ready[sslot], sphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
     if (!*abort_flag) {
       const uint8_t* stp = sring + sslot * Cfg::S_STAGE;
-      (void)sring_u;
+      const uint32_t svl[4] = {sv_lo.x, sv_lo.y, sv_lo.z, sv_lo.w}, svh[4] = {sv_hi.x, sv_hi.y, sv_hi.z, sv_hi.w};
+      const uint32_t bvl[4] = {bv_lo.x, bv_lo.y, bv_lo.z, bv_lo.w}, bvh[4] = {bv_hi.x, bv_hi.y, bv_hi.z, bv_hi.w};
 #pragma unroll
-      for (int g4 = 0; g4 < 4; ++g4) {
+      for (int gi = 0; gi < 8; ++gi) {
         uint4 b0[NT], b1[NT];
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
-          const uint4* fb = reinterpret_cast<const uint4*>(stp + bf_off[tt] + g4 * (Cfg::BF_TOK * 4 * 32));
+          const uint4* fb = reinterpret_cast<const uint4*>(stp + bf_off[tt] + gi * (Cfg::BF_TOK * 4 * 32));
           b0[tt] = fb[0];
           b1[tt] = fb[1];
         }
@@ -448,9 +438,9 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
         uint32_t e[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t w8 = A[g4][i] >> 8;
-          e[0][i] = lop3_and_or(A[g4][i], 0x000F000Fu);
-          e[1][i] = lop3_and_or(A[g4][i], 0x00F000F0u);
+          const uint32_t w8 = A[gi][i] >> 8;
+          e[0][i] = lop3_and_or(A[gi][i], 0x000F000Fu);
+          e[1][i] = lop3_and_or(A[gi][i], 0x00F000F0u);
           e[2][i] = lop3_and_or(w8, 0x000F000Fu);
           e[3][i] = lop3_and_or(w8, 0x00F000F0u);
         }
@@ -463,16 +453,14 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
           mma_16816(dB[tt], e[3][0], e[3][1], e[3][2], e[3][3], b1[tt].z, b1[tt].w);
         }
         // fold the group: y += s * (d - Z) + b * X
-        const uint32_t s_w_lo = (g4 < 2) ? sv_lo.x : sv_lo.y, s_w_hi = (g4 < 2) ? sv_hi.x : sv_hi.y;
-        const uint32_t b_w_lo = (g4 < 2) ? bv_lo.x : bv_lo.y, b_w_hi = (g4 < 2) ? bv_hi.x : bv_hi.y;
-        const float s_r = (g4 & 1) ? half_hi(s_w_lo) : half_lo(s_w_lo);
-        const float s_r8 = (g4 & 1) ? half_hi(s_w_hi) : half_lo(s_w_hi);
-        const float b_r = (g4 & 1) ? half_hi(b_w_lo) : half_lo(b_w_lo);
-        const float b_r8 = (g4 & 1) ? half_hi(b_w_hi) : half_lo(b_w_hi);
+        const float s_r = (gi & 1) ? half_hi(svl[gi / 2]) : half_lo(svl[gi / 2]);
+        const float s_r8 = (gi & 1) ? half_hi(svh[gi / 2]) : half_lo(svh[gi / 2]);
+        const float b_r = (gi & 1) ? half_hi(bvl[gi / 2]) : half_lo(bvl[gi / 2]);
+        const float b_r8 = (gi & 1) ? half_hi(bvh[gi / 2]) : half_lo(bvh[gi / 2]);
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt) {
           const float4 v =
-              *reinterpret_cast<const float4*>(stp + xz_off + (g4 * Cfg::XZ_COLS + tt * 8) * 8);  // X0, Z0, X1, Z1
+              *reinterpret_cast<const float4*>(stp + xz_off + (gi * Cfg::XZ_COLS + tt * 8) * 8);  // X0, Z0, X1, Z1
           acc[tt][0] = fmaf(s_r, (dA[tt][0] + dB[tt][0]) - v.y, fmaf(b_r, v.x, acc[tt][0]));
           acc[tt][2] = fmaf(s_r8, (dA[tt][2] + dB[tt][2]) - v.y, fmaf(b_r8, v.x, acc[tt][2]));
           if (MT > 1) {  // a single token uses column 0 only
@@ -502,27 +490,6 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
     if (!seg_end) continue;
     const bool whole = (seg_begin == 0) && (c == 0);
 
-    // Combine the two k-halves of each row tile: the second-half warp hands
-    // its accumulators to its partner through shared memory.
-    const uint32_t my_comb = comb + (rt * 32 + lane) * (16 * NT);
-    if (kh == 1) {
-#pragma unroll
-      for (int tt = 0; tt < NT; ++tt)
-        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(my_comb + tt * 16), "f"(acc[tt][0]),
-                     "f"(acc[tt][1]), "f"(acc[tt][2]), "f"(acc[tt][3])
-                     : "memory");
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
-    if (kh == 0) {
-#pragma unroll
-      for (int tt = 0; tt < NT; ++tt) {
-        const float4 v = lds_f32x4(my_comb + tt * 16);
-        acc[tt][0] += v.x;
-        acc[tt][1] += v.y;
-        acc[tt][2] += v.z;
-        acc[tt][3] += v.w;
-      }
-    }
     const int row0 = t_done * Cfg::BN + wrow + r;
     if (p.split > 1) {
       // Cluster split-K: this CTA's only segment.  Non-leaders store their
@@ -532,7 +499,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
       asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
       const uint32_t recv = smem_u32(smem + Cfg::OFF_RECV);
       if (rank != 0) {
-        if (kh == 0) {
+        {
           const uint32_t lrecv = recv + (rank - 1) * (Cfg::BN * Cfg::MPAD * 4);
           uint32_t rrecv;
           asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rrecv) : "r"(lrecv));
@@ -556,7 +523,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
       } else {
         if (!*abort_flag && !mbar_wait(recv_bar, 0, p.status, kDevTimeoutAccum)) *abort_flag = 1;
         asm volatile("fence.acq_rel.cluster;" ::: "memory");
-        if (kh == 0 && !*abort_flag) {
+        if (!*abort_flag) {
           for (int q = 1; q < p.split; ++q) {
             const uint32_t lrecv = recv + (q - 1) * (Cfg::BN * Cfg::MPAD * 4);
 #pragma unroll
@@ -587,7 +554,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
         }
       }
     } else if (whole) {
-      if (kh == 0 && !*abort_flag) {
+      if (!*abort_flag) {
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
@@ -610,7 +577,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
       // final segment.
       const int slot_idx = (t_done == first_tile) ? 0 : 1;
       float* mine = p.part + ((size_t)blockIdx.x * 2 + slot_idx) * Cfg::PART;
-      if (kh == 0) {
+      {
 #pragma unroll
         for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
@@ -642,7 +609,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
 #pragma unroll 1
       for (int q = 0; q < 2; ++q) {
         const int tf = fin_flag[q] - 1;
-        if (tf < 0 || kh != 0) continue;
+        if (tf < 0) continue;
         const long long tu0 = (long long)tf * p.C;
         const int i_first = cta_of_unit(tu0, p.U, p.G);
         const int i_last = cta_of_unit(tu0 + p.C - 1, p.U, p.G);
@@ -680,7 +647,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1)
         }
       }
     }
-    // the combine buffer and the flag are rewritten only after this barrier
+    // fin_flag and the partial slots are rewritten only after this barrier
     asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt)

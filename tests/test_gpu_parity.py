@@ -71,7 +71,13 @@ def test_golden_matmul(name):
     y = run_qmm(g["x"], g["wq"], g["scales"], g["biases"])
     assert rel_err(y, g["y32"]) <= TOL
     y32 = run_qmm(g["x"], g["wq"], g["scales"], g["biases"], out_dtype=torch.float32)
-    assert rel_err(y32, g["y32"]) <= 1e-3
+    if g["x"].shape[0] <= 16:
+        assert rel_err(y32, g["y32"]) <= 1e-3
+    else:
+        # M >= 17 multiplies the fp16 dequantized weights (deq_twice, bit-exact
+        # with qw_dequantize): compare against their float64 product.
+        y_deq = g["x"].astype(np.float64) @ g["deq_twice"].astype(np.float64).T
+        assert rel_err(y32, y_deq) <= 1e-4
 
 
 # ------------------------------------------------------------- sweeps
