@@ -71,6 +71,22 @@ typedef struct qw_array {
 int qw_quantized_matmul(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
                         int transpose, int group_size, int bits, const char* mode, qw_array* y, void* stream);
 
+/* As qw_quantized_matmul for at most 16 rows of x, for callers that must not
+ * have the library allocate device memory during the call (a runtime that
+ * owns all of the GPU's memory in its own pool; a decode loop that cannot
+ * absorb cudaFree's device-wide wait).  Allocates nothing: its scratch is a
+ * fixed 4 MiB device array that every GPU loading the library holds until the
+ * process exits.  The first call on a device resolves that array's address
+ * (make it before any stream capture).  All calls on a device share the
+ * array, so calls that overlap on the GPU race; calls on one stream are safe.
+ * More than 16 rows, or a shape whose scratch exceeds the array, returns
+ * QW_EUNSUPPORTED.  A kernel that gives up on a bounded wait leaves y
+ * incomplete without an error code here.
+ * No counterpart in the reference: MLX allocates through its own allocator. */
+int qw_quantized_matmul_static_scratch(const qw_array* x, const qw_array* w, const qw_array* scales,
+                                       const qw_array* biases, int transpose, int group_size, int bits,
+                                       const char* mode, qw_array* y, void* stream);
+
 /* y = x @ dequantize(w).T (+ linear_bias), linear_bias nullable f16 [N].
  * Replaces: quantized_linear_forward, lib.rs:591-601, mlx_cxx_bridge.cpp:1099-1133. */
 int qw_quantized_linear_forward(const qw_array* x, const qw_array* w, const qw_array* scales,

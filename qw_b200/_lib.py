@@ -43,6 +43,7 @@ _PA = ctypes.POINTER(QwArray)
 
 SIGNATURES = {
     "qw_quantized_matmul": ([_PA, _PA, _PA, _PA, _I, _I, _I, ctypes.c_char_p, _PA, _P], _I),
+    "qw_quantized_matmul_static_scratch": ([_PA, _PA, _PA, _PA, _I, _I, _I, ctypes.c_char_p, _PA, _P], _I),
     "qw_quantized_linear_forward": ([_PA, _PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, _PA, _P], _I),
     "qw_quantized_linear_forward_global_scale": (
         [_PA, _PA, _PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, _PA, _P], _I),

@@ -337,6 +337,40 @@ int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const 
 }
 
 }  // namespace
+
+int check_qmm_call(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
+                   int transpose, int group_size, int bits, const char* mode, qw_array* y, SkinnyArgs* sa) {
+  int rc;
+  if ((rc = check_quant_params(mode, biases != nullptr, group_size, bits))) return rc;
+  if (!transpose) return fail(QW_EUNSUPPORTED, "transpose=false is not supported");
+  WeightDims d;
+  if ((rc = check_weights(w, scales, biases, group_size, bits, &d))) return rc;
+  if ((rc = check_array(x, "x")) || (rc = check_array(y, "y"))) return rc;
+  if (x->dtype != QW_F16) return fail(QW_EUNSUPPORTED, std::string("x must be float16, got ") + dtype_name(x->dtype));
+  if (x->shape[x->ndim - 1] != d.K)
+    return fail(QW_EINVAL, "x's last dimension " + std::to_string(x->shape[x->ndim - 1]) +
+                               " does not match the weights' input width " + std::to_string(d.K));
+  const int64_t M = numel(x) / (d.K ? d.K : 1);
+  if (y->dtype != QW_F16 && y->dtype != QW_F32)
+    return fail(QW_EINVAL, std::string("y must be float16 or float32, got ") + dtype_name(y->dtype));
+  if (y->shape[y->ndim - 1] != d.N || numel(y) != M * d.N)
+    return fail(QW_EINVAL, "y must have shape [..., N] with the leading dimensions of x");
+  *sa = SkinnyArgs{};
+  sa->x = x->data;
+  sa->w = (const uint32_t*)w->data;
+  sa->scales = scales->data;
+  sa->biases = biases->data;
+  sa->y = y->data;
+  sa->y_f32 = y->dtype == QW_F32;
+  sa->M = M;
+  sa->N = d.N;
+  sa->K = d.K;
+  if (M == 0 || d.N == 0) return QW_OK;
+  if (!aligned(x->data, 16)) return fail(QW_EINVAL, "x must be 16-byte aligned");
+  if (!aligned(y->data, y->dtype == QW_F32 ? 4 : 2)) return fail(QW_EINVAL, "y is misaligned");
+  return QW_OK;
+}
+
 }  // namespace qw
 
 using namespace qw;

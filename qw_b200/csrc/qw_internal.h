@@ -7,6 +7,8 @@
 
 #include <string>
 
+struct qw_array;
+
 namespace qw {
 
 // Error reporting: the C-ABI stores a message in a thread-local string.
@@ -52,6 +54,14 @@ struct SkinnyArgs {
 size_t skinny_scratch_bytes(const SkinnyArgs& a, int device);
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                           std::string* err);
+// Bytes at the start of a skinny launch's scratch that must be zero when it
+// starts (its split-tile counters).
+size_t skinny_zeroed_bytes(const SkinnyArgs& a);
+// The matmul entry points' argument checks (qw_api.cu), without touching the
+// device; on QW_OK fills every field of `sa` but max_ctas and status, with M
+// the rows of x (all of them, not limited to 16).
+int check_qmm_call(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
+                   int transpose, int group_size, int bits, const char* mode, qw_array* y, SkinnyArgs* sa);
 
 // Prefill path (tcgen05, M >= 17).
 struct PrefillArgs {

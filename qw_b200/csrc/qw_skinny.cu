@@ -775,6 +775,12 @@ size_t skinny_scratch_bytes(const SkinnyArgs& a, int device) {
   return kCounterBytes + (size_t)di.sm_count * 2 * BN * mpad * sizeof(float);
 }
 
+size_t skinny_zeroed_bytes(const SkinnyArgs& a) {
+  static_assert(SkinnyCfg<1>::BN == 128 && SkinnyCfg<8>::BN == 128 && SkinnyCfg<16>::BN == 128, "row tile");
+  const size_t tiles = (size_t)((a.N + 127) / 128);
+  return (tiles < kMaxCounters ? tiles : kMaxCounters) * sizeof(unsigned int);
+}
+
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                           std::string* err) {
   if (a.M == 1) return launch_cfg<1>(a, scratch, stream, pdl, err);
