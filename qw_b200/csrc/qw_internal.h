@@ -50,6 +50,10 @@ struct SkinnyArgs {
   int max_ctas;          // 0 = occupancy-derived
   unsigned int* status;  // device status word
 };
+// Skinny-path scratch layout: split-tile counters (zero between launches) at
+// the start, then the partial-sum slots.
+constexpr size_t kSkinnyMaxCounters = 1u << 16;  // row tiles per launch
+constexpr size_t kSkinnyCounterBytes = kSkinnyMaxCounters * sizeof(unsigned int);
 // Scratch bytes the skinny path needs for a shape (0 when it runs unsplit).
 size_t skinny_scratch_bytes(const SkinnyArgs& a, int device);
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,

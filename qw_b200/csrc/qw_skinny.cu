@@ -46,8 +46,8 @@ namespace {
 constexpr int kGroup = 64;
 constexpr int kGroupsPerStage = 8;
 constexpr int kChunkK = kGroup * kGroupsPerStage;  // 512
-constexpr size_t kMaxCounters = 1u << 16;  // row tiles per launch (N <= 16M rows)
-constexpr size_t kCounterBytes = kMaxCounters * sizeof(unsigned int);
+constexpr size_t kMaxCounters = kSkinnyMaxCounters;  // row tiles per launch (N <= 8M rows)
+constexpr size_t kCounterBytes = kSkinnyCounterBytes;
 
 constexpr int align1k(int v) { return (v + 1023) / 1024 * 1024; }
 
