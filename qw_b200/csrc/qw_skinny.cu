@@ -12,16 +12,19 @@
 // order (deterministic) and writes y.
 //
 // CTA roles (warp-specialised), per pipeline stage of 128 rows x 512 k:
-//   warp 0        TMA producer: packed W (two 128-byte SW128 boxes, 32 KB),
-//                 scales and biases (one box each), and x (one 3-D box of
-//                 8 groups x M rows), the x box issued only after
-//                 griddepcontrol.wait, so the weight stream of this launch
-//                 overlaps the tail of the previous kernel under PDL.
+//   warp 0        TMA producer of packed W (two 128-byte SW128 boxes, 32 KB),
+//                 scales and biases (one box each); it does not wait for the
+//                 previous kernel, so under PDL this launch's weight stream
+//                 starts while the previous kernel finishes.
+//   warp 1        TMA producer of x (one 3-D box of 8 groups x M rows), after
+//                 griddepcontrol.wait (x is the previous kernel's output).
 //   helper warps  turn the stage's x into the MMA B fragments every consumer
 //                 warp needs (permuted, odd k pre-scaled by 1/16) and the
 //                 per-group sums X and Z of the fold below.
-//   16 consumers  16 weight rows and half of the stage's 8 groups each; the
-//                 two halves of a row tile are added at the end of a tile.
+//   8 consumers   16 weight rows and all 8 groups of a unit each.  With up to
+//                 8 tokens a consumer copies unit j+1's weights out of the
+//                 ring group by group while it computes unit j, so a weight
+//                 slot is released one unit earlier.
 //
 // Consumer arithmetic (no per-element dequantisation): a packed word w holds
 // nibbles q0..q7 (k ascending).  lop3(w & 0x000F000F | 0x64006400) is the fp16
@@ -400,28 +403,46 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
   int t = first_tile, c = first_chunk, wslot = 0, sslot = 0;
   uint32_t wphase = 0, sphase = 0;
   int seg_begin = first_chunk;
-  for (int j = 0; j < nunits; ++j) {
-    // 1) copy this warp's share of the unit's weights, scales and biases into
-    //    registers, then give the weight slot back to the producer.
-    uint32_t A[8][4];
-    uint4 sv_lo, sv_hi, bv_lo, bv_hi;
-    if (!*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
-    {
-      const uint32_t wb = wring_u + wslot * Cfg::W_STAGE;
-#pragma unroll
-      for (int gi = 0; gi < 8; ++gi)
-        ldmatrix_x4(wb + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
-      sv_lo = lds128(wb + Cfg::OFF_WS + sb_off);
-      sv_hi = lds128(wb + Cfg::OFF_WS + sb_off + 8 * 16);
-      bv_lo = lds128(wb + Cfg::OFF_WB + sb_off);
-      bv_hi = lds128(wb + Cfg::OFF_WB + sb_off + 8 * 16);
-    }
+
+  // This warp's share of a unit's weights, scales and biases lives in
+  // registers: A (ldmatrix fragments of 8 groups) and the rows' scale/bias
+  // words.  Unit j+1's fragments are loaded group by group while unit j is
+  // computed (A[gi] is free once group gi has been expanded), so the weight
+  // slot goes back to the producer one unit earlier and the shared-memory
+  // latency of the copy is hidden behind the MMAs.
+  // (With 16 tokens the register file has no room for this overlap: those
+  // warps copy each unit's share when they start it.)
+  constexpr bool kRoll = MT <= 8;
+  uint32_t A[8][4];
+  uint4 sv_lo, sv_hi, bv_lo, bv_hi;
+  auto release_wslot = [&]() {
     __syncwarp();
     if (lane == 0) mbar_arrive(&wempty[wslot]);
-
-    // 2) compute against the unit's x fragments.
+    if (++wslot == WST) {
+      wslot = 0;
+      wphase ^= 1u;
+    }
+  };
+  auto copy_unit = [&]() {
+    if (!*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
+    const uint32_t wb = wring_u + wslot * Cfg::W_STAGE;
+#pragma unroll
+    for (int gi = 0; gi < 8; ++gi)
+      ldmatrix_x4(wb + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
+    sv_lo = lds128(wb + Cfg::OFF_WS + sb_off);
+    sv_hi = lds128(wb + Cfg::OFF_WS + sb_off + 8 * 16);
+    bv_lo = lds128(wb + Cfg::OFF_WB + sb_off);
+    bv_hi = lds128(wb + Cfg::OFF_WB + sb_off + 8 * 16);
+    release_wslot();
+  };
+  if (nunits > 0) copy_unit();
+  for (int j = 0; j < nunits; ++j) {
+    if (!kRoll && j > 0) copy_unit();
+    const bool has_next = kRoll && j + 1 < nunits;
+    const uint32_t wb_next = wring_u + wslot * Cfg::W_STAGE;
+    // compute against the unit's x fragments, refilling A with unit j+1
     if (!*abort_flag && !mbar_wait(&ready[sslot], sphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
-    if (!*abort_flag) {
+    {
       const uint8_t* stp = sring + sslot * Cfg::S_STAGE;
       const uint32_t svl[4] = {sv_lo.x, sv_lo.y, sv_lo.z, sv_lo.w}, svh[4] = {sv_hi.x, sv_hi.y, sv_hi.z, sv_hi.w};
       const uint32_t bvl[4] = {bv_lo.x, bv_lo.y, bv_lo.z, bv_lo.w}, bvh[4] = {bv_hi.x, bv_hi.y, bv_hi.z, bv_hi.w};
@@ -443,6 +464,11 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
           e[1][i] = lop3_and_or(A[gi][i], 0x00F000F0u);
           e[2][i] = lop3_and_or(w8, 0x000F000Fu);
           e[3][i] = lop3_and_or(w8, 0x00F000F0u);
+        }
+        if (has_next) {
+          if (gi == 0 && !*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull))
+            *abort_flag = 1;
+          ldmatrix_x4(wb_next + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
         }
         float dA[NT][4], dB[NT][4];
 #pragma unroll
@@ -470,15 +496,18 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
         }
       }
     }
+    if (has_next) {
+      sv_lo = lds128(wb_next + Cfg::OFF_WS + sb_off);
+      sv_hi = lds128(wb_next + Cfg::OFF_WS + sb_off + 8 * 16);
+      bv_lo = lds128(wb_next + Cfg::OFF_WB + sb_off);
+      bv_hi = lds128(wb_next + Cfg::OFF_WB + sb_off + 8 * 16);
+      release_wslot();
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sempty[sslot]);
 
     const bool seg_end = (c == p.C - 1) || (j == nunits - 1);
     const int t_done = t;
-    if (++wslot == WST) {
-      wslot = 0;
-      wphase ^= 1u;
-    }
     if (++sslot == SST) {
       sslot = 0;
       sphase ^= 1u;
