@@ -82,8 +82,9 @@ __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&v)[
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 // Exact per-element dequantization, for scales outside the fast path's range.
-__device__ __noinline__ void dequant_group_slow(const uint32_t (&wd)[4], __half s, __half b, uint32_t (&out)[16]) {
-#pragma unroll 1
+// Inlined and fully unrolled so that `out` stays in registers on both paths.
+__device__ __forceinline__ void dequant_group_slow(const uint32_t (&wd)[4], __half s, __half b, uint32_t (&out)[16]) {
+#pragma unroll
   for (int i = 0; i < 4; ++i) {
 #pragma unroll
     for (int pp = 0; pp < 4; ++pp) {
