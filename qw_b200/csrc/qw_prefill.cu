@@ -11,8 +11,8 @@
 //               D[128 x 256, fp32, TMEM] += A[128 x 64, TMEM] * x^T, four
 //               K=16 instructions per group, tcgen05.commit releasing stages.
 //   warps 2-9   dequantize: the two warps of a TMEM lane quarter own its 32
-//               weight rows (one row per lane) and split each group's 64
-//               codes in halves; they write fp16 weights to a TMEM A stage
+//               weight rows (one row per lane) and take alternate groups, all
+//               64 codes of each; they write fp16 weights to a TMEM A stage
 //               with tcgen05.st.  After the last group of a tile they read D
 //               back (tcgen05.ld, half of the tokens each) and store y.
 //
@@ -120,8 +120,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&xfull[s], 1);
       mbar_init(&wpfull[s], 1);
-      mbar_init(&wpempty[s], DQW);
-      mbar_init(&afull[s], DQW);
+      mbar_init(&wpempty[s], DQW / 2);  // the four warps (lane quarters) that own the group
+      mbar_init(&afull[s], DQW / 2);
       mbar_init(&aempty[s], 1);
     }
     mbar_init(dfull, 1);
@@ -206,37 +206,43 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------------------------------------- dequant + epilogue
     const int dw = warp - 2;                 // 0..7
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-    const int khalf = dw >> 2;               // which 32 codes of each group / which 128 tokens
+    const int khalf = dw >> 2;               // which groups (even / odd) / which 128 tokens
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     pdl_wait();
-    uint32_t it = 0, tile_count = 0;
+    uint32_t tile_count = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tile_count) {
       const int nt = tile / p.m_tiles, mt = tile % p.m_tiles;
       const int row = nt * BM + row_in_tile;
       const bool row_ok = row < p.N;
       const __half* srow = p.scales + (size_t)(row_ok ? row : 0) * p.groups;
       const __half* brow = p.biases + (size_t)(row_ok ? row : 0) * p.groups;
-      __half s_next = row_ok ? srow[0] : __float2half(0.f);
-      __half b_next = row_ok ? brow[0] : __float2half(0.f);
-      for (int g = 0; g < p.groups; ++g, ++it) {
+      // This warp dequantizes every other group of the tile in full (the other
+      // warp of its lane quarter takes the rest), so each warp has two MMA
+      // group-times per group of its own.
+      __half s_next = (row_ok && khalf < p.groups) ? srow[khalf] : __float2half(0.f);
+      __half b_next = (row_ok && khalf < p.groups) ? brow[khalf] : __float2half(0.f);
+      for (int g = khalf; g < p.groups; g += 2) {
+        const uint32_t it = tile_count * (uint32_t)p.groups + (uint32_t)g;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         const __half sc = s_next, bi = b_next;
-        if (g + 1 < p.groups && row_ok) {  // prefetch the next group's scale/bias
-          s_next = srow[g + 1];
-          b_next = brow[g + 1];
+        if (g + 2 < p.groups && row_ok) {  // prefetch this warp's next group's scale/bias
+          s_next = srow[g + 2];
+          b_next = brow[g + 2];
         }
         if (!*abort_flag && !mbar_wait(&wpfull[s], ph, p.status, kDevTimeoutFull)) *abort_flag = 1;
-        uint32_t wd[4];
+        uint32_t wd[2][4];
         {
-          const uint4 a = reinterpret_cast<const uint4*>(smem + OFF_WP + s * WP_STAGE + row_in_tile * 32)[khalf];
-          wd[0] = a.x; wd[1] = a.y; wd[2] = a.z; wd[3] = a.w;
+          const uint4* src = reinterpret_cast<const uint4*>(smem + OFF_WP + s * WP_STAGE + row_in_tile * 32);
+          const uint4 a0 = src[0], a1 = src[1];
+          wd[0][0] = a0.x; wd[0][1] = a0.y; wd[0][2] = a0.z; wd[0][3] = a0.w;
+          wd[1][0] = a1.x; wd[1][1] = a1.y; wd[1][2] = a1.z; wd[1][3] = a1.w;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&wpempty[s]);
-        // dequantize this half's 32 codes into 16 fp16 pairs (k ascending)
-        uint32_t out[16];
+        // dequantize the group's 64 codes into 32 fp16 pairs (k ascending)
+        uint32_t out[2][16];
         const float sf = __half2float(sc);
         const bool fast = fabsf(sf) >= 0.0009765625f && fabsf(sf) < 63.0f;  // s/16 exact, 1024 s finite
         if (fast) {
@@ -245,21 +251,25 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t c2 = h2_bits(__halves2half2(__float2half_rn(-1024.f * sf), __float2half_rn(-64.f * sf)));
           const uint32_t b2 = h2_bits(__halves2half2(bi, bi));
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-            for (int pp = 0; pp < 4; ++pp) {
-              const uint32_t t = prmt(wd[i], 0x64646464u, 0x4040u + 0x0101u * pp) & 0xFFF0FF0Fu;
-              out[4 * i + pp] = hadd2_rn(hfma2_rn(t, s2, c2), b2);
+            for (int i = 0; i < 4; ++i) {
+#pragma unroll
+              for (int pp = 0; pp < 4; ++pp) {
+                const uint32_t t = prmt(wd[hh][i], 0x64646464u, 0x4040u + 0x0101u * pp) & 0xFFF0FF0Fu;
+                out[hh][4 * i + pp] = hadd2_rn(hfma2_rn(t, s2, c2), b2);
+              }
             }
-          }
         } else {
-          dequant_group_slow(wd, sc, bi, out);
+          dequant_group_slow(wd[0], sc, bi, out[0]);
+          dequant_group_slow(wd[1], sc, bi, out[1]);
         }
         // write A stage s once the MMAs that read it last have completed
         if (it >= STAGES && !*abort_flag && !mbar_wait(&aempty[s], ph ^ 1, p.status, kDevTimeoutEmpty))
           *abort_flag = 1;
         tc_fence_after();
-        tmem_st_x16(tmem + lane_base + A_COL + s * 32 + khalf * 16, out);
+        tmem_st_x16(tmem + lane_base + A_COL + s * 32, out[0]);
+        tmem_st_x16(tmem + lane_base + A_COL + s * 32 + 16, out[1]);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
