@@ -155,10 +155,16 @@ def build_stack(torch, qw, P, rank, layers, dev):
 
 
 class StackRunner:
-    """Fixed buffers + the per-step launch sequence, for graph capture and eager e2e."""
+    """Fixed buffers + the per-step launch sequence, for graph capture and eager e2e.
 
-    def __init__(self, torch, qw, ws, lm, M, P, group):
+    chain=False issues one qw_quantized_matmul per linear (the drop-in path);
+    chain=True hands each run of consecutive linears with nothing in between
+    (the whole stack on one GPU; qkv+o and gate_up+down between allreduces
+    under tensor parallelism) to qw_quantized_matmul_chain."""
+
+    def __init__(self, torch, qw, ws, lm, M, P, group, chain=False):
         self.torch, self.qw, self.ws, self.lm, self.M, self.P, self.group = torch, qw, ws, lm, M, P, group
+        self.chain = chain and M <= 16
         dev = lm[0].device
         H = synth.HIDDEN
         f16, f32 = torch.float16, torch.float32
@@ -173,6 +179,33 @@ class StackRunner:
         self.o = torch.empty(M, H, dtype=f16, device=dev)
         self.logits = torch.empty(M, lm[0].shape[0], dtype=f16, device=dev)
         self.launches_per_step = 4 * len(ws) + 1
+        if self.chain:
+            self._build_segments()
+
+    def _build_segments(self):
+        """Runs of matmuls separated by the tensor-parallel allreduces."""
+        q_view = self.qkv[:, : self.attn.shape[1]]   # row-strided views: no copies
+        g_view = self.gu[:, : self.gate.shape[1]]
+        segs, cur = [], []
+        for w in self.ws:
+            cur.append((self.h, *w["qkv"], self.qkv))
+            if self.P == 1:
+                cur.append((q_view, *w["o"], self.o))
+            else:
+                cur.append((q_view, *w["o"], self.part))
+                segs.append((cur, self.o))
+                cur = []
+            cur.append((self.o, *w["gate_up"], self.gu))
+            if self.P == 1:
+                cur.append((g_view, *w["down"], self.h))
+            else:
+                cur.append((g_view, *w["down"], self.part))
+                segs.append((cur, self.h))
+                cur = []
+        cur.append((self.h, *self.lm, self.logits))
+        segs.append((cur, None))
+        self.segments = segs
+        self.launches_per_step = sum((len(c) + 23) // 24 for c, _ in segs)
 
     def _mm(self, x, w, out):
         self.qw.quantized_matmul(x, w[0], w[1], w[2], out=out)
@@ -186,6 +219,13 @@ class StackRunner:
         out16.copy_(self.part)
 
     def step(self):
+        if self.chain:
+            for ops, reduced_into in self.segments:
+                self.qw.quantized_matmul_chain(ops)
+                if reduced_into is not None:
+                    self.torch.distributed.all_reduce(self.part, group=self.group)
+                    reduced_into.copy_(self.part)
+            return
         M = self.M
         for w in self.ws:
             self._mm(self.h, w["qkv"], self.qkv)
@@ -352,15 +392,25 @@ def run_ours(args):
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(dev)
 
-    runner = StackRunner(torch, qw, ws, lm, 1, P, group)
+    # value: one qw_quantized_matmul per linear (the drop-in path), the step
+    # captured once as a CUDA graph with programmatic dependent launch
+    runner = StackRunner(torch, qw, ws, lm, 1, P, group, chain=False)
     ms, clocks = timed_graph(torch, runner, args.steps, args.warmup, stream, dist_on, local)
     step_bytes = synth.stack_bytes(1, layers=args.layers) // P if P > 1 else synth.stack_bytes(1, layers=args.layers)
     tok_s = 1000.0 / ms
     launches = runner.launches_per_step
-
     e2e_ms, h2d, d2h = timed_e2e(torch, runner, args.steps, args.warmup, stream, dist_on)
+    # the same step through qw_quantized_matmul_chain (runs of linears per cooperative launch)
+    chained = StackRunner(torch, qw, ws, lm, 1, P, group, chain=True)
+    ms_chain, _ = timed_graph(torch, chained, args.steps, args.warmup, stream, dist_on, local)
+    chain_launches = chained.launches_per_step
+    del chained
 
-    extra = {}
+    extra = {"stack_m1_chain": {"tok_s": round(1000.0 / ms_chain, 2), "ms_per_step": round(ms_chain, 5),
+                                "GBps_per_gpu": round(step_bytes / (ms_chain * 1e-3) / 1e9, 1),
+                                "frac_hbm": round(step_bytes / (ms_chain * 1e-3) / 1e9 / hbm_peak, 4),
+                                "launches_per_step": chain_launches,
+                                "path": "qw_quantized_matmul_chain, CUDA graph"}}
     if not args.skip_extra:
         # verify-batch stacks (MTP M=4, DFlash2 block M=16): HBM-bound like M=1
         for Mv in (4, 16):

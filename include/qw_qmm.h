@@ -71,6 +71,29 @@ typedef struct qw_array {
 int qw_quantized_matmul(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
                         int transpose, int group_size, int bits, const char* mode, qw_array* y, void* stream);
 
+/* One matmul of a chain: y = x @ dequantize(w, scales, biases).T. */
+typedef struct qw_qmm_op {
+  const qw_array* x;
+  const qw_array* w;
+  const qw_array* scales;
+  const qw_array* biases;
+  qw_array* y;
+} qw_qmm_op;
+
+/* Runs ops[0..n_ops) in order, as n_ops calls of qw_quantized_matmul
+ * (transpose = true) would, where op i may read what earlier ops wrote (its x
+ * may be an earlier y).  Every op is validated as qw_quantized_matmul
+ * validates it, and all x must have the same number of rows M.  With
+ * M <= 16 up to 24 matmuls share one cooperative launch of one CTA per SM:
+ * a matmul's weights start streaming while the previous matmul finishes,
+ * and a grid-wide count of finished CTAs orders the dependent reads.  With
+ * larger M it issues one launch per op.
+ * No counterpart in the reference: it fuses a sequence of the reference's
+ * quantized_matmul calls (lib.rs:1134-1143) for decode loops whose
+ * consecutive linears have nothing in between. */
+int qw_quantized_matmul_chain(const qw_qmm_op* ops, int n_ops, int group_size, int bits, const char* mode,
+                              void* stream);
+
 /* As qw_quantized_matmul for at most 16 rows of x, for callers that must not
  * have the library allocate device memory during the call (a runtime that
  * owns all of the GPU's memory in its own pool; a decode loop that cannot

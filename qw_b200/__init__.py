@@ -6,7 +6,7 @@ The compute lives in libqwqmm.so (C ABI in include/qw_qmm.h); this package is
 the Python mirror of the reference's operator surface on torch tensors.
 """
 from .ops import (QuantizedLinear, dequantize, device_status, quantize_weights, quantized_linear_forward,
-                  quantized_linear_forward_global_scale, quantized_matmul)
+                  quantized_linear_forward_global_scale, quantized_matmul, quantized_matmul_chain)
 
 __all__ = [
     "QuantizedLinear",
@@ -16,4 +16,5 @@ __all__ = [
     "quantized_linear_forward",
     "quantized_linear_forward_global_scale",
     "quantized_matmul",
+    "quantized_matmul_chain",
 ]

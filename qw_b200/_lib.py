@@ -41,8 +41,14 @@ class QwArray(ctypes.Structure):
 
 _PA = ctypes.POINTER(QwArray)
 
+
+class QwQmmOp(ctypes.Structure):
+    _fields_ = [("x", _PA), ("w", _PA), ("scales", _PA), ("biases", _PA), ("y", _PA)]
+
+
 SIGNATURES = {
     "qw_quantized_matmul": ([_PA, _PA, _PA, _PA, _I, _I, _I, ctypes.c_char_p, _PA, _P], _I),
+    "qw_quantized_matmul_chain": ([ctypes.POINTER(QwQmmOp), _I, _I, _I, ctypes.c_char_p, _P], _I),
     "qw_quantized_matmul_static_scratch": ([_PA, _PA, _PA, _PA, _I, _I, _I, ctypes.c_char_p, _PA, _P], _I),
     "qw_quantized_linear_forward": ([_PA, _PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, _PA, _P], _I),
     "qw_quantized_linear_forward_global_scale": (

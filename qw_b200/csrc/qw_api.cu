@@ -10,6 +10,8 @@
 #include <mutex>
 #include <string>
 #include <utility>
+#include <vector>
+#include <algorithm>
 
 #include "../../include/qw_qmm.h"
 #include "qw_internal.h"
@@ -209,6 +211,42 @@ int check_array(const qw_array* a, const char* what) {
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// x: rows of K contiguous elements, one uniform step (*ld elements) from a
+// row to the next, leading dimensions flattened (so a column slice of a
+// wider matrix is accepted without a copy).  The step must keep every row
+// 16-byte aligned (a TMA stride).
+int check_x_rows(const qw_array* x, int64_t K, int64_t* ld) {
+  if (!x) return fail(QW_EINVAL, "x is null");
+  if (x->ndim < 1 || x->ndim > 4) return fail(QW_EINVAL, "x must have 1 to 4 dimensions");
+  for (int i = 0; i < x->ndim; ++i)
+    if (x->shape[i] < 0) return fail(QW_EINVAL, "x has a negative dimension");
+  if (numel(x) > 0 && x->data == nullptr) return fail(QW_EINVAL, "x has a null data pointer");
+  *ld = K;
+  if (contiguous(x)) return QW_OK;
+  const int last = x->ndim - 1;
+  if (x->shape[last] != 1 && x->strides[last] != 1)
+    return fail(QW_EINVAL, "x's last dimension must be contiguous");
+  int64_t rows = 1;
+  for (int i = 0; i < last; ++i) rows *= x->shape[i];
+  if (rows <= 1) return QW_OK;
+  // The leading dimensions must collapse into one row index: going outwards,
+  // each stride equals the next inner one times that dimension's size.
+  int64_t step = 0, inner = -1;
+  for (int i = last - 1; i >= 0; --i) {
+    if (x->shape[i] == 1) continue;
+    if (inner < 0) {
+      step = x->strides[i];
+    } else if (x->strides[i] != inner) {
+      return fail(QW_EINVAL, "x's leading dimensions must be contiguous over its rows");
+    }
+    inner = x->strides[i] * x->shape[i];
+  }
+  if (step < K) return fail(QW_EINVAL, "x's rows overlap (row stride below K)");
+  if ((step * 2) % 16 != 0) return fail(QW_EINVAL, "x's row stride must be a multiple of 8 elements");
+  *ld = step;
+  return QW_OK;
+}
+
 // Mode / bits / group checks in the order of the reference's validators:
 // mode allowlist (layers.rs:1367-1380), biases presence (layers.rs:1409-1440),
 // bits and group bounds (layers.rs:1286-1318).
@@ -282,7 +320,8 @@ int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const 
   if (!transpose) return fail(QW_EUNSUPPORTED, "transpose=false is not supported");
   WeightDims d;
   if ((rc = check_weights(w, scales, biases, group_size, bits, &d))) return rc;
-  if ((rc = check_array(x, "x")) || (rc = check_array(y, "y"))) return rc;
+  int64_t x_ld = 0;
+  if ((rc = check_x_rows(x, d.K, &x_ld)) || (rc = check_array(y, "y"))) return rc;
   if (x->dtype != QW_F16) return fail(QW_EUNSUPPORTED, std::string("x must be float16, got ") + dtype_name(x->dtype));
   if (x->shape[x->ndim - 1] != d.K)
     return fail(QW_EINVAL, "x's last dimension " + std::to_string(x->shape[x->ndim - 1]) +
@@ -309,6 +348,7 @@ int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const 
   if (M > 16 && prefill_available()) {
     PrefillArgs pa{x->data, (const uint32_t*)w->data, scales->data, biases->data, y->data, y32, M, d.N, d.K,
                    res->status};
+    pa.x_ld = x_ld;
     ce = launch_prefill(pa, stream, pdl_enabled(), &err);
     if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "prefill launch") : fail(QW_ECUDA, err);
     return QW_OK;
@@ -317,7 +357,8 @@ int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const 
   for (int64_t m0 = 0; m0 < M; m0 += 16) {
     const int64_t mb = (M - m0) < 16 ? (M - m0) : 16;
     SkinnyArgs sa{};
-    sa.x = static_cast<const uint8_t*>(x->data) + m0 * d.K * 2;
+    sa.x = static_cast<const uint8_t*>(x->data) + m0 * x_ld * 2;
+    sa.x_ld = x_ld;
     sa.w = (const uint32_t*)w->data;
     sa.scales = scales->data;
     sa.biases = biases->data;
@@ -345,7 +386,8 @@ int check_qmm_call(const qw_array* x, const qw_array* w, const qw_array* scales,
   if (!transpose) return fail(QW_EUNSUPPORTED, "transpose=false is not supported");
   WeightDims d;
   if ((rc = check_weights(w, scales, biases, group_size, bits, &d))) return rc;
-  if ((rc = check_array(x, "x")) || (rc = check_array(y, "y"))) return rc;
+  int64_t x_ld = 0;
+  if ((rc = check_x_rows(x, d.K, &x_ld)) || (rc = check_array(y, "y"))) return rc;
   if (x->dtype != QW_F16) return fail(QW_EUNSUPPORTED, std::string("x must be float16, got ") + dtype_name(x->dtype));
   if (x->shape[x->ndim - 1] != d.K)
     return fail(QW_EINVAL, "x's last dimension " + std::to_string(x->shape[x->ndim - 1]) +
@@ -365,6 +407,7 @@ int check_qmm_call(const qw_array* x, const qw_array* w, const qw_array* scales,
   sa->M = M;
   sa->N = d.N;
   sa->K = d.K;
+  sa->x_ld = x_ld;
   if (M == 0 || d.N == 0) return QW_OK;
   if (!aligned(x->data, 16)) return fail(QW_EINVAL, "x must be 16-byte aligned");
   if (!aligned(y->data, y->dtype == QW_F32 ? 4 : 2)) return fail(QW_EINVAL, "y is misaligned");
@@ -381,6 +424,62 @@ int qw_quantized_matmul(const qw_array* x, const qw_array* w, const qw_array* sc
                         int transpose, int group_size, int bits, const char* mode, qw_array* y, void* stream) {
   set_error("");
   return run_qmm(x, w, scales, biases, transpose, group_size, bits, mode, y, stream);
+}
+
+int qw_quantized_matmul_chain(const qw_qmm_op* ops, int n_ops, int group_size, int bits, const char* mode,
+                              void* stream_v) {
+  set_error("");
+  if (n_ops < 0) return fail(QW_EINVAL, "n_ops must not be negative");
+  if (n_ops > 0 && !ops) return fail(QW_EINVAL, "ops is null");
+  if (n_ops == 0) return QW_OK;
+  std::vector<SkinnyArgs> args((size_t)n_ops);
+  int rc;
+  for (int i = 0; i < n_ops; ++i) {
+    const qw_qmm_op& o = ops[i];
+    if ((rc = check_qmm_call(o.x, o.w, o.scales, o.biases, 1, group_size, bits, mode, o.y, &args[i]))) {
+      set_error("op " + std::to_string(i) + ": " + last_error());
+      return rc;
+    }
+    if (args[i].M != args[0].M)
+      return fail(QW_EINVAL, "op " + std::to_string(i) + " has " + std::to_string(args[i].M) +
+                                 " rows of x, op 0 has " + std::to_string(args[0].M));
+  }
+  const int64_t M = args[0].M;
+  if (M > 16 || args[0].M == 0) {
+    // Prefill-sized (or empty) chains: one launch per matmul, in order.
+    for (int i = 0; i < n_ops; ++i) {
+      const qw_qmm_op& o = ops[i];
+      if ((rc = run_qmm(o.x, o.w, o.scales, o.biases, 1, group_size, bits, mode, o.y, stream_v))) return rc;
+    }
+    return QW_OK;
+  }
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  DeviceRes* res = nullptr;
+  std::string err;
+  if (!device_res(dev, &res, &err)) return fail(QW_ENOMEM, err);
+  cudaStream_t stream = as_stream(stream_v);
+  size_t need = 0;
+  for (auto& a : args) {
+    a.status = res->status;
+    a.max_ctas = 0;
+    const size_t b = skinny_scratch_bytes(a, dev);
+    need = b > need ? b : need;
+  }
+  Scratch sc;
+  if (!scratch_for(dev, stream, need, &sc, &err)) return fail(QW_ENOMEM, err);
+  // Matmuls with no rows of y (N == 0) have nothing to compute.
+  std::vector<SkinnyArgs> live;
+  live.reserve(args.size());
+  for (auto& a : args)
+    if (a.N > 0) live.push_back(a);
+  for (size_t i0 = 0; i0 < live.size(); i0 += kSkinnyChainMax) {
+    const int n = (int)std::min(live.size() - i0, (size_t)kSkinnyChainMax);
+    ce = launch_skinny_chain(live.data() + i0, n, sc, stream, &err);
+    if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "chained skinny launch") : fail(QW_ECUDA, err);
+  }
+  return QW_OK;
 }
 
 static int linear_common(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,

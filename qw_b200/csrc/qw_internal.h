@@ -40,7 +40,7 @@ struct Scratch {
 
 // Skinny path (M <= 16): stream-K over (row tile, 512-wide k chunk) units.
 struct SkinnyArgs {
-  const void* x;         // fp16 [M][K]
+  const void* x;         // fp16 [M][K], rows x_ld apart
   const uint32_t* w;     // [N][K/8]
   const void* scales;    // fp16 [N][K/64]
   const void* biases;    // fp16 [N][K/64]
@@ -49,6 +49,7 @@ struct SkinnyArgs {
   int64_t M, N, K;
   int max_ctas;          // 0 = occupancy-derived
   unsigned int* status;  // device status word
+  int64_t x_ld = 0;      // elements from one row of x to the next (0 = K)
 };
 // Skinny-path scratch layout: split-tile counters (zero between launches) at
 // the start, then the partial-sum slots.
@@ -58,8 +59,14 @@ constexpr size_t kSkinnyCounterBytes = kSkinnyMaxCounters * sizeof(unsigned int)
 size_t skinny_scratch_bytes(const SkinnyArgs& a, int device);
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                           std::string* err);
+// Matmuls of one chained skinny launch (bounded by the kernel parameter space).
+constexpr int kSkinnyChainMax = 24;
+// Up to kSkinnyChainMax matmuls with the same M <= 16, in order, each allowed
+// to read any earlier one's y, in one cooperative launch.
+cudaError_t launch_skinny_chain(const SkinnyArgs* ops, int n, const Scratch& scratch, cudaStream_t stream,
+                                std::string* err);
 // Bytes at the start of a skinny launch's scratch that must be zero when it
-// starts (its split-tile counters).
+// starts (its grid-barrier word and split-tile counters).
 size_t skinny_zeroed_bytes(const SkinnyArgs& a);
 // The matmul entry points' argument checks (qw_api.cu), without touching the
 // device; on QW_OK fills every field of `sa` but max_ctas and status, with M
@@ -77,6 +84,7 @@ struct PrefillArgs {
   bool y_f32;
   int64_t M, N, K;
   unsigned int* status;
+  int64_t x_ld = 0;  // elements from one row of x to the next (0 = K)
 };
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err);
 bool prefill_available();

@@ -337,7 +337,8 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, 
   p.biases = reinterpret_cast<const __half*>(a.biases);
   p.status = a.status;
   CUtensorMap tx, tw;
-  if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2,
+  if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
+                      (uint64_t)(a.x_ld ? a.x_ld : a.K) * 2,
                       kGroup, BT, CU_TENSOR_MAP_SWIZZLE_128B, err))
     return cudaErrorInvalidValue;
   if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,

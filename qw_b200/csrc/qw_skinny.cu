@@ -39,6 +39,8 @@
 // fp32 (the reference semantics).
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "qw_internal.h"
 #include "qw_ptx.cuh"
 
@@ -108,20 +110,36 @@ struct SkinnyCfg {
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-struct SkinnyParams {
-  int M, N, K;
+// One quantized matmul of a launch.  The tensor maps live in the kernel's
+// parameter space (__grid_constant__), where TMA may read them.
+struct SkinnyOp {
+  CUtensorMap tm_w, tm_s, tm_b, tm_x;
+  int N, K;
   int C;          // chunks along K
   int T;          // row tiles
   long long U;    // T * C
-  int G;          // CTAs
+  int G;          // CTAs that take units of this matmul: the first min(grid, U)
   int sb_tma;     // scales/biases through TMA (needs K % 512 == 0)
-  int split;      // > 1: each tile is split over a cluster of `split` CTAs (G = T * split)
   int y_f32;
   void* y;
   const __half* scales;
   const __half* biases;
+};
+
+// A launch runs OPS_MAX >= n_ops matmuls in order, every CTA taking its share
+// of each.  With several, matmul o+1 may read what matmul o wrote: a CTA
+// counts itself in gbar[o] once all its writes for o are done, and loads x
+// for o+1 only when all G CTAs have (the weight ring runs ahead regardless).
+template <int OPS_MAX>
+struct SkinnyLaunch {
+  SkinnyOp op[OPS_MAX];
+  int n_ops;
+  int M;
+  int G;                  // CTAs (all resident at once when n_ops > 1)
+  int split;              // > 1 (one matmul only): each tile split over a cluster of `split` CTAs
   float* part;            // [G][2][PART]
   unsigned int* counter;  // [T], zero between launches
+  unsigned int* gbar;     // [n_ops]: CTAs done with each matmul, zero at launch (n_ops > 1)
   unsigned int* status;   // device status word
 };
 
@@ -151,11 +169,29 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t w, uint32_t mask) {
 __device__ __forceinline__ float half_lo(uint32_t h2) { return __half2float(__ushort_as_half((uint16_t)(h2 & 0xffffu))); }
 __device__ __forceinline__ float half_hi(uint32_t h2) { return __half2float(__ushort_as_half((uint16_t)(h2 >> 16))); }
 
-template <int MT>
+// Grid-wide wait of a chained launch: all `target` CTAs have finished the
+// matmul whose tally `gbar` is.
+__device__ __forceinline__ bool wait_matmuls_done(const unsigned int* gbar, unsigned int target,
+                                                  unsigned int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(gbar) : "memory");
+    if (v >= target) break;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_status(status, kDevTimeoutAccum);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  // x is read by TMA (async proxy) after other CTAs' generic stores
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
+template <int MT, int OPS_MAX>
 __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyCfg<MT>::MAXREG)
-    qmm_skinny_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
-                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_x,
-                      const SkinnyParams p) {
+    qmm_skinny_kernel(const __grid_constant__ SkinnyLaunch<OPS_MAX> p) {
   using Cfg = SkinnyCfg<MT>;
   constexpr int NT = Cfg::NT;
   constexpr int WST = Cfg::WST;
@@ -178,11 +214,16 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const long long u0 = unit_begin(blockIdx.x, p.U, p.G);
-  const long long u1 = unit_begin(blockIdx.x + 1, p.U, p.G);
-  const int nunits = (int)(u1 - u0);
-  const int first_tile = (int)(u0 / p.C);
-  const int first_chunk = (int)(u0 % p.C);
+  // This CTA's contiguous range of (tile, chunk) units of matmul o.
+  auto units_of = [&](int o, long long* u0) -> int {
+    const SkinnyOp& op = p.op[OPS_MAX == 1 ? 0 : o];
+    if ((int)blockIdx.x >= op.G) {
+      *u0 = 0;
+      return 0;
+    }
+    *u0 = unit_begin(blockIdx.x, op.U, op.G);
+    return (int)(unit_begin(blockIdx.x + 1, op.U, op.G) - *u0);
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < WST; ++i) {
@@ -211,60 +252,67 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
   if (warp == 0) {
     // ---------------------------------------------------- weight producer
     // Weights, scales and biases are constants of the launch: this ring does
-    // not wait for the previous kernel at all.
-    const uint32_t w_bytes = 2 * Cfg::W_BOX + (p.sb_tma ? 2 * Cfg::SB_BYTES : 0);
+    // not wait for the previous kernel, nor for the previous matmul of a
+    // chain, so their tails overlap the next weights' stream.
     const uint64_t pol_w = l2_policy_evict_first();
-    if (lane == 0) {
-      prefetch_tensormap(&tm_w);
-      if (p.sb_tma) {
-        prefetch_tensormap(&tm_s);
-        prefetch_tensormap(&tm_b);
-      }
-    }
-    const int G = p.K / kGroup;
-    int t = first_tile, c = first_chunk, slot = 0;
+    int slot = 0, issued = 0;
     uint32_t phase = 0;
-    for (int j = 0; j < nunits; ++j) {
-      if (j >= WST && !*abort_flag) {
-        if (!mbar_wait(&wempty[slot], phase ^ 1u, p.status, kDevTimeoutEmpty)) *abort_flag = 1;
+    for (int o = 0; o < (OPS_MAX == 1 ? 1 : p.n_ops); ++o) {
+      const SkinnyOp& op = p.op[OPS_MAX == 1 ? 0 : o];
+      const uint32_t w_bytes = 2 * Cfg::W_BOX + (op.sb_tma ? 2 * Cfg::SB_BYTES : 0);
+      if (lane == 0) {
+        prefetch_tensormap(&op.tm_w);
+        if (op.sb_tma) {
+          prefetch_tensormap(&op.tm_s);
+          prefetch_tensormap(&op.tm_b);
+        }
       }
-      if (*abort_flag) break;
-      uint8_t* st = wring + slot * Cfg::W_STAGE;
-      if (!p.sb_tma) {
-        // Scales/biases rows are not 16-byte strided (K % 512 != 0): stage
-        // them with plain loads, zero beyond the matrix edge.
-        __half* ss = reinterpret_cast<__half*>(st + Cfg::OFF_WS);
-        __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_WB);
-        for (int e = lane; e < Cfg::BN * kGroupsPerStage; e += 32) {
-          const int r = e / kGroupsPerStage, g = e % kGroupsPerStage;
-          const int row = t * Cfg::BN + r, grp = c * kGroupsPerStage + g;
-          __half sv = __float2half(0.f), bv = __float2half(0.f);
-          if (row < p.N && grp < G) {
-            sv = p.scales[(size_t)row * G + grp];
-            bv = p.biases[(size_t)row * G + grp];
+      long long u0;
+      const int nunits = units_of(o, &u0);
+      const int G = op.K / kGroup;
+      int t = (int)(u0 / op.C), c = (int)(u0 % op.C);
+      for (int j = 0; j < nunits; ++j, ++issued) {
+        if (issued >= WST && !*abort_flag) {
+          if (!mbar_wait(&wempty[slot], phase ^ 1u, p.status, kDevTimeoutEmpty)) *abort_flag = 1;
+        }
+        if (*abort_flag) break;
+        uint8_t* st = wring + slot * Cfg::W_STAGE;
+        if (!op.sb_tma) {
+          // Scales/biases rows are not 16-byte strided (K % 512 != 0): stage
+          // them with plain loads, zero beyond the matrix edge.
+          __half* ss = reinterpret_cast<__half*>(st + Cfg::OFF_WS);
+          __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_WB);
+          for (int e = lane; e < Cfg::BN * kGroupsPerStage; e += 32) {
+            const int r = e / kGroupsPerStage, g = e % kGroupsPerStage;
+            const int row = t * Cfg::BN + r, grp = c * kGroupsPerStage + g;
+            __half sv = __float2half(0.f), bv = __float2half(0.f);
+            if (row < op.N && grp < G) {
+              sv = op.scales[(size_t)row * G + grp];
+              bv = op.biases[(size_t)row * G + grp];
+            }
+            ss[e] = sv;
+            sb[e] = bv;
           }
-          ss[e] = sv;
-          sb[e] = bv;
+          __syncwarp();
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&wfull[slot], w_bytes);
+          tma_load_2d_hint(st, &op.tm_w, &wfull[slot], c * 256, t * Cfg::BN, pol_w);
+          tma_load_2d_hint(st + Cfg::W_BOX, &op.tm_w, &wfull[slot], c * 256 + 128, t * Cfg::BN, pol_w);
+          if (op.sb_tma) {
+            tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
+            tma_load_2d_hint(st + Cfg::OFF_WB, &op.tm_b, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
+          }
         }
         __syncwarp();
-      }
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&wfull[slot], w_bytes);
-        tma_load_2d_hint(st, &tm_w, &wfull[slot], c * 256, t * Cfg::BN, pol_w);
-        tma_load_2d_hint(st + Cfg::W_BOX, &tm_w, &wfull[slot], c * 256 + 128, t * Cfg::BN, pol_w);
-        if (p.sb_tma) {
-          tma_load_2d_hint(st + Cfg::OFF_WS, &tm_s, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
-          tma_load_2d_hint(st + Cfg::OFF_WB, &tm_b, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
+        if (++slot == WST) {
+          slot = 0;
+          phase ^= 1u;
         }
-      }
-      __syncwarp();
-      if (++slot == WST) {
-        slot = 0;
-        phase ^= 1u;
-      }
-      if (++c == p.C) {
-        c = 0;
-        ++t;
+        if (++c == op.C) {
+          c = 0;
+          ++t;
+        }
       }
     }
     return;
@@ -273,23 +321,34 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
   if (warp == 1) {
     // ------------------------------------------------------- x producer
     if (lane == 0) {
-      prefetch_tensormap(&tm_x);
       const uint32_t x_bytes = kGroupsPerStage * 128 * p.M;
       pdl_wait();  // x is the previous kernel's output
-      int c = first_chunk, slot = 0;
+      int slot = 0, issued = 0;
       uint32_t phase = 0;
-      for (int j = 0; j < nunits; ++j) {
-        if (j >= SST && !*abort_flag) {
-          if (!mbar_wait(&sempty[slot], phase ^ 1u, p.status, kDevTimeoutEmpty)) *abort_flag = 1;
+      for (int o = 0; o < (OPS_MAX == 1 ? 1 : p.n_ops) && !*abort_flag; ++o) {
+        const SkinnyOp& op = p.op[OPS_MAX == 1 ? 0 : o];
+        prefetch_tensormap(&op.tm_x);
+        // matmul o's x may be matmul o-1's y: wait until every CTA is done with it
+        if (o > 0 && !wait_matmuls_done(p.gbar + (o - 1), (unsigned int)p.G, p.status)) {
+          *abort_flag = 1;
+          break;
         }
-        if (*abort_flag) break;
-        mbar_arrive_expect_tx(&sfull[slot], x_bytes);
-        tma_load_3d(sring + slot * Cfg::S_STAGE + Cfg::OFF_X, &tm_x, &sfull[slot], 0, 0, c * kGroupsPerStage);
-        if (++slot == SST) {
-          slot = 0;
-          phase ^= 1u;
+        long long u0;
+        const int nunits = units_of(o, &u0);
+        int c = (int)(u0 % op.C);
+        for (int j = 0; j < nunits; ++j, ++issued) {
+          if (issued >= SST && !*abort_flag) {
+            if (!mbar_wait(&sempty[slot], phase ^ 1u, p.status, kDevTimeoutEmpty)) *abort_flag = 1;
+          }
+          if (*abort_flag) break;
+          mbar_arrive_expect_tx(&sfull[slot], x_bytes);
+          tma_load_3d(sring + slot * Cfg::S_STAGE + Cfg::OFF_X, &op.tm_x, &sfull[slot], 0, 0, c * kGroupsPerStage);
+          if (++slot == SST) {
+            slot = 0;
+            phase ^= 1u;
+          }
+          if (++c == op.C) c = 0;
         }
-        if (++c == p.C) c = 0;
       }
     }
     return;
@@ -310,56 +369,60 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
     }
     int slot = 0;
     uint32_t phase = 0;
-    for (int j = 0; j < nunits; ++j) {
-      if (!*abort_flag && !mbar_wait(&sfull[slot], phase, p.status, kDevTimeoutFull)) *abort_flag = 1;
-      uint8_t* st = sring + slot * Cfg::S_STAGE;
-      const uint32_t xbase = smem_u32(st + Cfg::OFF_X);
-      const uint32_t bf = smem_u32(st + Cfg::OFF_BF);
-      const uint32_t xz = smem_u32(st + Cfg::OFF_XZ);
-      // task = ((gi * M + n) * 4 + s): lanes 4k..4k+3 share one (group, token)
-      for (int base = h * 32; base < 32 * p.M; base += Cfg::HW * 32) {
-        const int task = base + lane;
-        const int s = task & 3;
-        const int gn = task >> 2;
-        const int gi = MT == 1 ? gn : gn / p.M;
-        const int n = MT == 1 ? 0 : gn - gi * p.M;
-        const int line = gn;  // box layout [group][token][64 halves]
-        const uint4 xv0 = lds128(xbase + line * 128 + ((s ^ (line & 7)) << 4));
-        const uint4 xv1 = lds128(xbase + line * 128 + (((4 + s) ^ (line & 7)) << 4));
-        // B fragment of MMA jj: (x[8s+jj], x[8s+jj+4]) and the same 32 further
-        // on; odd jj scaled by 1/16 to match the in-place odd nibbles.
-        uint4 f0, f1;
-        f0.x = prmt(xv0.x, xv0.z, 0x5410);
-        f0.y = prmt(xv1.x, xv1.z, 0x5410);
-        f0.z = hmul2_rn(prmt(xv0.x, xv0.z, 0x7632), 0x2C002C00u);
-        f0.w = hmul2_rn(prmt(xv1.x, xv1.z, 0x7632), 0x2C002C00u);
-        f1.x = prmt(xv0.y, xv0.w, 0x5410);
-        f1.y = prmt(xv1.y, xv1.w, 0x5410);
-        f1.z = hmul2_rn(prmt(xv0.y, xv0.w, 0x7632), 0x2C002C00u);
-        f1.w = hmul2_rn(prmt(xv1.y, xv1.w, 0x7632), 0x2C002C00u);
-        const uint32_t fa = bf + ((gi * Cfg::BF_TOK + n) * 4 + s) * 32;
-        sts128(fa, f0);
-        sts128(fa + 16, f1);
-        // sums over even and odd k of the 16 x values this lane holds
-        float xe = 0.f, xo = 0.f;
-        const uint32_t wv[8] = {xv0.x, xv0.y, xv0.z, xv0.w, xv1.x, xv1.y, xv1.z, xv1.w};
+    for (int o = 0; o < (OPS_MAX == 1 ? 1 : p.n_ops); ++o) {
+      long long u0;
+      const int nunits = units_of(o, &u0);
+      for (int j = 0; j < nunits; ++j) {
+        if (!*abort_flag && !mbar_wait(&sfull[slot], phase, p.status, kDevTimeoutFull)) *abort_flag = 1;
+        uint8_t* st = sring + slot * Cfg::S_STAGE;
+        const uint32_t xbase = smem_u32(st + Cfg::OFF_X);
+        const uint32_t bf = smem_u32(st + Cfg::OFF_BF);
+        const uint32_t xz = smem_u32(st + Cfg::OFF_XZ);
+        // task = ((gi * M + n) * 4 + s): lanes 4k..4k+3 share one (group, token)
+        for (int base = h * 32; base < 32 * p.M; base += Cfg::HW * 32) {
+          const int task = base + lane;
+          const int s = task & 3;
+          const int gn = task >> 2;
+          const int gi = MT == 1 ? gn : gn / p.M;
+          const int n = MT == 1 ? 0 : gn - gi * p.M;
+          const int line = gn;  // box layout [group][token][64 halves]
+          const uint4 xv0 = lds128(xbase + line * 128 + ((s ^ (line & 7)) << 4));
+          const uint4 xv1 = lds128(xbase + line * 128 + (((4 + s) ^ (line & 7)) << 4));
+          // B fragment of MMA jj: (x[8s+jj], x[8s+jj+4]) and the same 32 further
+          // on; odd jj scaled by 1/16 to match the in-place odd nibbles.
+          uint4 f0, f1;
+          f0.x = prmt(xv0.x, xv0.z, 0x5410);
+          f0.y = prmt(xv1.x, xv1.z, 0x5410);
+          f0.z = hmul2_rn(prmt(xv0.x, xv0.z, 0x7632), 0x2C002C00u);
+          f0.w = hmul2_rn(prmt(xv1.x, xv1.z, 0x7632), 0x2C002C00u);
+          f1.x = prmt(xv0.y, xv0.w, 0x5410);
+          f1.y = prmt(xv1.y, xv1.w, 0x5410);
+          f1.z = hmul2_rn(prmt(xv0.y, xv0.w, 0x7632), 0x2C002C00u);
+          f1.w = hmul2_rn(prmt(xv1.y, xv1.w, 0x7632), 0x2C002C00u);
+          const uint32_t fa = bf + ((gi * Cfg::BF_TOK + n) * 4 + s) * 32;
+          sts128(fa, f0);
+          sts128(fa + 16, f1);
+          // sums over even and odd k of the 16 x values this lane holds
+          float xe = 0.f, xo = 0.f;
+          const uint32_t wv[8] = {xv0.x, xv0.y, xv0.z, xv0.w, xv1.x, xv1.y, xv1.z, xv1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[i]));
-          xe += f.x;
-          xo += f.y;
+          for (int i = 0; i < 8; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[i]));
+            xe += f.x;
+            xo += f.y;
+          }
+          xe += __shfl_xor_sync(0xffffffffu, xe, 1);
+          xo += __shfl_xor_sync(0xffffffffu, xo, 1);
+          xe += __shfl_xor_sync(0xffffffffu, xe, 2);
+          xo += __shfl_xor_sync(0xffffffffu, xo, 2);
+          if (s == 0) sts_f32x2(xz + (gi * Cfg::XZ_COLS + n) * 8, xe + xo, 1024.f * xe + 64.f * xo);
         }
-        xe += __shfl_xor_sync(0xffffffffu, xe, 1);
-        xo += __shfl_xor_sync(0xffffffffu, xo, 1);
-        xe += __shfl_xor_sync(0xffffffffu, xe, 2);
-        xo += __shfl_xor_sync(0xffffffffu, xo, 2);
-        if (s == 0) sts_f32x2(xz + (gi * Cfg::XZ_COLS + n) * 8, xe + xo, 1024.f * xe + 64.f * xo);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ready[slot]);
-      if (++slot == SST) {
-        slot = 0;
-        phase ^= 1u;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[slot]);
+        if (++slot == SST) {
+          slot = 0;
+          phase ^= 1u;
+        }
       }
     }
     return;
@@ -400,18 +463,24 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
   const uint32_t xz_off = Cfg::OFF_XZ + 2 * s4 * 8;
   const uint32_t wring_u = smem_u32(wring);
 
-  int t = first_tile, c = first_chunk, wslot = 0, sslot = 0;
+  int wslot = 0, sslot = 0;
   uint32_t wphase = 0, sphase = 0;
-  int seg_begin = first_chunk;
+  // units of every matmul this CTA takes, in ring order
+  int total = 0;
+  for (int o = 0; o < (OPS_MAX == 1 ? 1 : p.n_ops); ++o) {
+    long long u0;
+    total += units_of(o, &u0);
+  }
+  int done = 0;
 
   // This warp's share of a unit's weights, scales and biases lives in
   // registers: A (ldmatrix fragments of 8 groups) and the rows' scale/bias
-  // words.  Unit j+1's fragments are loaded group by group while unit j is
-  // computed (A[gi] is free once group gi has been expanded), so the weight
-  // slot goes back to the producer one unit earlier and the shared-memory
-  // latency of the copy is hidden behind the MMAs.
-  // (With 16 tokens the register file has no room for this overlap: those
-  // warps copy each unit's share when they start it.)
+  // words.  The next unit's fragments (of this matmul or the next) are loaded
+  // group by group while a unit is computed (A[gi] is free once group gi has
+  // been expanded), so the weight slot goes back to the producer one unit
+  // earlier and the shared-memory latency of the copy is hidden behind the
+  // MMAs.  (With 16 tokens the register file has no room for this overlap:
+  // those warps copy each unit's share when they start it.)
   constexpr bool kRoll = MT <= 8;
   uint32_t A[8][4];
   uint4 sv_lo, sv_hi, bv_lo, bv_hi;
@@ -435,341 +504,383 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
     bv_hi = lds128(wb + Cfg::OFF_WB + sb_off + 8 * 16);
     release_wslot();
   };
-  if (nunits > 0) copy_unit();
-  for (int j = 0; j < nunits; ++j) {
-    if (!kRoll && j > 0) copy_unit();
-    const bool has_next = kRoll && j + 1 < nunits;
-    const uint32_t wb_next = wring_u + wslot * Cfg::W_STAGE;
-    // compute against the unit's x fragments, refilling A with unit j+1
-    if (!*abort_flag && !mbar_wait(&ready[sslot], sphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
-    {
-      const uint8_t* stp = sring + sslot * Cfg::S_STAGE;
-      const uint32_t svl[4] = {sv_lo.x, sv_lo.y, sv_lo.z, sv_lo.w}, svh[4] = {sv_hi.x, sv_hi.y, sv_hi.z, sv_hi.w};
-      const uint32_t bvl[4] = {bv_lo.x, bv_lo.y, bv_lo.z, bv_lo.w}, bvh[4] = {bv_hi.x, bv_hi.y, bv_hi.z, bv_hi.w};
+  if (total > 0) copy_unit();
+
+  for (int o = 0; o < (OPS_MAX == 1 ? 1 : p.n_ops); ++o) {
+    const SkinnyOp& op = p.op[OPS_MAX == 1 ? 0 : o];
+    long long u0;
+    const int nunits = units_of(o, &u0);
+    const int first_tile = (int)(u0 / op.C);
+    int t = first_tile, c = (int)(u0 % op.C);
+    int seg_begin = c;
+    for (int j = 0; j < nunits; ++j, ++done) {
+      if (!kRoll && done > 0) copy_unit();
+      const bool has_next = kRoll && done + 1 < total;
+      const uint32_t wb_next = wring_u + wslot * Cfg::W_STAGE;
+      // compute against the unit's x fragments, refilling A with the next unit
+      if (!*abort_flag && !mbar_wait(&ready[sslot], sphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
+      {
+        const uint8_t* stp = sring + sslot * Cfg::S_STAGE;
+        const uint32_t svl[4] = {sv_lo.x, sv_lo.y, sv_lo.z, sv_lo.w}, svh[4] = {sv_hi.x, sv_hi.y, sv_hi.z, sv_hi.w};
+        const uint32_t bvl[4] = {bv_lo.x, bv_lo.y, bv_lo.z, bv_lo.w}, bvh[4] = {bv_hi.x, bv_hi.y, bv_hi.z, bv_hi.w};
 #pragma unroll
-      for (int gi = 0; gi < 8; ++gi) {
-        uint4 b0[NT], b1[NT];
+        for (int gi = 0; gi < 8; ++gi) {
+          uint4 b0[NT], b1[NT];
 #pragma unroll
-        for (int tt = 0; tt < NT; ++tt) {
-          const uint4* fb = reinterpret_cast<const uint4*>(stp + bf_off[tt] + gi * (Cfg::BF_TOK * 4 * 32));
-          b0[tt] = fb[0];
-          b1[tt] = fb[1];
-        }
-        // expanded A registers: e[jj][i] for word i
-        uint32_t e[4][4];
+          for (int tt = 0; tt < NT; ++tt) {
+            const uint4* fb = reinterpret_cast<const uint4*>(stp + bf_off[tt] + gi * (Cfg::BF_TOK * 4 * 32));
+            b0[tt] = fb[0];
+            b1[tt] = fb[1];
+          }
+          // expanded A registers: e[jj][i] for word i
+          uint32_t e[4][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t w8 = A[gi][i] >> 8;
-          e[0][i] = lop3_and_or(A[gi][i], 0x000F000Fu);
-          e[1][i] = lop3_and_or(A[gi][i], 0x00F000F0u);
-          e[2][i] = lop3_and_or(w8, 0x000F000Fu);
-          e[3][i] = lop3_and_or(w8, 0x00F000F0u);
-        }
-        if (has_next) {
-          if (gi == 0 && !*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull))
-            *abort_flag = 1;
-          ldmatrix_x4(wb_next + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
-        }
-        float dA[NT][4], dB[NT][4];
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t w8 = A[gi][i] >> 8;
+            e[0][i] = lop3_and_or(A[gi][i], 0x000F000Fu);
+            e[1][i] = lop3_and_or(A[gi][i], 0x00F000F0u);
+            e[2][i] = lop3_and_or(w8, 0x000F000Fu);
+            e[3][i] = lop3_and_or(w8, 0x00F000F0u);
+          }
+          if (has_next) {
+            if (gi == 0 && !*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull))
+              *abort_flag = 1;
+            ldmatrix_x4(wb_next + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
+          }
+          float dA[NT][4], dB[NT][4];
 #pragma unroll
-        for (int tt = 0; tt < NT; ++tt) {
-          mma_16816_zc(dA[tt], e[0][0], e[0][1], e[0][2], e[0][3], b0[tt].x, b0[tt].y);
-          mma_16816_zc(dB[tt], e[1][0], e[1][1], e[1][2], e[1][3], b0[tt].z, b0[tt].w);
-          mma_16816(dA[tt], e[2][0], e[2][1], e[2][2], e[2][3], b1[tt].x, b1[tt].y);
-          mma_16816(dB[tt], e[3][0], e[3][1], e[3][2], e[3][3], b1[tt].z, b1[tt].w);
-        }
-        // fold the group: y += s * (d - Z) + b * X
-        const float s_r = (gi & 1) ? half_hi(svl[gi / 2]) : half_lo(svl[gi / 2]);
-        const float s_r8 = (gi & 1) ? half_hi(svh[gi / 2]) : half_lo(svh[gi / 2]);
-        const float b_r = (gi & 1) ? half_hi(bvl[gi / 2]) : half_lo(bvl[gi / 2]);
-        const float b_r8 = (gi & 1) ? half_hi(bvh[gi / 2]) : half_lo(bvh[gi / 2]);
+          for (int tt = 0; tt < NT; ++tt) {
+            mma_16816_zc(dA[tt], e[0][0], e[0][1], e[0][2], e[0][3], b0[tt].x, b0[tt].y);
+            mma_16816_zc(dB[tt], e[1][0], e[1][1], e[1][2], e[1][3], b0[tt].z, b0[tt].w);
+            mma_16816(dA[tt], e[2][0], e[2][1], e[2][2], e[2][3], b1[tt].x, b1[tt].y);
+            mma_16816(dB[tt], e[3][0], e[3][1], e[3][2], e[3][3], b1[tt].z, b1[tt].w);
+          }
+          // fold the group: y += s * (d - Z) + b * X
+          const float s_r = (gi & 1) ? half_hi(svl[gi / 2]) : half_lo(svl[gi / 2]);
+          const float s_r8 = (gi & 1) ? half_hi(svh[gi / 2]) : half_lo(svh[gi / 2]);
+          const float b_r = (gi & 1) ? half_hi(bvl[gi / 2]) : half_lo(bvl[gi / 2]);
+          const float b_r8 = (gi & 1) ? half_hi(bvh[gi / 2]) : half_lo(bvh[gi / 2]);
 #pragma unroll
-        for (int tt = 0; tt < NT; ++tt) {
-          const float4 v =
-              *reinterpret_cast<const float4*>(stp + xz_off + (gi * Cfg::XZ_COLS + tt * 8) * 8);  // X0, Z0, X1, Z1
-          acc[tt][0] = fmaf(s_r, (dA[tt][0] + dB[tt][0]) - v.y, fmaf(b_r, v.x, acc[tt][0]));
-          acc[tt][2] = fmaf(s_r8, (dA[tt][2] + dB[tt][2]) - v.y, fmaf(b_r8, v.x, acc[tt][2]));
-          if (MT > 1) {  // a single token uses column 0 only
-            acc[tt][1] = fmaf(s_r, (dA[tt][1] + dB[tt][1]) - v.w, fmaf(b_r, v.z, acc[tt][1]));
-            acc[tt][3] = fmaf(s_r8, (dA[tt][3] + dB[tt][3]) - v.w, fmaf(b_r8, v.z, acc[tt][3]));
+          for (int tt = 0; tt < NT; ++tt) {
+            const float4 v =
+                *reinterpret_cast<const float4*>(stp + xz_off + (gi * Cfg::XZ_COLS + tt * 8) * 8);  // X0, Z0, X1, Z1
+            acc[tt][0] = fmaf(s_r, (dA[tt][0] + dB[tt][0]) - v.y, fmaf(b_r, v.x, acc[tt][0]));
+            acc[tt][2] = fmaf(s_r8, (dA[tt][2] + dB[tt][2]) - v.y, fmaf(b_r8, v.x, acc[tt][2]));
+            if (MT > 1) {  // a single token uses column 0 only
+              acc[tt][1] = fmaf(s_r, (dA[tt][1] + dB[tt][1]) - v.w, fmaf(b_r, v.z, acc[tt][1]));
+              acc[tt][3] = fmaf(s_r8, (dA[tt][3] + dB[tt][3]) - v.w, fmaf(b_r8, v.z, acc[tt][3]));
+            }
           }
         }
       }
-    }
-    if (has_next) {
-      sv_lo = lds128(wb_next + Cfg::OFF_WS + sb_off);
-      sv_hi = lds128(wb_next + Cfg::OFF_WS + sb_off + 8 * 16);
-      bv_lo = lds128(wb_next + Cfg::OFF_WB + sb_off);
-      bv_hi = lds128(wb_next + Cfg::OFF_WB + sb_off + 8 * 16);
-      release_wslot();
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sempty[sslot]);
+      if (has_next) {
+        sv_lo = lds128(wb_next + Cfg::OFF_WS + sb_off);
+        sv_hi = lds128(wb_next + Cfg::OFF_WS + sb_off + 8 * 16);
+        bv_lo = lds128(wb_next + Cfg::OFF_WB + sb_off);
+        bv_hi = lds128(wb_next + Cfg::OFF_WB + sb_off + 8 * 16);
+        release_wslot();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[sslot]);
 
-    const bool seg_end = (c == p.C - 1) || (j == nunits - 1);
-    const int t_done = t;
-    if (++sslot == SST) {
-      sslot = 0;
-      sphase ^= 1u;
-    }
-    if (++c == p.C) {
-      c = 0;
-      ++t;
-    }
-    if (!seg_end) continue;
-    const bool whole = (seg_begin == 0) && (c == 0);
+      const bool seg_end = (c == op.C - 1) || (j == nunits - 1);
+      const int t_done = t;
+      if (++sslot == SST) {
+        sslot = 0;
+        sphase ^= 1u;
+      }
+      if (++c == op.C) {
+        c = 0;
+        ++t;
+      }
+      if (!seg_end) continue;
+      const bool whole = (seg_begin == 0) && (c == 0);
 
-    const int row0 = t_done * Cfg::BN + wrow + r;
-    if (p.split > 1) {
-      // Cluster split-K: this CTA's only segment.  Non-leaders store their
-      // partial into the leader's shared memory and arrive on its barrier;
-      // the leader adds them in rank order and writes y.
-      uint32_t rank;
-      asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
-      const uint32_t recv = smem_u32(smem + Cfg::OFF_RECV);
-      if (rank != 0) {
-        {
-          const uint32_t lrecv = recv + (rank - 1) * (Cfg::BN * Cfg::MPAD * 4);
-          uint32_t rrecv;
-          asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rrecv) : "r"(lrecv));
-#pragma unroll
-          for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const int rl = wrow + r + 8 * hh;
-              const uint32_t a = rrecv + (rl * Cfg::MPAD + tt * 8 + 2 * s4) * 4;
-              asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(acc[tt][2 * hh]),
-                           "f"(acc[tt][2 * hh + 1])
-                           : "memory");
-            }
-        }
-        __syncwarp();
-        if (lane == 0) {
-          uint32_t rbar;
-          asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rbar) : "r"(smem_u32(recv_bar)));
-          asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(rbar) : "memory");
-        }
-      } else {
-        if (!*abort_flag && !mbar_wait(recv_bar, 0, p.status, kDevTimeoutAccum)) *abort_flag = 1;
-        asm volatile("fence.acq_rel.cluster;" ::: "memory");
-        if (!*abort_flag) {
-          for (int q = 1; q < p.split; ++q) {
-            const uint32_t lrecv = recv + (q - 1) * (Cfg::BN * Cfg::MPAD * 4);
+      const int row0 = t_done * Cfg::BN + wrow + r;
+      if (p.split > 1) {
+        // Cluster split-K: this CTA's only segment.  Non-leaders store their
+        // partial into the leader's shared memory and arrive on its barrier;
+        // the leader adds them in rank order and writes y.
+        uint32_t rank;
+        asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+        const uint32_t recv = smem_u32(smem + Cfg::OFF_RECV);
+        if (rank != 0) {
+          {
+            const uint32_t lrecv = recv + (rank - 1) * (Cfg::BN * Cfg::MPAD * 4);
+            uint32_t rrecv;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rrecv) : "r"(lrecv));
 #pragma unroll
             for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh) {
                 const int rl = wrow + r + 8 * hh;
-                float2 v;
-                asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];"
-                             : "=f"(v.x), "=f"(v.y)
-                             : "r"(lrecv + (rl * Cfg::MPAD + tt * 8 + 2 * s4) * 4));
-                acc[tt][2 * hh] += v.x;
-                acc[tt][2 * hh + 1] += v.y;
+                const uint32_t a = rrecv + (rl * Cfg::MPAD + tt * 8 + 2 * s4) * 4;
+                asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(acc[tt][2 * hh]),
+                             "f"(acc[tt][2 * hh + 1])
+                             : "memory");
               }
           }
+          __syncwarp();
+          if (lane == 0) {
+            uint32_t rbar;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(rbar) : "r"(smem_u32(recv_bar)));
+            asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(rbar) : "memory");
+          }
+        } else {
+          if (!*abort_flag && !mbar_wait(recv_bar, 0, p.status, kDevTimeoutAccum)) *abort_flag = 1;
+          asm volatile("fence.acq_rel.cluster;" ::: "memory");
+          if (!*abort_flag) {
+            for (int q = 1; q < p.split; ++q) {
+              const uint32_t lrecv = recv + (q - 1) * (Cfg::BN * Cfg::MPAD * 4);
+#pragma unroll
+              for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                  const int rl = wrow + r + 8 * hh;
+                  float2 v;
+                  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];"
+                               : "=f"(v.x), "=f"(v.y)
+                               : "r"(lrecv + (rl * Cfg::MPAD + tt * 8 + 2 * s4) * 4));
+                  acc[tt][2 * hh] += v.x;
+                  acc[tt][2 * hh + 1] += v.y;
+                }
+            }
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int n = tt * 8 + 2 * s4 + (e & 1);
+                const int row = row0 + ((e & 2) ? 8 : 0);
+                if (n < p.M && row < op.N) {
+                  const size_t idx = (size_t)n * op.N + row;
+                  if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = acc[tt][e];
+                  else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(acc[tt][e]);
+                }
+              }
+          }
+        }
+      } else if (whole) {
+        if (!*abort_flag) {
 #pragma unroll
           for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int n = tt * 8 + 2 * s4 + (e & 1);
               const int row = row0 + ((e & 2) ? 8 : 0);
-              if (n < p.M && row < p.N) {
-                const size_t idx = (size_t)n * p.N + row;
-                if (p.y_f32) reinterpret_cast<float*>(p.y)[idx] = acc[tt][e];
-                else reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(acc[tt][e]);
+              if (n < p.M && row < op.N) {
+                const size_t idx = (size_t)n * op.N + row;
+                if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = acc[tt][e];
+                else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(acc[tt][e]);
               }
             }
         }
-      }
-    } else if (whole) {
-      if (!*abort_flag) {
-#pragma unroll
-        for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int n = tt * 8 + 2 * s4 + (e & 1);
-            const int row = row0 + ((e & 2) ? 8 : 0);
-            if (n < p.M && row < p.N) {
-              const size_t idx = (size_t)n * p.N + row;
-              if (p.y_f32) reinterpret_cast<float*>(p.y)[idx] = acc[tt][e];
-              else reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(acc[tt][e]);
-            }
-          }
-      }
-    } else {
-      // Split tile: publish this CTA's partial; the last contributor to
-      // arrive adds the partials in CTA order.  A segment that is not this
-      // CTA's final one does not wait for its arrival's result: thread 0
-      // (consumer warp 0) fences and arrives while the other warps go on
-      // consuming, and a tile found complete there is finished after the
-      // final segment.
-      const int slot_idx = (t_done == first_tile) ? 0 : 1;
-      float* mine = p.part + ((size_t)blockIdx.x * 2 + slot_idx) * Cfg::PART;
-      {
-#pragma unroll
-        for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int n = tt * 8 + 2 * s4 + (e & 1);
-            const int rl = wrow + r + ((e & 2) ? 8 : 0);
-            mine[rl * Cfg::MPAD + n] = acc[tt][e];
-          }
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
-      if (cw == 0 && lane == 0) {
-        // One release fence for the whole CTA's partial (ordered before it by
-        // the barrier), then the arrival; the last arrival acquires.
-        const long long tu0 = (long long)t_done * p.C;
-        const unsigned int ncontrib =
-            (unsigned int)(cta_of_unit(tu0 + p.C - 1, p.U, p.G) - cta_of_unit(tu0, p.U, p.G) + 1);
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        const unsigned int old = atomicAdd(&p.counter[t_done], 1u);
-        if (old == ncontrib - 1) {
-          atomicExch(&p.counter[t_done], 0u);
-          asm volatile("fence.acq_rel.gpu;" ::: "memory");
-          fin_flag[slot_idx] = t_done + 1;  // finish tile t_done after the final segment
-        }
-      }
-    }
-    if (j == nunits - 1) {
-      // Final segment: finish the split tiles this CTA completed.
-      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
-#pragma unroll 1
-      for (int q = 0; q < 2; ++q) {
-        const int tf = fin_flag[q] - 1;
-        if (tf < 0) continue;
-        const long long tu0 = (long long)tf * p.C;
-        const int i_first = cta_of_unit(tu0, p.U, p.G);
-        const int i_last = cta_of_unit(tu0 + p.C - 1, p.U, p.G);
-        float tot[NT][4];
-#pragma unroll
-        for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) tot[tt][e] = 0.f;
-        for (int i = i_first; i <= i_last; ++i) {
-          const int ft = (int)(unit_begin(i, p.U, p.G) / p.C);
-          const float* src = p.part + ((size_t)i * 2 + (tf == ft ? 0 : 1)) * Cfg::PART;
+      } else {
+        // Split tile: publish this CTA's partial; the last contributor to
+        // arrive adds the partials in CTA order.  A segment that is not this
+        // CTA's final one does not wait for its arrival's result: thread 0
+        // (consumer warp 0) fences and arrives while the other warps go on
+        // consuming, and a tile found complete there is finished after the
+        // final segment.
+        const int slot_idx = (t_done == first_tile) ? 0 : 1;
+        float* mine = p.part + ((size_t)blockIdx.x * 2 + slot_idx) * Cfg::PART;
+        {
 #pragma unroll
           for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int n = tt * 8 + 2 * s4 + (e & 1);
               const int rl = wrow + r + ((e & 2) ? 8 : 0);
-              tot[tt][e] += __ldcg(src + rl * Cfg::MPAD + n);
+              mine[rl * Cfg::MPAD + n] = acc[tt][e];
             }
         }
-        if (!*abort_flag) {
-          const int rowf = tf * Cfg::BN + wrow + r;
+        asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+        if (cw == 0 && lane == 0) {
+          // One release fence for the whole CTA's partial (ordered before it by
+          // the barrier), then the arrival; the last arrival acquires.
+          const long long tu0 = (long long)t_done * op.C;
+          const unsigned int ncontrib =
+              (unsigned int)(cta_of_unit(tu0 + op.C - 1, op.U, op.G) - cta_of_unit(tu0, op.U, op.G) + 1);
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
+          const unsigned int old = atomicAdd(&p.counter[t_done], 1u);
+          if (old == ncontrib - 1) {
+            atomicExch(&p.counter[t_done], 0u);
+            asm volatile("fence.acq_rel.gpu;" ::: "memory");
+            fin_flag[slot_idx] = t_done + 1;  // finish tile t_done after the final segment
+          }
+        }
+      }
+      if (j == nunits - 1) {
+        // Final segment: finish the split tiles this CTA completed.
+        asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+#pragma unroll 1
+        for (int q = 0; q < 2; ++q) {
+          const int tf = fin_flag[q] - 1;
+          if (tf < 0) continue;
+          const long long tu0 = (long long)tf * op.C;
+          const int i_first = cta_of_unit(tu0, op.U, op.G);
+          const int i_last = cta_of_unit(tu0 + op.C - 1, op.U, op.G);
+          float tot[NT][4];
 #pragma unroll
           for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int n = tt * 8 + 2 * s4 + (e & 1);
-              const int row = rowf + ((e & 2) ? 8 : 0);
-              if (n < p.M && row < p.N) {
-                const size_t idx = (size_t)n * p.N + row;
-                if (p.y_f32) reinterpret_cast<float*>(p.y)[idx] = tot[tt][e];
-                else reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(tot[tt][e]);
+            for (int e = 0; e < 4; ++e) tot[tt][e] = 0.f;
+          for (int i = i_first; i <= i_last; ++i) {
+            const int ft = (int)(unit_begin(i, op.U, op.G) / op.C);
+            const float* src = p.part + ((size_t)i * 2 + (tf == ft ? 0 : 1)) * Cfg::PART;
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int n = tt * 8 + 2 * s4 + (e & 1);
+                const int rl = wrow + r + ((e & 2) ? 8 : 0);
+                tot[tt][e] += __ldcg(src + rl * Cfg::MPAD + n);
               }
-            }
+          }
+          if (!*abort_flag) {
+            const int rowf = tf * Cfg::BN + wrow + r;
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int n = tt * 8 + 2 * s4 + (e & 1);
+                const int row = rowf + ((e & 2) ? 8 : 0);
+                if (n < p.M && row < op.N) {
+                  const size_t idx = (size_t)n * op.N + row;
+                  if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = tot[tt][e];
+                  else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(tot[tt][e]);
+                }
+              }
+          }
         }
       }
+      // fin_flag and the partial slots are rewritten only after this barrier
+      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+#pragma unroll
+      for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[tt][e] = 0.f;
+      seg_begin = 0;
     }
-    // fin_flag and the partial slots are rewritten only after this barrier
-    asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
-#pragma unroll
-    for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[tt][e] = 0.f;
-    seg_begin = 0;
+    if (OPS_MAX > 1 && p.n_ops > 1) {
+      // Matmul o is done here (y tiles, partials, finished split tiles):
+      // count this CTA in the grid-wide tally the next matmul's x waits on.
+      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+      if (cw == 0 && lane == 0) {
+        fin_flag[0] = 0;
+        fin_flag[1] = 0;
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        atomicAdd(p.gbar + o, 1u);
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+    }
   }
+}
+
+// Scratch layout: the chain's grid-barrier word, the split-tile counters
+// (zero between launches, whatever grid the previous launch used), then the
+// partial slots, which need no initialisation.
+constexpr size_t kGbarBytes = 256;
+static_assert(kSkinnyChainMax * sizeof(unsigned int) <= kGbarBytes, "per-matmul tallies fit");
+
+// One matmul's descriptor: tensor maps and schedule-independent sizes.
+template <int MT>
+bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
+  using Cfg = SkinnyCfg<MT>;
+  op->N = (int)a.N;
+  op->K = (int)a.K;
+  op->C = (int)((a.K + kChunkK - 1) / kChunkK);
+  op->T = (int)((a.N + Cfg::BN - 1) / Cfg::BN);
+  op->U = (long long)op->T * op->C;
+  op->sb_tma = (a.K % kChunkK == 0) ? 1 : 0;
+  op->y_f32 = a.y_f32 ? 1 : 0;
+  op->y = a.y;
+  op->scales = reinterpret_cast<const __half*>(a.scales);
+  op->biases = reinterpret_cast<const __half*>(a.biases);
+  if ((size_t)op->T > kMaxCounters) {
+    *err = "too many row tiles for the skinny path's counter block";
+    return false;
+  }
+  if (!encode_tmap_2d(&op->tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
+                      (uint64_t)(a.K / 2), 128, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_128B, err))
+    return false;
+  {
+    // x viewed as [K/64 groups][M tokens][64 halves]: one box = 8 groups x M tokens
+    const uint64_t dims[3] = {(uint64_t)kGroup, (uint64_t)a.M, (uint64_t)(a.K / kGroup)};
+    const uint64_t strides[2] = {(uint64_t)(a.x_ld ? a.x_ld : a.K) * 2, (uint64_t)kGroup * 2};
+    const uint32_t box[3] = {(uint32_t)kGroup, (uint32_t)a.M, (uint32_t)kGroupsPerStage};
+    if (!encode_tmap_3d(&op->tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B, err))
+      return false;
+  }
+  if (op->sb_tma) {
+    const uint64_t G64 = (uint64_t)(a.K / kGroup);
+    if (!encode_tmap_2d(&op->tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.scales, G64, (uint64_t)a.N, G64 * 2,
+                        kGroupsPerStage, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+      return false;
+    if (!encode_tmap_2d(&op->tm_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.biases, G64, (uint64_t)a.N, G64 * 2,
+                        kGroupsPerStage, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+      return false;
+  } else {
+    op->tm_s = op->tm_w;  // unused
+    op->tm_b = op->tm_w;
+  }
+  return true;
+}
+
+template <int MT, int OPS_MAX>
+cudaError_t set_smem_attr(int dev) {
+  static thread_local int configured_dev = -1;
+  // cudaFuncSetAttribute is per device; cheap enough to repeat on change.
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(qmm_skinny_kernel<MT, OPS_MAX>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SkinnyCfg<MT>::SMEM);
+    if (e != cudaSuccess) return e;
+    configured_dev = dev;
+  }
+  return cudaSuccess;
 }
 
 template <int MT>
 cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                        std::string* err) {
   using Cfg = SkinnyCfg<MT>;
-  auto kern = qmm_skinny_kernel<MT>;
   int dev = 0;
   cudaGetDevice(&dev);
   const DeviceInfo& di = device_info(dev);
-  static thread_local int configured_dev = -1;
-  // cudaFuncSetAttribute is per device; cheap enough to repeat on change.
-  if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    if (e != cudaSuccess) return e;
-    configured_dev = dev;
-  }
-  SkinnyParams p{};
+  cudaError_t e = set_smem_attr<MT, 1>(dev);
+  if (e != cudaSuccess) return e;
+  SkinnyLaunch<1> p{};
+  if (!make_op<MT>(a, &p.op[0], err)) return cudaErrorInvalidValue;
+  p.n_ops = 1;
   p.M = (int)a.M;
-  p.N = (int)a.N;
-  p.K = (int)a.K;
-  p.C = (int)((a.K + kChunkK - 1) / kChunkK);
-  p.T = (int)((a.N + Cfg::BN - 1) / Cfg::BN);
-  p.U = (long long)p.T * p.C;
+  const SkinnyOp& op = p.op[0];
   // Schedule: with fewer row tiles than SMs, each tile gets `split` CTAs (a
   // thread-block cluster reducing through distributed shared memory; one
   // CTA per tile when split == 1).  Otherwise stream-K over all SMs.
   long long G = (long long)di.sm_count;
   if (a.max_ctas > 0 && G > a.max_ctas) G = a.max_ctas;
   p.split = 1;
-  if (p.T <= G) {
-    int split = (int)(G / p.T);
+  if (op.T <= G) {
+    int split = (int)(G / op.T);
     if (split > Cfg::SPLIT_MAX) split = Cfg::SPLIT_MAX;
-    if (split > p.C) split = p.C;
+    if (split > op.C) split = op.C;
     if (split < 1) split = 1;
     p.split = split;
-    G = (long long)p.T * split;
+    G = (long long)op.T * split;
   }
-  if (G > p.U) G = p.U;
+  if (G > op.U) G = op.U;
   p.G = (int)G;
-  p.sb_tma = (a.K % kChunkK == 0) ? 1 : 0;
-  p.y_f32 = a.y_f32 ? 1 : 0;
-  p.y = a.y;
-  p.scales = reinterpret_cast<const __half*>(a.scales);
-  p.biases = reinterpret_cast<const __half*>(a.biases);
-  // Scratch layout: the split-tile counters at a fixed offset (they are zero
-  // between launches, whatever grid the previous launch used), then the
-  // partial slots, which need no initialisation.
-  if ((size_t)p.T > kMaxCounters) {
-    *err = "too many row tiles for the skinny path's counter block";
-    return cudaErrorInvalidValue;
-  }
-  const size_t need = kCounterBytes + (size_t)p.G * 2 * Cfg::PART * sizeof(float);
+  p.op[0].G = p.G;
+  const size_t need = kGbarBytes + kCounterBytes + (size_t)p.G * 2 * Cfg::PART * sizeof(float);
   if (scratch.bytes < need || scratch.base == nullptr) {
     *err = "scratch too small for the skinny path";
     return cudaErrorInvalidValue;
   }
+  uint8_t* base = reinterpret_cast<uint8_t*>(scratch.base);
+  p.gbar = reinterpret_cast<unsigned int*>(base);
+  p.counter = reinterpret_cast<unsigned int*>(base + kGbarBytes);
+  p.part = reinterpret_cast<float*>(base + kGbarBytes + kCounterBytes);
   p.status = a.status;
-  p.counter = reinterpret_cast<unsigned int*>(scratch.base);
-  p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch.base) + kCounterBytes);
-
-  CUtensorMap tw, ts, tb, tx;
-  if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
-                      (uint64_t)(a.K / 2), 128, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_128B, err))
-    return cudaErrorInvalidValue;
-  {
-    // x viewed as [K/64 groups][M tokens][64 halves]: one box = 8 groups x M tokens
-    const uint64_t dims[3] = {(uint64_t)kGroup, (uint64_t)a.M, (uint64_t)(a.K / kGroup)};
-    const uint64_t strides[2] = {(uint64_t)a.K * 2, (uint64_t)kGroup * 2};
-    const uint32_t box[3] = {(uint32_t)kGroup, (uint32_t)a.M, (uint32_t)kGroupsPerStage};
-    if (!encode_tmap_3d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
-                        err))
-      return cudaErrorInvalidValue;
-  }
-  if (p.sb_tma) {
-    const uint64_t G64 = (uint64_t)(a.K / kGroup);
-    if (!encode_tmap_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.scales, G64, (uint64_t)a.N, G64 * 2,
-                        kGroupsPerStage, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
-      return cudaErrorInvalidValue;
-    if (!encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.biases, G64, (uint64_t)a.N, G64 * 2,
-                        kGroupsPerStage, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
-      return cudaErrorInvalidValue;
-  } else {
-    ts = tw;  // unused
-    tb = tw;
-  }
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.G);
@@ -792,7 +903,57 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   }
   cfg.attrs = attr;
   cfg.numAttrs = nattr;
-  return cudaLaunchKernelEx(&cfg, kern, tw, ts, tb, tx, p);
+  return cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, 1>, p);
+}
+
+// A chain of up to kSkinnyChainMax matmuls in one cooperative launch of one
+// CTA per SM, stream-K for every matmul.
+template <int MT>
+cudaError_t launch_chain_cfg(const SkinnyArgs* ops, int n, const Scratch& scratch, cudaStream_t stream,
+                             std::string* err) {
+  using Cfg = SkinnyCfg<MT>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const DeviceInfo& di = device_info(dev);
+  cudaError_t e = set_smem_attr<MT, kSkinnyChainMax>(dev);
+  if (e != cudaSuccess) return e;
+  static SkinnyLaunch<kSkinnyChainMax> p;  // large: build it outside the stack (copied at launch)
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  p = SkinnyLaunch<kSkinnyChainMax>{};
+  for (int i = 0; i < n; ++i)
+    if (!make_op<MT>(ops[i], &p.op[i], err)) return cudaErrorInvalidValue;
+  p.n_ops = n;
+  p.M = (int)ops[0].M;
+  p.G = di.sm_count;
+  p.split = 1;
+  for (int i = 0; i < n; ++i) p.op[i].G = p.op[i].U < p.G ? (int)p.op[i].U : p.G;
+  const size_t need = kGbarBytes + kCounterBytes + (size_t)p.G * 2 * Cfg::PART * sizeof(float);
+  if (scratch.bytes < need || scratch.base == nullptr) {
+    *err = "scratch too small for the skinny path";
+    return cudaErrorInvalidValue;
+  }
+  uint8_t* base = reinterpret_cast<uint8_t*>(scratch.base);
+  p.gbar = reinterpret_cast<unsigned int*>(base);
+  p.counter = reinterpret_cast<unsigned int*>(base + kGbarBytes);
+  p.part = reinterpret_cast<float*>(base + kGbarBytes + kCounterBytes);
+  p.status = ops[0].status;
+  // The per-matmul tallies start at zero; stream order puts this after any
+  // earlier launch that used the same scratch (this launch does not overlap
+  // its predecessor).
+  e = cudaMemsetAsync(p.gbar, 0, (size_t)n * sizeof(unsigned int), stream);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.G);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the grid-wide waits can complete
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, kSkinnyChainMax>, p);
 }
 
 }  // namespace
@@ -801,13 +962,13 @@ size_t skinny_scratch_bytes(const SkinnyArgs& a, int device) {
   const DeviceInfo& di = device_info(device);
   const int mpad = a.M <= 8 ? 8 : 16;
   const int BN = 128;
-  return kCounterBytes + (size_t)di.sm_count * 2 * BN * mpad * sizeof(float);
+  return kGbarBytes + kCounterBytes + (size_t)di.sm_count * 2 * BN * mpad * sizeof(float);
 }
 
 size_t skinny_zeroed_bytes(const SkinnyArgs& a) {
   static_assert(SkinnyCfg<1>::BN == 128 && SkinnyCfg<8>::BN == 128 && SkinnyCfg<16>::BN == 128, "row tile");
   const size_t tiles = (size_t)((a.N + 127) / 128);
-  return (tiles < kMaxCounters ? tiles : kMaxCounters) * sizeof(unsigned int);
+  return kGbarBytes + (tiles < kMaxCounters ? tiles : kMaxCounters) * sizeof(unsigned int);
 }
 
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
@@ -815,6 +976,23 @@ cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStrea
   if (a.M == 1) return launch_cfg<1>(a, scratch, stream, pdl, err);
   if (a.M <= 8) return launch_cfg<8>(a, scratch, stream, pdl, err);
   return launch_cfg<16>(a, scratch, stream, pdl, err);
+}
+
+cudaError_t launch_skinny_chain(const SkinnyArgs* ops, int n, const Scratch& scratch, cudaStream_t stream,
+                                std::string* err) {
+  if (n < 1 || n > kSkinnyChainMax) {
+    *err = "a chained launch takes 1 to " + std::to_string(kSkinnyChainMax) + " matmuls";
+    return cudaErrorInvalidValue;
+  }
+  const int64_t M = ops[0].M;
+  for (int i = 1; i < n; ++i)
+    if (ops[i].M != M) {
+      *err = "every matmul of a chain must have the same number of rows of x";
+      return cudaErrorInvalidValue;
+    }
+  if (M == 1) return launch_chain_cfg<1>(ops, n, scratch, stream, err);
+  if (M <= 8) return launch_chain_cfg<8>(ops, n, scratch, stream, err);
+  return launch_chain_cfg<16>(ops, n, scratch, stream, err);
 }
 
 }  // namespace qw

@@ -66,6 +66,22 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     return out
 
 
+def quantized_matmul_chain(ops, group_size: int = 64, bits: int = 4, mode: str = "affine") -> None:
+    """Runs [(x, w, scales, biases, y), ...] in order, each y = x @ dequantize(w).T
+    written into its preallocated ``y``; an op's x may be an earlier op's y.
+    One cooperative launch per 24 ops when every x has at most 16 rows."""
+    if not ops:
+        return
+    keep = []  # the descriptors must outlive the call
+    arr = (_lib.QwQmmOp * len(ops))()
+    for i, (x, w, s, b, y) in enumerate(ops):
+        d = [_arr(x), _arr(w), _arr(s), _arr(b), _arr(y)]
+        keep.append(d)
+        arr[i].x, arr[i].w, arr[i].scales, arr[i].biases, arr[i].y = d
+    L = _lib.load()
+    _lib.check(L.qw_quantized_matmul_chain(arr, len(ops), group_size, bits, _mode(mode), _stream(ops[0][0])))
+
+
 def quantized_linear_forward(x, w, scales, biases, linear_bias=None, group_size: int = 64, bits: int = 4,
                              mode: str = "affine", out=None) -> torch.Tensor:
     """Quantized linear layer forward (lib.rs:591-601)."""

@@ -127,6 +127,32 @@ def test_output_shape_checked():
     assert _qmm(x, w, s, b, y=_arr([1, 255], _lib.QW_F16)) == _lib.QW_EINVAL
 
 
+def _arr_strided(shape, strides, dtype, ptr=0x1000):
+    a = _arr(shape, dtype, ptr)
+    for i, st in enumerate(strides):
+        a.contents.strides[i] = st
+    return a
+
+
+def test_row_strided_x_layouts():
+    """x may be a column slice (rows of K, one row stride, 16-byte aligned);
+    anything else is rejected before any device work."""
+    _, w, s, b, y = std_args(M=4)
+    # row stride 516: not a multiple of 8 elements (rows would lose 16-byte alignment)
+    assert _qmm(_arr_strided([4, 512], [516, 1], _lib.QW_F16), w, s, b, y=y) == _lib.QW_EINVAL
+    assert "multiple of 8" in err()
+    # overlapping rows
+    assert _qmm(_arr_strided([4, 512], [256, 1], _lib.QW_F16), w, s, b, y=y) == _lib.QW_EINVAL
+    assert "overlap" in err()
+    # last dimension not contiguous
+    assert _qmm(_arr_strided([4, 512], [1024, 2], _lib.QW_F16), w, s, b, y=y) == _lib.QW_EINVAL
+    assert "last dimension" in err()
+    # leading dimensions that do not collapse into one row index
+    y3 = _arr([2, 2, 256], _lib.QW_F16)
+    assert _qmm(_arr_strided([2, 2, 512], [4096, 1024, 1], _lib.QW_F16), w, s, b, y=y3) == _lib.QW_EINVAL
+    assert "leading dimensions" in err()
+
+
 def test_transpose_false_unsupported():
     x, w, s, b, y = std_args()
     assert _qmm(x, w, s, b, y=y, transpose=0) == _lib.QW_EUNSUPPORTED

@@ -142,6 +142,20 @@ def test_leading_batch_dims():
     assert rel_err(host(y), y_ref) <= TOL
 
 
+@pytest.mark.parametrize("M", [1, 4, 16, 40])
+def test_row_strided_x(M):
+    """x as a column slice of a wider matrix (rows 1536 apart) gives the same
+    y as the contiguous copy, on the skinny (M <= 16) and prefill paths."""
+    wq, s, b = quantized(300, 1024, seed=M)
+    wide = torch.from_numpy(synth.activations(M, 1536, seed=M)).cuda()
+    xs = wide[:, 256:256 + 1024]
+    assert M == 1 or not xs.is_contiguous()
+    y_s = qw_b200.quantized_matmul(xs, dev_u32(wq), dev(s), dev(b), out_dtype=torch.float32)
+    y_c = qw_b200.quantized_matmul(xs.contiguous(), dev_u32(wq), dev(s), dev(b), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(y_s, y_c)
+
+
 # -------------------------------------------------------------- edge codes
 @pytest.mark.parametrize("fill", [0x00000000, 0xFFFFFFFF, 0x0F0F0F0F])
 def test_constant_codes(fill):
