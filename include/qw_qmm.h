@@ -94,6 +94,19 @@ typedef struct qw_qmm_op {
 int qw_quantized_matmul_chain(const qw_qmm_op* ops, int n_ops, int group_size, int bits, const char* mode,
                               void* stream);
 
+/* Greedy token of a projection: idx[m] = argmax_n of the fp16 logits
+ * (x @ dequantize(w, scales, biases).T)[m, n], the lowest n among equal
+ * maxima, as uint32 [M]; logits (nullable) receives the fp16 logits.  With
+ * M <= 16 the argmax is folded into the matmul's epilogue (one atomic per CTA
+ * and token) and the logits need not be written; with larger M the logits
+ * buffer is required and a row argmax follows the matmul.
+ * Replaces: quantized_linear_forward (project_logits, crates/runtime/src/
+ * qwen3_5.rs:1038-1044) followed by argmax_last_axis (lib.rs:2055,
+ * mlx_cxx_bridge.cpp:4434-4436). */
+int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_array* scales,
+                               const qw_array* biases, int group_size, int bits, const char* mode, qw_array* logits,
+                               qw_array* idx, void* stream);
+
 /* As qw_quantized_matmul for at most 16 rows of x, for callers that must not
  * have the library allocate device memory during the call (a runtime that
  * owns all of the GPU's memory in its own pool; a decode loop that cannot

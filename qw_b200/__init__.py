@@ -6,7 +6,8 @@ The compute lives in libqwqmm.so (C ABI in include/qw_qmm.h); this package is
 the Python mirror of the reference's operator surface on torch tensors.
 """
 from .ops import (QuantizedLinear, dequantize, device_status, quantize_weights, quantized_linear_forward,
-                  quantized_linear_forward_global_scale, quantized_matmul, quantized_matmul_chain)
+                  quantized_linear_forward_global_scale, quantized_matmul, quantized_matmul_argmax,
+                  quantized_matmul_chain)
 
 __all__ = [
     "QuantizedLinear",
@@ -16,5 +17,6 @@ __all__ = [
     "quantized_linear_forward",
     "quantized_linear_forward_global_scale",
     "quantized_matmul",
+    "quantized_matmul_argmax",
     "quantized_matmul_chain",
 ]

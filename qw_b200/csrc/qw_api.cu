@@ -482,6 +482,69 @@ int qw_quantized_matmul_chain(const qw_qmm_op* ops, int n_ops, int group_size, i
   return QW_OK;
 }
 
+int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_array* scales,
+                               const qw_array* biases, int group_size, int bits, const char* mode, qw_array* logits,
+                               qw_array* idx, void* stream_v) {
+  set_error("");
+  int rc;
+  if ((rc = check_quant_params(mode, biases != nullptr, group_size, bits))) return rc;
+  WeightDims d;
+  if ((rc = check_weights(w, scales, biases, group_size, bits, &d))) return rc;
+  int64_t x_ld = 0;
+  if ((rc = check_x_rows(x, d.K, &x_ld)) || (rc = check_array(idx, "idx"))) return rc;
+  if (logits && (rc = check_array(logits, "logits"))) return rc;
+  if (x->dtype != QW_F16) return fail(QW_EUNSUPPORTED, std::string("x must be float16, got ") + dtype_name(x->dtype));
+  if (x->shape[x->ndim - 1] != d.K)
+    return fail(QW_EINVAL, "x's last dimension " + std::to_string(x->shape[x->ndim - 1]) +
+                               " does not match the weights' input width " + std::to_string(d.K));
+  const int64_t M = numel(x) / (d.K ? d.K : 1);
+  if (idx->dtype != QW_U32 || numel(idx) != M)
+    return fail(QW_EINVAL, "idx must be uint32 with one element per row of x");
+  if (logits && (logits->dtype != QW_F16 || logits->shape[logits->ndim - 1] != d.N || numel(logits) != M * d.N))
+    return fail(QW_EINVAL, "logits must be float16 [..., N] with the leading dimensions of x");
+  if (M == 0) return QW_OK;
+  if (d.N == 0) return fail(QW_EINVAL, "argmax over an empty row (N == 0)");
+  if (!aligned(x->data, 16) || !aligned(idx->data, 4) || (logits && !aligned(logits->data, 2)))
+    return fail(QW_EINVAL, "x must be 16-byte aligned, idx 4-byte aligned");
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  cudaStream_t stream = as_stream(stream_v);
+  std::string err;
+  if (M > 16) {
+    if (!logits) return fail(QW_EINVAL, "a logits buffer is required when x has more than 16 rows");
+    if ((rc = run_qmm(x, w, scales, biases, 1, group_size, bits, mode, logits, stream_v))) return rc;
+    ce = launch_argmax_rows(logits->data, M, d.N, (uint32_t*)idx->data, stream);
+    return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "argmax launch");
+  }
+  DeviceRes* res = nullptr;
+  if (!device_res(dev, &res, &err)) return fail(QW_ENOMEM, err);
+  SkinnyArgs sa{};
+  sa.x = x->data;
+  sa.w = (const uint32_t*)w->data;
+  sa.scales = scales->data;
+  sa.biases = biases->data;
+  sa.y = logits ? logits->data : nullptr;
+  sa.y_f32 = false;
+  sa.M = M;
+  sa.N = d.N;
+  sa.K = d.K;
+  sa.max_ctas = 0;
+  sa.status = res->status;
+  sa.x_ld = x_ld;
+  Scratch sc;
+  if (!scratch_for(dev, stream, skinny_scratch_bytes(sa, dev), &sc, &err)) return fail(QW_ENOMEM, err);
+  // keys in the first 256 bytes of the scratch (the chains' tallies use the first 96)
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(sc.base) + 128);
+  ce = cudaMemsetAsync(keys, 0, (size_t)M * sizeof(unsigned long long), stream);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync");
+  sa.amax = keys;
+  ce = launch_skinny(sa, sc, stream, pdl_enabled(), &err);
+  if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "skinny launch") : fail(QW_ECUDA, err);
+  ce = launch_argmax_finalize(keys, (uint32_t*)idx->data, M, stream);
+  return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "argmax launch");
+}
+
 static int linear_common(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
                          const qw_array* global_scale, const qw_array* linear_bias, int group_size, int bits,
                          const char* mode, qw_array* y, void* stream) {

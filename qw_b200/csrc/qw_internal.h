@@ -50,6 +50,7 @@ struct SkinnyArgs {
   int max_ctas;          // 0 = occupancy-derived
   unsigned int* status;  // device status word
   int64_t x_ld = 0;      // elements from one row of x to the next (0 = K)
+  unsigned long long* amax = nullptr;  // greedy-token keys [M], zeroed by the caller (y may be null)
 };
 // Skinny-path scratch layout: split-tile counters (zero between launches) at
 // the start, then the partial-sum slots.
@@ -88,6 +89,11 @@ struct PrefillArgs {
 };
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err);
 bool prefill_available();
+
+// Greedy token from the keys the skinny kernel left: idx[m] = the row.
+cudaError_t launch_argmax_finalize(const unsigned long long* keys, uint32_t* idx, int64_t M, cudaStream_t stream);
+// Greedy token of each row of fp16 logits [M][N] (lowest index among equal maxima).
+cudaError_t launch_argmax_rows(const void* logits, int64_t M, int64_t N, uint32_t* idx, cudaStream_t stream);
 
 // Quantize / dequantize kernels (affine, 4-bit, group 64 for now).
 cudaError_t launch_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N,

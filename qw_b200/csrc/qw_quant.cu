@@ -147,4 +147,53 @@ cudaError_t launch_f32_to_f16(const float* src, void* dst, int64_t n, cudaStream
   return cudaGetLastError();
 }
 
+
+// ------------------------------------------------------------ greedy token
+namespace {
+
+__global__ void argmax_finalize_kernel(const unsigned long long* keys, uint32_t* idx, int M) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m < M) idx[m] = 0xFFFFFFFFu - (uint32_t)(keys[m] & 0xFFFFFFFFull);
+}
+
+// One block per row; keys as in the skinny kernel's epilogue (order-preserving
+// value above, complemented index below), reduced over the block.
+__global__ void argmax_rows_kernel(const __half* logits, int64_t N, uint32_t* idx) {
+  const __half* row = logits + (size_t)blockIdx.x * N;
+  unsigned long long best = 0ull;
+  for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
+    uint32_t b = __float_as_uint(__half2float(row[n]));
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    const unsigned long long k = ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+    best = v > best ? v : best;
+  }
+  __shared__ unsigned long long warp_best[32];
+  if ((threadIdx.x & 31) == 0) warp_best[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long v = 0ull;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v = warp_best[w] > v ? warp_best[w] : v;
+    idx[blockIdx.x] = 0xFFFFFFFFu - (uint32_t)(v & 0xFFFFFFFFull);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_argmax_finalize(const unsigned long long* keys, uint32_t* idx, int64_t M, cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  argmax_finalize_kernel<<<(unsigned)((M + 127) / 128), 128, 0, stream>>>(keys, idx, (int)M);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_rows(const void* logits, int64_t M, int64_t N, uint32_t* idx, cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  argmax_rows_kernel<<<(unsigned)M, 512, 0, stream>>>(reinterpret_cast<const __half*>(logits), N, idx);
+  return cudaGetLastError();
+}
+
 }  // namespace qw

@@ -140,6 +140,7 @@ struct SkinnyLaunch {
   float* part;            // [G][2][PART]
   unsigned int* counter;  // [T], zero between launches
   unsigned int* gbar;     // [n_ops]: CTAs done with each matmul, zero at launch (n_ops > 1)
+  unsigned long long* amax;  // one matmul only, may be null: [M] greedy-token keys (atomicMax)
   unsigned int* status;   // device status word
 };
 
@@ -168,6 +169,18 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t w, uint32_t mask) {
 }
 __device__ __forceinline__ float half_lo(uint32_t h2) { return __half2float(__ushort_as_half((uint16_t)(h2 & 0xffffu))); }
 __device__ __forceinline__ float half_hi(uint32_t h2) { return __half2float(__ushort_as_half((uint16_t)(h2 >> 16))); }
+
+// Greedy-token key of logit `v` at `row`: the fp16 logit as an order-
+// preserving unsigned integer above, the complement of the row below, so the
+// largest key is the largest logit and, among equal logits, the lowest row.
+__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) {
+  return a > b ? a : b;
+}
+__device__ __forceinline__ unsigned long long amax_key(float v, int row) {
+  uint32_t b = __float_as_uint(__half2float(__float2half_rn(v)));
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row);
+}
 
 // Grid-wide wait of a chained launch: all `target` CTAs have finished the
 // matmul whose tally `gbar` is.
@@ -439,6 +452,10 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
   for (int q = 0; q < NT; ++q)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[q][e] = 0.f;
+  // greedy-token keys of the logits this thread writes: tokens tt*8 + 2*s4 + j
+  unsigned long long best[NT][2];
+#pragma unroll
+  for (int q = 0; q < NT; ++q) best[q][0] = best[q][1] = 0ull;
 
   // ldmatrix lane addressing: matrix mi = lane/8 covers rows 8*(mi&1).. of
   // chunk (mi>>1) of the group; per-lane offsets (groups 0-3 of box 0; box 1
@@ -653,8 +670,10 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
                 const int row = row0 + ((e & 2) ? 8 : 0);
                 if (n < p.M && row < op.N) {
                   const size_t idx = (size_t)n * op.N + row;
-                  if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = acc[tt][e];
+                  if (!op.y) {
+                  } else if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = acc[tt][e];
                   else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(acc[tt][e]);
+                  if (p.amax) best[tt][e & 1] = umax64(best[tt][e & 1], amax_key(acc[tt][e], row));
                 }
               }
           }
@@ -669,8 +688,10 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
               const int row = row0 + ((e & 2) ? 8 : 0);
               if (n < p.M && row < op.N) {
                 const size_t idx = (size_t)n * op.N + row;
-                if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = acc[tt][e];
+                if (!op.y) {
+                } else if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = acc[tt][e];
                 else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(acc[tt][e]);
+                if (p.amax) best[tt][e & 1] = umax64(best[tt][e & 1], amax_key(acc[tt][e], row));
               }
             }
         }
@@ -746,8 +767,10 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
                 const int row = rowf + ((e & 2) ? 8 : 0);
                 if (n < p.M && row < op.N) {
                   const size_t idx = (size_t)n * op.N + row;
-                  if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = tot[tt][e];
+                  if (!op.y) {
+                  } else if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = tot[tt][e];
                   else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(tot[tt][e]);
+                  if (p.amax) best[tt][e & 1] = umax64(best[tt][e & 1], amax_key(tot[tt][e], row));
                 }
               }
           }
@@ -772,6 +795,28 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
         atomicAdd(p.gbar + o, 1u);
       }
       asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+    }
+  }
+  if (p.amax) {
+    // Greedy token: reduce the keys over the warp (lanes of one s4 share
+    // tokens), then over the consumer warps through shared memory (the
+    // cluster receive buffer is idle by now), then one atomicMax per token.
+    unsigned long long* red = reinterpret_cast<unsigned long long*>(smem + Cfg::OFF_RECV);
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        unsigned long long v = best[tt][j];
+#pragma unroll
+        for (int o2 = 4; o2 < 32; o2 <<= 1) v = umax64(v, __shfl_xor_sync(0xffffffffu, v, o2));
+        if (r == 0) red[cw * Cfg::MPAD + tt * 8 + 2 * s4 + j] = v;
+      }
+    asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+    const int tid = cw * 32 + lane;
+    if (tid < p.M) {
+      unsigned long long v = 0ull;
+      for (int q = 0; q < Cfg::CW; ++q) v = umax64(v, red[q * Cfg::MPAD + tid]);
+      if (!*abort_flag && v != 0ull) atomicMax(p.amax + tid, v);
     }
   }
 }
@@ -881,6 +926,7 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   p.counter = reinterpret_cast<unsigned int*>(base + kGbarBytes);
   p.part = reinterpret_cast<float*>(base + kGbarBytes + kCounterBytes);
   p.status = a.status;
+  p.amax = a.amax;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.G);

@@ -66,6 +66,23 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     return out
 
 
+def quantized_matmul_argmax(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: Optional[torch.Tensor],
+                            group_size: int = 64, bits: int = 4, mode: str = "affine",
+                            logits: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Greedy token per row of x: argmax over the fp16 logits x @ dequantize(w).T
+    (project_logits then argmax_last_axis, qwen3_5.rs:1038, lib.rs:2055).
+    Returns uint32 indices as int64 (torch has no uint32 arithmetic); pass
+    ``logits`` to also receive the fp16 logits (required above 16 rows)."""
+    M = x.numel() // x.shape[-1]
+    idx = torch.empty(M, dtype=torch.int32, device=x.device)
+    L = _lib.load()
+    ia = _arr(idx)
+    ia.contents.dtype = _lib.QW_U32
+    _lib.check(L.qw_quantized_matmul_argmax(_arr(x), _arr(w), _arr(scales), _arr(biases), group_size, bits,
+                                            _mode(mode), _arr(logits), ia, _stream(x)))
+    return idx.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+
+
 def quantized_matmul_chain(ops, group_size: int = 64, bits: int = 4, mode: str = "affine") -> None:
     """Runs [(x, w, scales, biases, y), ...] in order, each y = x @ dequantize(w).T
     written into its preallocated ``y``; an op's x may be an earlier op's y.
