@@ -209,7 +209,8 @@ class QuantizedTensors:
         from .ops import QuantizedLinear
 
         def dev(a, dt):
-            return torch.from_numpy(np.ascontiguousarray(a).view(dt)).to(device)
+            # the memory-mapped views are read-only: stage a writable host copy
+            return torch.from_numpy(np.require(a, requirements=["C", "W"]).view(dt)).to(device)
 
         wq = dev(self.weight, np.int32)
         s = dev(self.scales, np.float16)
