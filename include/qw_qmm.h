@@ -18,10 +18,11 @@
  *    cxx bridge as std::terminate, crates/mlxcel-core/src/layers.rs:1255-1285),
  *    so the checks it performs at load time (layers.rs:1286-1318, :1409-1440,
  *    :1783-1868) are performed here on every call instead.
- *  - Supported quantization: mode "affine", bits 4, group_size 64, activations
- *    and scales/biases fp16 (the Qwen 27B checkpoint, crates/runtime/src/
- *    qwen3_5.rs:208-211).  Other combinations MLX accepts return
- *    QW_EUNSUPPORTED.
+ *  - Supported quantization: mode "affine" with fp16 activations and
+ *    scales/biases; bits 4 in groups of 64 (the Qwen 27B checkpoint,
+ *    crates/runtime/src/qwen3_5.rs:208-211) and the per-tensor overrides'
+ *    bits 4 or 8 in groups of 64 or 128 (qwen3_next.rs:39-74).  Other
+ *    combinations MLX accepts return QW_EUNSUPPORTED.
  */
 #ifndef QW_QMM_H
 #define QW_QMM_H

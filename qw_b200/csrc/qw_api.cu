@@ -264,11 +264,15 @@ int check_quant_params(const char* mode, bool has_biases, int group_size, int bi
   if (bits < 1 || bits > 32) return fail(QW_EINVAL, "bits must be between 1 and 32");
   if (group_size < 1 || group_size > (1 << 20)) return fail(QW_EINVAL, "group_size must be between 1 and 2^20");
   if (!affine) return fail(QW_EUNSUPPORTED, std::string("quantization mode \"") + mode + "\" is not supported");
-  if (bits != 4 || group_size != 64)
-    return fail(QW_EUNSUPPORTED, "only bits=4, group_size=64 affine quantization is supported (got bits=" +
+  if ((bits != 4 && bits != 8) || (group_size != 64 && group_size != 128))
+    return fail(QW_EUNSUPPORTED, "affine quantization is supported with bits 4 or 8 and group_size 64 or 128 (got bits=" +
                                      std::to_string(bits) + ", group_size=" + std::to_string(group_size) + ")");
   return QW_OK;
 }
+
+// The checkpoint's configuration (4-bit, groups of 64) has the skinny decode
+// kernel; the other supported ones run on the tensor-core kernel at every M.
+bool skinny_config(int group_size, int bits) { return bits == 4 && group_size == 64; }
 
 struct WeightDims {
   int64_t N, K, G;
@@ -345,10 +349,12 @@ int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const 
   const bool y32 = y->dtype == QW_F32;
   const size_t ysz = y32 ? 4 : 2;
 
-  if (M > 16 && prefill_available()) {
+  if ((M > 16 || !skinny_config(group_size, bits)) && prefill_available()) {
     PrefillArgs pa{x->data, (const uint32_t*)w->data, scales->data, biases->data, y->data, y32, M, d.N, d.K,
                    res->status};
     pa.x_ld = x_ld;
+    pa.bits = bits;
+    pa.group_size = group_size;
     ce = launch_prefill(pa, stream, pdl_enabled(), &err);
     if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "prefill launch") : fail(QW_ECUDA, err);
     return QW_OK;
@@ -445,7 +451,7 @@ int qw_quantized_matmul_chain(const qw_qmm_op* ops, int n_ops, int group_size, i
                                  " rows of x, op 0 has " + std::to_string(args[0].M));
   }
   const int64_t M = args[0].M;
-  if (M > 16 || args[0].M == 0) {
+  if (M > 16 || args[0].M == 0 || !skinny_config(group_size, bits)) {
     // Prefill-sized (or empty) chains: one launch per matmul, in order.
     for (int i = 0; i < n_ops; ++i) {
       const qw_qmm_op& o = ops[i];
@@ -511,8 +517,10 @@ int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_ar
   if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
   cudaStream_t stream = as_stream(stream_v);
   std::string err;
-  if (M > 16) {
-    if (!logits) return fail(QW_EINVAL, "a logits buffer is required when x has more than 16 rows");
+  if (M > 16 || !skinny_config(group_size, bits)) {
+    if (!logits)
+      return fail(QW_EINVAL, "a logits buffer is required when x has more than 16 rows or the weights are not "
+                             "4-bit in groups of 64");
     if ((rc = run_qmm(x, w, scales, biases, 1, group_size, bits, mode, logits, stream_v))) return rc;
     ce = launch_argmax_rows(logits->data, M, d.N, (uint32_t*)idx->data, stream);
     return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "argmax launch");

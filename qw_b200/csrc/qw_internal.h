@@ -86,6 +86,8 @@ struct PrefillArgs {
   int64_t M, N, K;
   unsigned int* status;
   int64_t x_ld = 0;  // elements from one row of x to the next (0 = K)
+  int bits = 4;          // 4 or 8
+  int group_size = 64;   // 64 or 128
 };
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err);
 bool prefill_available();

@@ -36,13 +36,19 @@ constexpr int BM = 128;       // weight rows per tile (UMMA M, TMEM lanes)
 constexpr int BT = 256;       // tokens per tile (UMMA N)
 constexpr int STAGES = 4;     // pipeline depth (x box, packed W, TMEM A)
 constexpr int X_STAGE = BT * 128;          // 32 KB
-constexpr int WP_STAGE = BM * 32;          // 4 KB
 constexpr int OFF_X = 0;
-constexpr int OFF_WP = STAGES * X_STAGE;
-constexpr int OFF_BAR = OFF_WP + STAGES * WP_STAGE;
 // barriers: xfull, wpfull, wpempty, afull, aempty (per stage), dfull, dempty
 constexpr int NBAR = 5 * STAGES + 2;
-constexpr int SMEM = OFF_BAR + NBAR * 8 + 64 + 1024;
+// Packed codes of one 64-wide k block: BITS/2 words (4-bit: 8, 8-bit: 16) per row.
+template <int BITS>
+struct PfCfg {
+  static constexpr int WP_ROW = kGroup * BITS / 8;   // bytes per row per k block
+  static constexpr int WORDS = kGroup * BITS / 32;   // packed words per row per k block
+  static constexpr int WP_STAGE = BM * WP_ROW;
+  static constexpr int OFF_WP = STAGES * X_STAGE;
+  static constexpr int OFF_BAR = OFF_WP + STAGES * WP_STAGE;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 64 + 1024;
+};
 constexpr int DQW = 8;             // dequant / epilogue warps: 2 per TMEM lane quarter
 constexpr int THREADS = (2 + DQW) * 32;
 constexpr uint32_t TMEM_COLS = 512;  // D: 256 columns, A stages: 4 x 32
@@ -51,7 +57,9 @@ constexpr uint32_t A_COL = 256;
 
 struct PrefillParams {
   int M, N, K;
-  int n_tiles, m_tiles, groups;
+  int n_tiles, m_tiles, groups;  // groups: 64-wide k blocks
+  int gsh;                       // k blocks per quantization group (group_size / 64)
+  int sb_groups;                 // quantization groups per row (K / group_size)
   int y_f32;
   void* y;
   const __half* scales;
@@ -96,12 +104,14 @@ __device__ __forceinline__ void dequant_group_slow(const uint32_t (&wd)[4], __ha
   }
 }
 
+template <int BITS>
 __global__ void __launch_bounds__(THREADS, 1)
     qmm_prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                        const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  using Cfg = PfCfg<BITS>;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
   uint64_t* xfull = bars;
   uint64_t* wpfull = bars + STAGES;
   uint64_t* wpempty = bars + 2 * STAGES;
@@ -163,8 +173,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           mbar_arrive_expect_tx(&xfull[s], X_STAGE);
           tma_load_2d(smem + OFF_X + s * X_STAGE, &tm_x, &xfull[s], g * kGroup, mt * BT);
-          mbar_arrive_expect_tx(&wpfull[s], WP_STAGE);
-          tma_load_2d_hint(smem + OFF_WP + s * WP_STAGE, &tm_w, &wpfull[s], g * 32, nt * BM, pol_w);
+          mbar_arrive_expect_tx(&wpfull[s], Cfg::WP_STAGE);
+          tma_load_2d_hint(smem + Cfg::OFF_WP + s * Cfg::WP_STAGE, &tm_w, &wpfull[s], g * Cfg::WP_ROW, nt * BM,
+                           pol_w);
         }
       }
     }
@@ -215,54 +226,88 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int nt = tile / p.m_tiles, mt = tile % p.m_tiles;
       const int row = nt * BM + row_in_tile;
       const bool row_ok = row < p.N;
-      const __half* srow = p.scales + (size_t)(row_ok ? row : 0) * p.groups;
-      const __half* brow = p.biases + (size_t)(row_ok ? row : 0) * p.groups;
-      // This warp dequantizes every other group of the tile in full (the other
-      // warp of its lane quarter takes the rest), so each warp has two MMA
-      // group-times per group of its own.
-      __half s_next = (row_ok && khalf < p.groups) ? srow[khalf] : __float2half(0.f);
-      __half b_next = (row_ok && khalf < p.groups) ? brow[khalf] : __float2half(0.f);
+      const __half* srow = p.scales + (size_t)(row_ok ? row : 0) * p.sb_groups;
+      const __half* brow = p.biases + (size_t)(row_ok ? row : 0) * p.sb_groups;
+      // This warp dequantizes every other k block of the tile in full (the
+      // other warp of its lane quarter takes the rest), so each warp has two
+      // MMA block-times per block of its own.
+      __half s_next = (row_ok && khalf < p.groups) ? srow[khalf / p.gsh] : __float2half(0.f);
+      __half b_next = (row_ok && khalf < p.groups) ? brow[khalf / p.gsh] : __float2half(0.f);
       for (int g = khalf; g < p.groups; g += 2) {
         const uint32_t it = tile_count * (uint32_t)p.groups + (uint32_t)g;
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
         const __half sc = s_next, bi = b_next;
-        if (g + 2 < p.groups && row_ok) {  // prefetch this warp's next group's scale/bias
-          s_next = srow[g + 2];
-          b_next = brow[g + 2];
+        if (g + 2 < p.groups && row_ok) {  // prefetch this warp's next block's scale/bias
+          s_next = srow[(g + 2) / p.gsh];
+          b_next = brow[(g + 2) / p.gsh];
         }
         if (!*abort_flag && !mbar_wait(&wpfull[s], ph, p.status, kDevTimeoutFull)) *abort_flag = 1;
-        uint32_t wd[2][4];
+        uint32_t wd[Cfg::WORDS];
         {
-          const uint4* src = reinterpret_cast<const uint4*>(smem + OFF_WP + s * WP_STAGE + row_in_tile * 32);
-          const uint4 a0 = src[0], a1 = src[1];
-          wd[0][0] = a0.x; wd[0][1] = a0.y; wd[0][2] = a0.z; wd[0][3] = a0.w;
-          wd[1][0] = a1.x; wd[1][1] = a1.y; wd[1][2] = a1.z; wd[1][3] = a1.w;
+          const uint4* src =
+              reinterpret_cast<const uint4*>(smem + Cfg::OFF_WP + s * Cfg::WP_STAGE + row_in_tile * Cfg::WP_ROW);
+#pragma unroll
+          for (int i = 0; i < Cfg::WORDS / 4; ++i) {
+            const uint4 a = src[i];
+            wd[4 * i] = a.x; wd[4 * i + 1] = a.y; wd[4 * i + 2] = a.z; wd[4 * i + 3] = a.w;
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&wpempty[s]);
-        // dequantize the group's 64 codes into 32 fp16 pairs (k ascending)
+        // dequantize the block's 64 codes into 32 fp16 pairs (k ascending)
         uint32_t out[2][16];
         const float sf = __half2float(sc);
-        const bool fast = fabsf(sf) >= 0.0009765625f && fabsf(sf) < 63.0f;  // s/16 exact, 1024 s finite
-        if (fast) {
-          const __half s16 = __float2half_rn(sf * 0.0625f);  // exact: s >= 2^-10
-          const uint32_t s2 = h2_bits(__halves2half2(sc, s16));
-          const uint32_t c2 = h2_bits(__halves2half2(__float2half_rn(-1024.f * sf), __float2half_rn(-64.f * sf)));
-          const uint32_t b2 = h2_bits(__halves2half2(bi, bi));
+        const uint32_t b2 = h2_bits(__halves2half2(bi, bi));
+        if (BITS == 4) {
+          const bool fast = fabsf(sf) >= 0.0009765625f && fabsf(sf) < 63.0f;  // s/16 exact, 1024 s finite
+          if (fast) {
+            const __half s16 = __float2half_rn(sf * 0.0625f);  // exact: s >= 2^-10
+            const uint32_t s2 = h2_bits(__halves2half2(sc, s16));
+            const uint32_t c2 =
+                h2_bits(__halves2half2(__float2half_rn(-1024.f * sf), __float2half_rn(-64.f * sf)));
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh)
+            for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
+              for (int i = 0; i < 4; ++i) {
 #pragma unroll
-              for (int pp = 0; pp < 4; ++pp) {
-                const uint32_t t = prmt(wd[hh][i], 0x64646464u, 0x4040u + 0x0101u * pp) & 0xFFF0FF0Fu;
-                out[hh][4 * i + pp] = hadd2_rn(hfma2_rn(t, s2, c2), b2);
+                for (int pp = 0; pp < 4; ++pp) {
+                  const uint32_t t = prmt(wd[4 * hh + i], 0x64646464u, 0x4040u + 0x0101u * pp) & 0xFFF0FF0Fu;
+                  out[hh][4 * i + pp] = hadd2_rn(hfma2_rn(t, s2, c2), b2);
+                }
               }
-            }
+          } else {
+            uint32_t w0[4] = {wd[0], wd[1], wd[2], wd[3]}, w1[4] = {wd[4], wd[5], wd[6], wd[7]};
+            dequant_group_slow(w0, sc, bi, out[0]);
+            dequant_group_slow(w1, sc, bi, out[1]);
+          }
         } else {
-          dequant_group_slow(wd[0], sc, bi, out[0]);
-          dequant_group_slow(wd[1], sc, bi, out[1]);
+          // 8-bit: a word holds 4 codes; prmt pairs them with 0x64 into
+          // (1024 + q_even, 1024 + q_odd), and fma with (s, s), (-1024 s,
+          // -1024 s) rounds s*q once from the exact product.
+          const bool fast = fabsf(sf) < 63.0f;  // 1024 s finite
+          if (fast) {
+            const uint32_t s2 = h2_bits(__halves2half2(sc, sc));
+            const __half c = __float2half_rn(-1024.f * sf);
+            const uint32_t c2 = h2_bits(__halves2half2(c, c));
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const uint32_t t0 = prmt(wd[i], 0x64646464u, 0x5140u);
+              const uint32_t t1 = prmt(wd[i], 0x64646464u, 0x5342u);
+              out[i / 8][2 * (i % 8)] = hadd2_rn(hfma2_rn(t0, s2, c2), b2);
+              out[i / 8][2 * (i % 8) + 1] = hadd2_rn(hfma2_rn(t1, s2, c2), b2);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+#pragma unroll
+              for (int pp = 0; pp < 2; ++pp) {
+                const uint32_t q0 = (wd[i] >> (16 * pp)) & 0xFFu, q1 = (wd[i] >> (16 * pp + 8)) & 0xFFu;
+                const __half t0 = __hmul_rn(sc, __uint2half_rn(q0));
+                const __half t1 = __hmul_rn(sc, __uint2half_rn(q1));
+                out[i / 8][2 * (i % 8) + pp] = h2_bits(__halves2half2(__hadd_rn(t0, bi), __hadd_rn(t1, bi)));
+              }
+          }
         }
         // write A stage s once the MMAs that read it last have completed
         if (it >= STAGES && !*abort_flag && !mbar_wait(&aempty[s], ph ^ 1, p.status, kDevTimeoutEmpty))
@@ -314,13 +359,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 bool prefill_available() { return true; }
 
-cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err) {
+namespace {
+template <int BITS>
+cudaError_t launch_cfg(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err) {
+  using Cfg = PfCfg<BITS>;
   int dev = 0;
   cudaGetDevice(&dev);
   const DeviceInfo& di = device_info(dev);
   static thread_local int configured_dev = -1;
   if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(qmm_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    cudaError_t e =
+        cudaFuncSetAttribute(qmm_prefill_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
@@ -329,6 +378,8 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, 
   p.N = (int)a.N;
   p.K = (int)a.K;
   p.groups = (int)(a.K / kGroup);
+  p.gsh = a.group_size / kGroup;
+  p.sb_groups = (int)(a.K / a.group_size);
   p.n_tiles = (int)((a.N + BM - 1) / BM);
   p.m_tiles = (int)((a.M + BT - 1) / BT);
   p.y_f32 = a.y_f32 ? 1 : 0;
@@ -338,25 +389,34 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, 
   p.status = a.status;
   CUtensorMap tx, tw;
   if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
-                      (uint64_t)(a.x_ld ? a.x_ld : a.K) * 2,
-                      kGroup, BT, CU_TENSOR_MAP_SWIZZLE_128B, err))
+                      (uint64_t)(a.x_ld ? a.x_ld : a.K) * 2, kGroup, BT, CU_TENSOR_MAP_SWIZZLE_128B, err))
     return cudaErrorInvalidValue;
-  if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
-                      (uint64_t)(a.K / 2), 32, BM, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+  const uint64_t row_bytes = (uint64_t)a.K * BITS / 8;
+  if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.N, row_bytes, Cfg::WP_ROW, BM,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, err))
     return cudaErrorInvalidValue;
   const int tiles = p.n_tiles * p.m_tiles;
   int grid = di.sm_count < tiles ? di.sm_count : tiles;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = SMEM;
+  cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, qmm_prefill_kernel, tx, tw, p);
+  return cudaLaunchKernelEx(&cfg, qmm_prefill_kernel<BITS>, tx, tw, p);
+}
+}  // namespace
+
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err) {
+  if ((a.bits != 4 && a.bits != 8) || (a.group_size != 64 && a.group_size != 128) || a.K % a.group_size) {
+    *err = "the prefill kernel takes 4- or 8-bit codes in groups of 64 or 128";
+    return cudaErrorInvalidValue;
+  }
+  return a.bits == 4 ? launch_cfg<4>(a, stream, pdl, err) : launch_cfg<8>(a, stream, pdl, err);
 }
 
 }  // namespace qw

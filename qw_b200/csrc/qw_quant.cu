@@ -1,5 +1,6 @@
-// qw_quant.cu -- affine 4-bit group-64 dequantize / quantize kernels and the
-// small elementwise epilogues of the linear-forward entry points.
+// qw_quant.cu -- affine dequantize / quantize kernels (4- or 8-bit codes,
+// groups of 64 or 128) and the small elementwise epilogues of the
+// linear-forward entry points.
 //
 // dequantize is bit-exact with the oracle under both roundings: every fp16
 // product and sum goes through an explicitly rounded (.rn) f16x2 instruction.
@@ -14,42 +15,62 @@ namespace qw {
 
 namespace {
 
-// One thread per packed word: 8 outputs (16 bytes) per thread.
+// One packed word of 8-bit codes (4 codes, k ascending from bit 0) of a group
+// with scale pair s2 and bias pair b2: 4 fp16 weights as 2 words.
 template <bool kRoundOnce>
+__device__ __forceinline__ uint2 dequant_word8(uint32_t w, uint32_t s2, uint32_t b2) {
+  uint2 o;
+  // (q_even, q_odd) exact: prmt makes (1024 + q, 1024 + q'), minus 1024
+  const uint32_t q01 = hsub2_rn(prmt(w, 0x64646464u, 0x5140u), 0x64006400u);
+  const uint32_t q23 = hsub2_rn(prmt(w, 0x64646464u, 0x5342u), 0x64006400u);
+  o.x = kRoundOnce ? hfma2_rn(q01, s2, b2) : hadd2_rn(hmul2_rn(q01, s2), b2);
+  o.y = kRoundOnce ? hfma2_rn(q23, s2, b2) : hadd2_rn(hmul2_rn(q23, s2), b2);
+  return o;
+}
+
+// One thread per packed word: 8 (4-bit) or 4 (8-bit) outputs per thread.
+template <bool kRoundOnce, int BITS>
 __global__ void dequantize_kernel(const uint32_t* __restrict__ w, const __half* __restrict__ scales,
-                                  const __half* __restrict__ biases, uint4* __restrict__ out, int64_t N,
-                                  int64_t words_per_row, int64_t groups) {
+                                  const __half* __restrict__ biases, void* __restrict__ out, int64_t N,
+                                  int64_t words_per_row, int64_t groups, int words_per_group) {
   const int64_t total = N * words_per_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = i / words_per_row;
     const int64_t kw = i - n * words_per_row;
-    const int64_t g = kw / 8;  // 8 words per group of 64
+    const int64_t g = kw / words_per_group;
     const __half s = scales[n * groups + g];
     const __half b = biases[n * groups + g];
     const uint32_t s2 = (uint32_t)__half_as_ushort(s) * 0x10001u;
     const uint32_t b2 = (uint32_t)__half_as_ushort(b) * 0x10001u;
-    out[i] = dequant_word<kRoundOnce>(__ldg(w + i), s2, b2);
+    if (BITS == 4) reinterpret_cast<uint4*>(out)[i] = dequant_word<kRoundOnce>(__ldg(w + i), s2, b2);
+    else reinterpret_cast<uint2*>(out)[i] = dequant_word8<kRoundOnce>(__ldg(w + i), s2, b2);
   }
 }
 
-// One thread per group of 64 weights.
-__global__ void quantize_kernel(const uint4* __restrict__ w, uint4* __restrict__ wq, __half* __restrict__ scales,
+// One thread per group of GS weights (GS = 64 or 128, BITS = 4 or 8).  Two
+// passes over the group's fp16 values (min/max, then codes), both from L1.
+template <int BITS, int GS>
+__global__ void quantize_kernel(const __half* __restrict__ w, uint32_t* __restrict__ wq, __half* __restrict__ scales,
                                 __half* __restrict__ biases, int64_t ngroups) {
+  constexpr int PF = 32 / BITS;                // codes per word
+  constexpr float NBINS = (float)((1 << BITS) - 1);
   for (int64_t gidx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; gidx < ngroups;
        gidx += (int64_t)gridDim.x * blockDim.x) {
-    uint4 v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __ldg(w + gidx * 8 + i);
-    const __half* h = reinterpret_cast<const __half*>(v);
+    const uint4* src = reinterpret_cast<const uint4*>(w + gidx * GS);
     float mn = __int_as_float(0x7f800000), mx = -__int_as_float(0x7f800000);
+#pragma unroll 4
+    for (int i = 0; i < GS / 8; ++i) {
+      const uint4 v = __ldg(src + i);
+      const __half* h = reinterpret_cast<const __half*>(&v);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const float f = __half2float(h[i]);
-      if (f < mn) mn = f;
-      if (f > mx) mx = f;
+      for (int j = 0; j < 8; ++j) {
+        const float f = __half2float(h[j]);
+        if (f < mn) mn = f;
+        if (f > mx) mx = f;
+      }
     }
-    float scale = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+    float scale = __fdiv_rn(__fsub_rn(mx, mn), NBINS);
     if (!(scale >= 1e-7f)) scale = 1e-7f;
     const __half sh = __float2half_rn(scale);
     const __half bh = __float2half_rn(mn);
@@ -57,21 +78,21 @@ __global__ void quantize_kernel(const uint4* __restrict__ w, uint4* __restrict__
     const float bf = __half2float(bh);
     scales[gidx] = sh;
     biases[gidx] = bh;
-    uint32_t words[8];
+    uint32_t* dst = wq + gidx * (GS / PF);
+#pragma unroll 4
+    for (int i = 0; i < GS / 8; ++i) {  // 8 values: one 4-bit word or two 8-bit words
+      const uint4 v = __ldg(src + i);
+      const __half* h = reinterpret_cast<const __half*>(&v);
+      uint32_t word[8 / PF + (PF > 8 ? 1 : 0)] = {};
 #pragma unroll
-    for (int wi = 0; wi < 8; ++wi) {
-      uint32_t word = 0;
-#pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        const float f = __half2float(h[wi * 8 + p]);
-        float r = rintf(__fdiv_rn(__fsub_rn(f, bf), sf));
-        r = fminf(fmaxf(r, 0.0f), 15.0f);
-        word |= ((uint32_t)r) << (4 * p);
+      for (int j = 0; j < 8; ++j) {
+        float r = rintf(__fdiv_rn(__fsub_rn(__half2float(h[j]), bf), sf));
+        r = fminf(fmaxf(r, 0.0f), NBINS);
+        word[j / PF] |= ((uint32_t)r) << (BITS * (j % PF));
       }
-      words[wi] = word;
+#pragma unroll
+      for (int k = 0; k < 8 / PF; ++k) dst[i * (8 / PF) + k] = word[k];
     }
-    wq[gidx * 2] = make_uint4(words[0], words[1], words[2], words[3]);
-    wq[gidx * 2 + 1] = make_uint4(words[4], words[5], words[6], words[7]);
   }
 }
 
@@ -105,29 +126,40 @@ int grid_for(int64_t work, int threads) {
 
 cudaError_t launch_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N,
                               int64_t K, int group_size, int bits, int rounding, cudaStream_t stream) {
-  if (group_size != 64 || bits != 4) return cudaErrorInvalidValue;
-  const int64_t wpr = K / 8;
+  if ((bits != 4 && bits != 8) || (group_size != 64 && group_size != 128)) return cudaErrorInvalidValue;
+  const int64_t wpr = K * bits / 32;
   const int64_t total = N * wpr;
   if (total == 0) return cudaSuccess;
   const int threads = 256;
   const int blocks = grid_for(total, threads);
-  if (rounding == 1)
-    dequantize_kernel<true><<<blocks, threads, 0, stream>>>(w, (const __half*)scales, (const __half*)biases,
-                                                            (uint4*)out, N, wpr, K / 64);
-  else
-    dequantize_kernel<false><<<blocks, threads, 0, stream>>>(w, (const __half*)scales, (const __half*)biases,
-                                                             (uint4*)out, N, wpr, K / 64);
+  const int wpg = group_size * bits / 32;
+  const __half* sp = (const __half*)scales;
+  const __half* bp = (const __half*)biases;
+  const int64_t G = K / group_size;
+  if (bits == 4) {
+    if (rounding == 1) dequantize_kernel<true, 4><<<blocks, threads, 0, stream>>>(w, sp, bp, out, N, wpr, G, wpg);
+    else dequantize_kernel<false, 4><<<blocks, threads, 0, stream>>>(w, sp, bp, out, N, wpr, G, wpg);
+  } else {
+    if (rounding == 1) dequantize_kernel<true, 8><<<blocks, threads, 0, stream>>>(w, sp, bp, out, N, wpr, G, wpg);
+    else dequantize_kernel<false, 8><<<blocks, threads, 0, stream>>>(w, sp, bp, out, N, wpr, G, wpg);
+  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_quantize(const void* w, uint32_t* wq, void* scales, void* biases, int64_t N, int64_t K,
                             int group_size, int bits, cudaStream_t stream) {
-  if (group_size != 64 || bits != 4) return cudaErrorInvalidValue;
-  const int64_t ngroups = N * (K / 64);
+  if ((bits != 4 && bits != 8) || (group_size != 64 && group_size != 128)) return cudaErrorInvalidValue;
+  const int64_t ngroups = N * (K / group_size);
   if (ngroups == 0) return cudaSuccess;
   const int threads = 128;
-  quantize_kernel<<<grid_for(ngroups, threads), threads, 0, stream>>>((const uint4*)w, (uint4*)wq,
-                                                                       (__half*)scales, (__half*)biases, ngroups);
+  const int blocks = grid_for(ngroups, threads);
+  const __half* wp = (const __half*)w;
+  __half* sp = (__half*)scales;
+  __half* bp = (__half*)biases;
+  if (bits == 4 && group_size == 64) quantize_kernel<4, 64><<<blocks, threads, 0, stream>>>(wp, wq, sp, bp, ngroups);
+  else if (bits == 4) quantize_kernel<4, 128><<<blocks, threads, 0, stream>>>(wp, wq, sp, bp, ngroups);
+  else if (group_size == 64) quantize_kernel<8, 64><<<blocks, threads, 0, stream>>>(wp, wq, sp, bp, ngroups);
+  else quantize_kernel<8, 128><<<blocks, threads, 0, stream>>>(wp, wq, sp, bp, ngroups);
   return cudaGetLastError();
 }
 

@@ -35,12 +35,12 @@
 // host threads -- race on the array and may return wrong results.  Calls on
 // one stream are ordered and safe.
 //
-// Limits: 16 rows of x per call (the skinny kernel's tile), and the scratch
-// that the shape needs on this device at most kStaticScratchBytes minus the
-// status word (the split-tile counters, 4 bytes per 128 output rows up to
-// 256 KiB, plus two partial-sum slots of 128 x 16 floats per SM).  On a
-// 148-SM B200 a call needs at most 2.6 MiB.  Larger requests return
-// QW_EUNSUPPORTED with a message.
+// Limits: 4-bit weights in groups of 64 (the skinny kernel), 16 rows of x per
+// call (its tile), and the scratch that the shape needs on this device at
+// most kStaticScratchBytes minus the status word (a 256-byte header, the
+// split-tile counters, 4 bytes per 128 output rows up to 256 KiB, plus two
+// partial-sum slots of 128 x 16 floats per SM).  On a 148-SM B200 a call needs
+// at most 2.6 MiB.  Other requests return QW_EUNSUPPORTED with a message.
 //
 // Errors: like qw_quantized_matmul's, except for a kernel that gives up on one
 // of its bounded waits: it records the cause in a status word at the start of
@@ -108,6 +108,8 @@ extern "C" int qw_quantized_matmul_static_scratch(const qw_array* x, const qw_ar
   int rc = check_qmm_call(x, w, scales, biases, transpose, group_size, bits, mode, y, &sa);
   if (rc != QW_OK) return rc;
   if (sa.M == 0 || sa.N == 0) return QW_OK;
+  if (bits != 4 || group_size != 64)
+    return static_fail(QW_EUNSUPPORTED, "qw_quantized_matmul_static_scratch takes 4-bit weights in groups of 64");
   if (sa.M > kStaticMaxRows)
     return static_fail(QW_EUNSUPPORTED, "qw_quantized_matmul_static_scratch takes at most " +
                                             std::to_string(kStaticMaxRows) + " rows of x per call, got " +

@@ -96,9 +96,11 @@ def test_biases_with_block_float_mode_rejected():
 
 @pytest.mark.parametrize("bits,gs,code", [(0, 64, _lib.QW_EINVAL), (33, 64, _lib.QW_EINVAL),
                                           (4, 0, _lib.QW_EINVAL), (4, (1 << 20) + 1, _lib.QW_EINVAL),
-                                          (8, 64, _lib.QW_EUNSUPPORTED), (4, 128, _lib.QW_EUNSUPPORTED)])
+                                          (2, 64, _lib.QW_EUNSUPPORTED), (4, 32, _lib.QW_EUNSUPPORTED),
+                                          (6, 64, _lib.QW_EUNSUPPORTED), (8, 256, _lib.QW_EUNSUPPORTED)])
 def test_bits_and_group_bounds(bits, gs, code):
-    """Bounds of layers.rs:1286-1318; in-range values other than 4/64 are unsupported."""
+    """Bounds of layers.rs:1286-1318; in-range values other than bits 4/8 with
+    groups of 64/128 are unsupported."""
     x, w, s, b, y = std_args()
     assert _qmm(x, w, s, b, gs=gs, bits=bits, y=y) == code
 

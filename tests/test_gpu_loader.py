@@ -36,13 +36,24 @@ def test_loaded_linears_match_the_oracle(tmp_path, cuda_dev):
             assert rel_err(y.float().cpu().numpy(), y_ref) <= TOL, (prefix, M)
 
 
-def test_unsupported_override_fails_loudly(tmp_path, cuda_dev):
-    wq, s, b = oracle.quantize(synth.weight_fp16(64, 512, seed=1), group_size=64, bits=8)
-    loader.write_safetensors(str(tmp_path / "model.safetensors"),
-                             {"g.weight": wq, "g.scales": s, "g.biases": b})
+def test_overrides_run_or_fail_loudly(tmp_path, cuda_dev):
+    """An 8-bit override runs through the kernels; a 2-bit one (which MLX
+    accepts and this library does not implement) raises QW_EUNSUPPORTED."""
+    w8 = oracle.quantize(synth.weight_fp16(64, 512, seed=1), group_size=64, bits=8)
+    w2 = oracle.quantize(synth.weight_fp16(64, 512, seed=2), group_size=64, bits=2)
+    loader.write_safetensors(str(tmp_path / "model.safetensors"), {
+        "g8.weight": w8[0], "g8.scales": w8[1], "g8.biases": w8[2],
+        "g2.weight": w2[0], "g2.scales": w2[1], "g2.biases": w2[2]})
     (tmp_path / "config.json").write_text(json.dumps({"quantization": {
-        "group_size": 64, "bits": 4, "mode": "affine", "g": {"group_size": 64, "bits": 8}}}))
-    lin = loader.Checkpoint(str(tmp_path)).quantized("g").to_device()
+        "group_size": 64, "bits": 4, "mode": "affine",
+        "g8": {"group_size": 64, "bits": 8}, "g2": {"group_size": 64, "bits": 2}}}))
+    ck = loader.Checkpoint(str(tmp_path))
+    x = synth.activations(3, 512, seed=3)
+    y = ck.quantized("g8").to_device()(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    _, y_ref = oracle.quantized_matmul(x, *w8, group_size=64, bits=8, want_f32=True)
+    assert rel_err(y.float().cpu().numpy(), y_ref) <= TOL
+    lin = ck.quantized("g2").to_device()
     with pytest.raises(_lib.QwError) as e:
         lin(torch.zeros(1, 512, dtype=torch.float16, device="cuda"))
     assert e.value.code == _lib.QW_EUNSUPPORTED

@@ -132,6 +132,36 @@ def test_packing_invariant_is_enforced():
 
 
 # ------------------------------------------------------------- restatements
+@pytest.mark.parametrize("bits,gs", [(8, 64), (4, 128), (8, 128)])
+def test_restatements_agree_for_other_configs(bits, gs):
+    """The 8-bit and group-128 configurations of the per-tensor overrides."""
+    N, K = 40, 768
+    w = synth.weight_fp16(N, K, seed=bits + gs)
+    wq, s, b = oracle.quantize(w, group_size=gs, bits=bits)
+    wq2, s2, b2 = np_ref.quantize(w, group_size=gs, bits=bits)
+    np.testing.assert_array_equal(wq, wq2)
+    np.testing.assert_array_equal(s.view(np.uint16), s2.view(np.uint16))
+    np.testing.assert_array_equal(b.view(np.uint16), b2.view(np.uint16))
+    for r, name in ((oracle.ROUND_TWICE, "twice"), (oracle.ROUND_ONCE, "once")):
+        np.testing.assert_array_equal(
+            oracle.dequantize(wq, s, b, group_size=gs, bits=bits, rounding=r).view(np.uint16),
+            np_ref.dequantize(wq, s, b, group_size=gs, bits=bits, rounding=name).view(np.uint16))
+    x = synth.activations(3, K, seed=2)
+    _, y32 = oracle.quantized_matmul(x, wq, s, b, group_size=gs, bits=bits, want_f32=True)
+    assert rel_err(y32, np_ref.quantized_matmul(x, wq, s, b, group_size=gs, bits=bits)) < 1e-5
+
+
+def test_eight_bit_code_order_known_answer():
+    """8-bit codes: element k of a row is byte k % 4 of word k / 4."""
+    wq = np.array([[0x04030201, 0xFF00807F]], dtype=np.uint32)  # k = 0..7
+    s = np.array([[1.0]], dtype=np.float16)
+    b = np.array([[0.0]], dtype=np.float16)
+    wq64 = np.tile(wq, (1, 8))  # 64 codes
+    d = oracle.dequantize(wq64, s, b, group_size=64, bits=8)
+    assert d[0, :8].tolist() == [1, 2, 3, 4, 127, 128, 0, 255]
+
+
+# -------------------------------------------------------------------------
 @pytest.mark.parametrize("N,K", [(8, 64), (33, 256), (100, 640), (17, 1024)])
 def test_c_and_numpy_restatements_agree(N, K):
     w = synth.weight_fp16(N, K, seed=11)
