@@ -5,12 +5,15 @@ Headline (BASELINE metric "4-bit qmatmul HBM GB/s & % peak at M=1/16; 27B
 linear-stack tok/s"): decode tokens/s of the 64-layer Qwen 27B linear stack at
 M=1 (q|k|v 5120->8192, o 6144->5120, gate|up 5120->34816, down 17408->5120 per
 layer, then lm_head 5120->151936), synthetic seeded weights quantized on the
-GPU by the library's own quantizer.  One step = one token through the stack.
+GPU by the library's own quantizer.  The MLP's gate|up projection runs with
+its SwiGLU activation fused (qw_quantized_matmul_swiglu), so down consumes
+silu(gate) * up as in the model.  One step = one token through the stack.
 
   value   device-resident inputs, the step captured once as a CUDA graph of
           the library's launches (programmatic dependent launch between them)
   e2e     the same step through the public C ABI call by call (qw_quantized_matmul
-          via ctypes), x copied from pinned host memory before and the logits
+          and qw_quantized_matmul_swiglu via ctypes), x copied from pinned host
+          memory before and the logits
           read back after, every step
 Extra keys report the single-matrix qmv (M=1) and verify qmm (M=16) GB/s with
 L2 defeated by rotating weight copies, and the M=16 stack.
@@ -157,10 +160,13 @@ def build_stack(torch, qw, P, rank, layers, dev):
 class StackRunner:
     """Fixed buffers + the per-step launch sequence, for graph capture and eager e2e.
 
-    chain=False issues one qw_quantized_matmul per linear (the drop-in path);
-    chain=True hands each run of consecutive linears with nothing in between
-    (the whole stack on one GPU; qkv+o and gate_up+down between allreduces
-    under tensor parallelism) to qw_quantized_matmul_chain."""
+    Per layer: qkv, o, the MLP's gate and up projections with SwiGLU fused
+    (qw_quantized_matmul_swiglu over the two row halves of the rank's gate_up
+    shard), down; then lm_head.  chain=False issues one C-ABI call per
+    linear (the drop-in path); chain=True hands each run of plain matmuls
+    with nothing in between (down of one layer with qkv and o of the next on
+    one GPU; qkv+o between allreduces under tensor parallelism) to
+    qw_quantized_matmul_chain."""
 
     def __init__(self, torch, qw, ws, lm, M, P, group, chain=False):
         self.torch, self.qw, self.ws, self.lm, self.M, self.P, self.group = torch, qw, ws, lm, M, P, group
@@ -173,8 +179,8 @@ class StackRunner:
         ngu = tp.shard_shape(synth.layer_linears()[2], P)[0]
         self.qkv = torch.empty(M, nq, dtype=f16, device=dev)
         self.attn = torch.empty(M, synth.Q_OUT // P, dtype=f16, device=dev)
-        self.gu = torch.empty(M, ngu, dtype=f16, device=dev)
-        self.gate = torch.empty(M, synth.INTER // P, dtype=f16, device=dev)
+        self.gate = torch.empty(M, ngu // 2, dtype=f16, device=dev)  # silu(gate) * up, down's input
+        self.halves = [tuple(t for half in tp.gate_up_halves(w["gate_up"]) for t in half) for w in ws]
         self.part = torch.empty(M, H, dtype=f32, device=dev)
         self.o = torch.empty(M, H, dtype=f16, device=dev)
         self.logits = torch.empty(M, lm[0].shape[0], dtype=f16, device=dev)
@@ -183,29 +189,38 @@ class StackRunner:
             self._build_segments()
 
     def _build_segments(self):
-        """Runs of matmuls separated by the tensor-parallel allreduces."""
-        q_view = self.qkv[:, : self.attn.shape[1]]   # row-strided views: no copies
-        g_view = self.gu[:, : self.gate.shape[1]]
-        segs, cur = [], []
-        for w in self.ws:
+        """The step as actions: ("chain", ops) runs of plain matmuls,
+        ("swiglu", layer) the fused MLP input projections, ("reduce", dst)
+        the tensor-parallel allreduce of the fp32 partials into dst."""
+        q_view = self.qkv[:, : self.attn.shape[1]]   # row-strided view: no copy
+        acts, cur = [], []
+
+        def flush():
+            if cur:
+                acts.append(("chain", list(cur)))
+                cur.clear()
+
+        for l, w in enumerate(self.ws):
             cur.append((self.h, *w["qkv"], self.qkv))
             if self.P == 1:
                 cur.append((q_view, *w["o"], self.o))
             else:
                 cur.append((q_view, *w["o"], self.part))
-                segs.append((cur, self.o))
-                cur = []
-            cur.append((self.o, *w["gate_up"], self.gu))
+                flush()
+                acts.append(("reduce", self.o))
+            flush()
+            acts.append(("swiglu", l))
             if self.P == 1:
-                cur.append((g_view, *w["down"], self.h))
+                cur.append((self.gate, *w["down"], self.h))
             else:
-                cur.append((g_view, *w["down"], self.part))
-                segs.append((cur, self.h))
-                cur = []
+                cur.append((self.gate, *w["down"], self.part))
+                flush()
+                acts.append(("reduce", self.h))
         cur.append((self.h, *self.lm, self.logits))
-        segs.append((cur, None))
-        self.segments = segs
-        self.launches_per_step = sum((len(c) + 23) // 24 for c, _ in segs)
+        flush()
+        self.actions = acts
+        self.launches_per_step = sum((len(a[1]) + 23) // 24 if a[0] == "chain" else 1
+                                     for a in acts if a[0] != "reduce")
 
     def _mm(self, x, w, out):
         self.qw.quantized_matmul(x, w[0], w[1], w[2], out=out)
@@ -218,16 +233,22 @@ class StackRunner:
         self.torch.distributed.all_reduce(self.part, group=self.group)
         out16.copy_(self.part)
 
+    def _swiglu(self, x, l, out):
+        self.qw.quantized_matmul_swiglu(x, *self.halves[l], out=out)
+
     def step(self):
         if self.chain:
-            for ops, reduced_into in self.segments:
-                self.qw.quantized_matmul_chain(ops)
-                if reduced_into is not None:
+            for a in self.actions:
+                if a[0] == "chain":
+                    self.qw.quantized_matmul_chain(a[1])
+                elif a[0] == "swiglu":
+                    self._swiglu(self.o, a[1], self.gate)
+                else:
                     self.torch.distributed.all_reduce(self.part, group=self.group)
-                    reduced_into.copy_(self.part)
+                    a[1].copy_(self.part)
             return
         M = self.M
-        for w in self.ws:
+        for l, w in enumerate(self.ws):
             self._mm(self.h, w["qkv"], self.qkv)
             if M == 1:
                 attn = self.qkv[:, : self.attn.shape[1]]
@@ -235,13 +256,8 @@ class StackRunner:
                 self.attn.copy_(self.qkv[:, : self.attn.shape[1]])
                 attn = self.attn
             self._rowpar(attn, w["o"], self.o)
-            self._mm(self.o, w["gate_up"], self.gu)
-            if M == 1:
-                gate = self.gu[:, : self.gate.shape[1]]
-            else:
-                self.gate.copy_(self.gu[:, : self.gate.shape[1]])
-                gate = self.gate
-            self._rowpar(gate, w["down"], self.h)
+            self._swiglu(self.o, l, self.gate)
+            self._rowpar(self.gate, w["down"], self.h)
         self._mm(self.h, self.lm, self.logits)
 
 
@@ -452,7 +468,7 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "f16 activations, u4 weights, f32 accumulate",
         "data": "synthetic: x~N(0,1), W~N(0,0.02) fp16 quantized on GPU (affine, 4-bit, group 64)",
-        "config": {"workload": f"decode linear stack M=1, {args.layers} layers (qkv/o/gate_up/down) + lm_head",
+        "config": {"workload": f"decode linear stack M=1, {args.layers} layers (qkv/o/gate_up+SwiGLU/down) + lm_head",
                    "M": 1, "layers": args.layers, "hidden": synth.HIDDEN, "vocab": synth.VOCAB,
                    "parallelism": f"tp{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (weights %.2f GB per step)" % (synth.stack_bytes(1, args.layers) / 1e9),
@@ -523,12 +539,15 @@ def run_reference(args):
     for _ in range(args.steps):
         for lin in lins:
             wq, s, b = mats[lin.name]
-            oracle.quantized_matmul(x[lin.K], wq[:rows], s[:rows], b[:rows], nthreads=threads)
+            y = oracle.quantized_matmul(x[lin.K], wq[:rows], s[:rows], b[:rows], nthreads=threads)
+            if lin.name == "gate_up":  # the MLP activation on the slab's gate and up halves
+                oracle.swiglu(y[:, : rows // 2], y[:, rows // 2:])
             nbytes += synth.algorithmic_bytes(1, rows, lin.K)
     dt = time.perf_counter() - t0
     gbs = nbytes / dt / 1e9
     tok_s = gbs * 1e9 / synth.stack_bytes(1, args.layers)
-    sample = (f"{rows} rows of each of qkv/o/gate_up/down per step through the C oracle (OpenMP, {threads} threads); "
+    sample = (f"{rows} rows of each of qkv/o/gate_up/down per step through the C oracle (OpenMP, {threads} threads), "
+              f"SwiGLU on the gate_up slab; "
               f"tok/s = GB/s / {synth.stack_bytes(1, args.layers)} bytes per token")
     out = {
         "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": "tok/s", "n_gpus": world,

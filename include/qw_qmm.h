@@ -108,6 +108,40 @@ int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_ar
                                const qw_array* biases, int group_size, int bits, const char* mode, qw_array* logits,
                                qw_array* idx, void* stream);
 
+/* SwiGLU input projections of a dense MLP, activation fused:
+ *   y = silu(g) * u,  g = x @ dequantize(w_gate).T,  u = x @ dequantize(w_up).T,
+ * evaluated as the reference does on fp16 arrays: g and u rounded to fp16,
+ * then sigmoid(g), g * sigmoid(g) and the product with u each rounded to fp16.
+ * Gate and up have the same shape [I, K*bits/32] and quantization; y is f16
+ * (or f32) [..., I].  A checkpoint whose gate and up are stored as one
+ * concatenated projection passes its two row halves as w_gate / w_up views.
+ * One kernel per call: a row tile holds 64 gate rows and the same 64 up
+ * rows, and only y is written.
+ * Replaces: Mlp::forward_hidden (crates/runtime/src/qwen3_next.rs:463-487:
+ * the gate and up quantized_matmul calls, or the fused projection and its two
+ * slices) followed by compiled_swiglu_activation (lib.rs:627,
+ * mlx_cxx_bridge.cpp:1205-1216, :1255-1265). */
+int qw_quantized_matmul_swiglu(const qw_array* x, const qw_array* w_gate, const qw_array* scales_gate,
+                               const qw_array* biases_gate, const qw_array* w_up, const qw_array* scales_up,
+                               const qw_array* biases_up, int transpose, int group_size, int bits, const char* mode,
+                               qw_array* y, void* stream);
+
+/* y = silu(gate) * up elementwise on f16 arrays of one shape, rounded to
+ * fp16 after each op as qw_quantized_matmul_swiglu's epilogue.
+ * Replaces: compiled_swiglu_activation (lib.rs:627, mlx_cxx_bridge.cpp:1255-1265)
+ * for gate and up computed apart (Mlp's Separate arm, qwen3_next.rs:465). */
+int qw_swiglu_activation(const qw_array* gate, const qw_array* up, qw_array* y, void* stream);
+
+/* Dense quantized SwiGLU MLP: y = (silu(x gate^T) * (x up^T)) @ dequantize(w_down).T,
+ * the intermediate held in a per-(device, stream) buffer the library keeps.
+ * All three projections share group_size, bits and mode.
+ * Replaces: compiled_moe_expert_forward (lib.rs:1636-1652,
+ * mlx_cxx_bridge.cpp:4203-4270) and Mlp::forward (qwen3_next.rs:458-461). */
+int qw_swiglu_mlp(const qw_array* x, const qw_array* w_gate, const qw_array* scales_gate, const qw_array* biases_gate,
+                  const qw_array* w_up, const qw_array* scales_up, const qw_array* biases_up, const qw_array* w_down,
+                  const qw_array* scales_down, const qw_array* biases_down, int group_size, int bits,
+                  const char* mode, qw_array* y, void* stream);
+
 /* As qw_quantized_matmul for at most 16 rows of x, for callers that must not
  * have the library allocate device memory during the call (a runtime that
  * owns all of the GPU's memory in its own pool; a decode loop that cannot

@@ -118,5 +118,28 @@ def quantized_matmul(x, wq, scales, biases, group_size: int = 64, bits: int = 4,
     return y
 
 
+def swiglu(gate, up):
+    """silu(gate) * up on fp16 arrays, rounded to fp16 after every op: the
+    reference's activation (mlx_cxx_bridge.cpp:1205-1216, silu_gate =
+    gate * sigmoid(gate); out = silu_gate * x) evaluated on its fp16 matmul
+    outputs, each elementwise op producing an fp16 array.  sigmoid is formed
+    in float32 and rounded once."""
+    g = np.asarray(gate, dtype=np.float16).astype(np.float32)
+    u = np.asarray(up, dtype=np.float16).astype(np.float32)
+    with np.errstate(over="ignore"):
+        sig = (np.float32(1.0) / (np.float32(1.0) + np.exp(-g))).astype(np.float16).astype(np.float32)
+    silu = (g * sig).astype(np.float16).astype(np.float32)
+    return (silu * u).astype(np.float16)
+
+
+def quantized_matmul_swiglu(x, gate, up, group_size: int = 64, bits: int = 4, nthreads: int = 0):
+    """silu(x . gate^T) * (x . up^T) with gate/up = (wq, scales, biases):
+    Mlp::forward_hidden (crates/runtime/src/qwen3_next.rs:463-487) as two
+    quantized matmuls (fp16 outputs) and the activation above."""
+    g = quantized_matmul(x, *gate, group_size=group_size, bits=bits, nthreads=nthreads)
+    u = quantized_matmul(x, *up, group_size=group_size, bits=bits, nthreads=nthreads)
+    return swiglu(g, u)
+
+
 def max_threads() -> int:
     return int(lib().qwo_max_threads())

@@ -5,12 +5,15 @@ tensor-parallel linear stack).
 The compute lives in libqwqmm.so (C ABI in include/qw_qmm.h); this package is
 the Python mirror of the reference's operator surface on torch tensors.
 """
-from .ops import (QuantizedLinear, dequantize, device_status, quantize_weights, quantized_linear_forward,
-                  quantized_linear_forward_global_scale, quantized_matmul, quantized_matmul_argmax,
-                  quantized_matmul_chain)
+from .ops import (QuantizedLinear, QuantizedMlp, compiled_moe_expert_forward, compiled_swiglu_activation, dequantize, device_status,
+                  quantize_weights, quantized_linear_forward, quantized_linear_forward_global_scale, quantized_matmul,
+                  quantized_matmul_argmax, quantized_matmul_chain, quantized_matmul_swiglu, swiglu_mlp)
 
 __all__ = [
     "QuantizedLinear",
+    "QuantizedMlp",
+    "compiled_moe_expert_forward",
+    "compiled_swiglu_activation",
     "dequantize",
     "device_status",
     "quantize_weights",
@@ -19,4 +22,6 @@ __all__ = [
     "quantized_matmul",
     "quantized_matmul_argmax",
     "quantized_matmul_chain",
+    "quantized_matmul_swiglu",
+    "swiglu_mlp",
 ]

@@ -316,14 +316,31 @@ int cuda_fail(cudaError_t e, const char* where) {
   return fail(QW_ECUDA, std::string(where) + ": " + cudaGetErrorString(e));
 }
 
-// Core of the matmul entry points.  y may be f16 or f32.
+// The up projection of a SwiGLU call (null for a plain matmul).
+struct UpProj {
+  const qw_array* w;
+  const qw_array* scales;
+  const qw_array* biases;
+};
+
+// Core of the matmul entry points.  y may be f16 or f32.  With `up`, w /
+// scales / biases are the gate projection and y = silu(x gate^T) * (x up^T).
 int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases, int transpose,
-            int group_size, int bits, const char* mode, qw_array* y, void* stream_v) {
+            int group_size, int bits, const char* mode, qw_array* y, void* stream_v, const UpProj* up = nullptr) {
   int rc;
   if ((rc = check_quant_params(mode, biases != nullptr, group_size, bits))) return rc;
+  if (up && (rc = check_quant_params(mode, up->biases != nullptr, group_size, bits))) return rc;
   if (!transpose) return fail(QW_EUNSUPPORTED, "transpose=false is not supported");
   WeightDims d;
   if ((rc = check_weights(w, scales, biases, group_size, bits, &d))) return rc;
+  if (up) {
+    WeightDims du;
+    if ((rc = check_weights(up->w, up->scales, up->biases, group_size, bits, &du))) return rc;
+    if (du.N != d.N || du.K != d.K)
+      return fail(QW_EINVAL, "gate and up projections must have the same shape (gate " + std::to_string(d.N) + "x" +
+                                 std::to_string(d.K) + ", up " + std::to_string(du.N) + "x" + std::to_string(du.K) +
+                                 ")");
+  }
   int64_t x_ld = 0;
   if ((rc = check_x_rows(x, d.K, &x_ld)) || (rc = check_array(y, "y"))) return rc;
   if (x->dtype != QW_F16) return fail(QW_EUNSUPPORTED, std::string("x must be float16, got ") + dtype_name(x->dtype));
@@ -355,6 +372,12 @@ int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const 
     pa.x_ld = x_ld;
     pa.bits = bits;
     pa.group_size = group_size;
+    if (up) {
+      pa.swiglu = true;
+      pa.w2 = (const uint32_t*)up->w->data;
+      pa.scales2 = up->scales->data;
+      pa.biases2 = up->biases->data;
+    }
     ce = launch_prefill(pa, stream, pdl_enabled(), &err);
     if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "prefill launch") : fail(QW_ECUDA, err);
     return QW_OK;
@@ -375,12 +398,45 @@ int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const 
     sa.K = d.K;
     sa.max_ctas = 0;
     sa.status = res->status;
+    if (up) {
+      sa.swiglu = true;
+      sa.w2 = (const uint32_t*)up->w->data;
+      sa.scales2 = up->scales->data;
+      sa.biases2 = up->biases->data;
+    }
     Scratch sc;
     if (!scratch_for(dev, stream, skinny_scratch_bytes(sa, dev), &sc, &err)) return fail(QW_ENOMEM, err);
     ce = launch_skinny(sa, sc, stream, pdl_enabled(), &err);
     if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "skinny launch") : fail(QW_ECUDA, err);
   }
   return QW_OK;
+}
+
+// Per-(device, stream) device buffer for an intermediate activation (the
+// MLP's silu(gate) * up), kept apart from the kernels' scratch.  Grows on
+// demand like the scratch.
+std::map<std::pair<int, cudaStream_t>, Scratch> g_act;
+
+bool activation_for(int device, cudaStream_t stream, size_t bytes, void** out, std::string* err) {
+  std::lock_guard<std::mutex> lock(g_res_mu);
+  Scratch& s = g_act[{device, stream}];
+  if (s.bytes < bytes) {
+    if (s.base) {
+      cudaStreamSynchronize(stream);
+      cudaFree(s.base);
+      s = Scratch{};
+    }
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      *err = "activation buffer allocation of " + std::to_string(bytes) + " bytes failed";
+      return false;
+    }
+    s.base = p;
+    s.bytes = bytes;
+  }
+  *out = s.base;
+  return true;
 }
 
 }  // namespace
@@ -551,6 +607,65 @@ int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_ar
   if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "skinny launch") : fail(QW_ECUDA, err);
   ce = launch_argmax_finalize(keys, (uint32_t*)idx->data, M, stream);
   return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "argmax launch");
+}
+
+int qw_quantized_matmul_swiglu(const qw_array* x, const qw_array* w_gate, const qw_array* scales_gate,
+                               const qw_array* biases_gate, const qw_array* w_up, const qw_array* scales_up,
+                               const qw_array* biases_up, int transpose, int group_size, int bits, const char* mode,
+                               qw_array* y, void* stream) {
+  set_error("");
+  const UpProj up{w_up, scales_up, biases_up};
+  return run_qmm(x, w_gate, scales_gate, biases_gate, transpose, group_size, bits, mode, y, stream, &up);
+}
+
+int qw_swiglu_activation(const qw_array* gate, const qw_array* up, qw_array* y, void* stream) {
+  set_error("");
+  int rc;
+  if ((rc = check_array(gate, "gate")) || (rc = check_array(up, "up")) || (rc = check_array(y, "y"))) return rc;
+  if (gate->dtype != QW_F16 || up->dtype != QW_F16 || y->dtype != QW_F16)
+    return fail(QW_EUNSUPPORTED, "gate, up and y must be float16");
+  const int64_t n = numel(gate);
+  if (numel(up) != n || numel(y) != n || gate->ndim != up->ndim || gate->ndim != y->ndim)
+    return fail(QW_EINVAL, "gate, up and y must have the same shape");
+  for (int i = 0; i < gate->ndim; ++i)
+    if (gate->shape[i] != up->shape[i] || gate->shape[i] != y->shape[i])
+      return fail(QW_EINVAL, "gate, up and y must have the same shape");
+  const cudaError_t ce = launch_swiglu(gate->data, up->data, y->data, n, as_stream(stream));
+  return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "swiglu launch");
+}
+
+int qw_swiglu_mlp(const qw_array* x, const qw_array* w_gate, const qw_array* scales_gate, const qw_array* biases_gate,
+                  const qw_array* w_up, const qw_array* scales_up, const qw_array* biases_up, const qw_array* w_down,
+                  const qw_array* scales_down, const qw_array* biases_down, int group_size, int bits,
+                  const char* mode, qw_array* y, void* stream_v) {
+  set_error("");
+  int rc;
+  if ((rc = check_array(w_gate, "w_gate"))) return rc;
+  if (w_gate->ndim != 2) return fail(QW_EUNSUPPORTED, "w_gate must be 2-D [N, K*bits/32]");
+  if (!x) return fail(QW_EINVAL, "x is null");
+  if (x->ndim < 1 || x->ndim > 4) return fail(QW_EINVAL, "x must have 1 to 4 dimensions");
+  const int64_t inter = w_gate->shape[0];
+  const int64_t K = x->ndim ? x->shape[x->ndim - 1] : 0;
+  const int64_t M = K ? numel(x) / K : 0;
+  // h = silu(x gate^T) * (x up^T), [M, inter] fp16, in this stream's activation buffer
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  void* hbuf = nullptr;
+  std::string err;
+  const size_t hbytes = (size_t)(M * inter) * 2;
+  if (hbytes && !activation_for(dev, as_stream(stream_v), hbytes, &hbuf, &err)) return fail(QW_ENOMEM, err);
+  qw_array h{};
+  h.data = hbuf;
+  h.dtype = QW_F16;
+  h.ndim = 2;
+  h.shape[0] = M;
+  h.shape[1] = inter;
+  h.strides[0] = inter;
+  h.strides[1] = 1;
+  const UpProj up{w_up, scales_up, biases_up};
+  if ((rc = run_qmm(x, w_gate, scales_gate, biases_gate, 1, group_size, bits, mode, &h, stream_v, &up))) return rc;
+  return run_qmm(&h, w_down, scales_down, biases_down, 1, group_size, bits, mode, y, stream_v);
 }
 
 static int linear_common(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,

@@ -51,6 +51,13 @@ struct SkinnyArgs {
   unsigned int* status;  // device status word
   int64_t x_ld = 0;      // elements from one row of x to the next (0 = K)
   unsigned long long* amax = nullptr;  // greedy-token keys [M], zeroed by the caller (y may be null)
+  // SwiGLU (gate and up of an MLP, activation fused): w/scales/biases are the
+  // gate projection's, w2/scales2/biases2 the up projection's, both [N] rows,
+  // and y [M][N] = silu(x gate^T) * (x up^T).
+  bool swiglu = false;
+  const uint32_t* w2 = nullptr;
+  const void* scales2 = nullptr;
+  const void* biases2 = nullptr;
 };
 // Skinny-path scratch layout: split-tile counters (zero between launches) at
 // the start, then the partial-sum slots.
@@ -88,6 +95,11 @@ struct PrefillArgs {
   int64_t x_ld = 0;  // elements from one row of x to the next (0 = K)
   int bits = 4;          // 4 or 8
   int group_size = 64;   // 64 or 128
+  // SwiGLU, as in SkinnyArgs: w/scales/biases the gate, w2/scales2/biases2 the up projection
+  bool swiglu = false;
+  const uint32_t* w2 = nullptr;
+  const void* scales2 = nullptr;
+  const void* biases2 = nullptr;
 };
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err);
 bool prefill_available();
@@ -107,5 +119,7 @@ cudaError_t launch_quantize(const void* w, uint32_t* wq, void* scales, void* bia
 cudaError_t launch_affine_epilogue(void* y, const void* linear_bias, const float* global_scale, int64_t M,
                                    int64_t N, cudaStream_t stream);
 cudaError_t launch_f32_to_f16(const float* src, void* dst, int64_t n, cudaStream_t stream);
+// y = silu(gate) * up elementwise on n fp16 values.
+cudaError_t launch_swiglu(const void* gate, const void* up, void* y, int64_t n, cudaStream_t stream);
 
 }  // namespace qw

@@ -16,6 +16,12 @@
 //               with tcgen05.st.  After the last group of a tile they read D
 //               back (tcgen05.ld, half of the tokens each) and store y.
 //
+// SwiGLU (gate and up projections with the activation fused): a tile is 64
+// gate rows and the same 64 up rows, staged so that TMEM lanes l and l + 16
+// of each lane quarter hold one output's gate and up sums; the epilogue pairs
+// them with one shuffle per token and writes silu(gate) * up (64 outputs per
+// tile, each op rounded to fp16).
+//
 // The weights the MMA consumes are exactly qw_dequantize's (fp16(fp16(s*q)
 // + b)): pairs (1024 + q_even, 1024 + 16 q_odd) come from one prmt and one
 // and, fma.rn.f16x2 with (s, s/16) and (-1024 s, -64 s) gives fp16(s*q)
@@ -61,9 +67,13 @@ struct PrefillParams {
   int gsh;                       // k blocks per quantization group (group_size / 64)
   int sb_groups;                 // quantization groups per row (K / group_size)
   int y_f32;
+  int swiglu;      // gate (tm_w, scales, biases) and up (tm_w2, scales2, biases2), 64 rows of each per tile
+  int tile_rows;   // output rows per tile: 128, or 64 with swiglu
   void* y;
   const __half* scales;
   const __half* biases;
+  const __half* scales2;
+  const __half* biases2;
   unsigned int* status;
 };
 
@@ -107,7 +117,7 @@ __device__ __forceinline__ void dequant_group_slow(const uint32_t (&wd)[4], __ha
 template <int BITS>
 __global__ void __launch_bounds__(THREADS, 1)
     qmm_prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                       const PrefillParams p) {
+                       const __grid_constant__ CUtensorMap tm_w2, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   using Cfg = PfCfg<BITS>;
@@ -154,6 +164,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       prefetch_tensormap(&tm_x);
       prefetch_tensormap(&tm_w);
+      if (p.swiglu) prefetch_tensormap(&tm_w2);
       pdl_wait();
       const uint64_t pol_w = l2_policy_evict_last();
       uint32_t it = 0;
@@ -174,8 +185,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_arrive_expect_tx(&xfull[s], X_STAGE);
           tma_load_2d(smem + OFF_X + s * X_STAGE, &tm_x, &xfull[s], g * kGroup, mt * BT);
           mbar_arrive_expect_tx(&wpfull[s], Cfg::WP_STAGE);
-          tma_load_2d_hint(smem + Cfg::OFF_WP + s * Cfg::WP_STAGE, &tm_w, &wpfull[s], g * Cfg::WP_ROW, nt * BM,
-                           pol_w);
+          uint8_t* wp = smem + Cfg::OFF_WP + s * Cfg::WP_STAGE;
+          if (!p.swiglu) {
+            tma_load_2d_hint(wp, &tm_w, &wpfull[s], g * Cfg::WP_ROW, nt * BM, pol_w);
+          } else {  // 64 gate rows, then the same 64 up rows
+            tma_load_2d_hint(wp, &tm_w, &wpfull[s], g * Cfg::WP_ROW, nt * (BM / 2), pol_w);
+            tma_load_2d_hint(wp + (BM / 2) * Cfg::WP_ROW, &tm_w2, &wpfull[s], g * Cfg::WP_ROW, nt * (BM / 2), pol_w);
+          }
         }
       }
     }
@@ -218,16 +234,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int dw = warp - 2;                 // 0..7
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
     const int khalf = dw >> 2;               // which groups (even / odd) / which 128 tokens
-    const int row_in_tile = quarter * 32 + lane;
+    // The weight row this lane dequantizes into its TMEM lane (quarter * 32 +
+    // lane): the tile's row quarter * 32 + lane, or with SwiGLU, lanes 0-15
+    // of a quarter take gate rows 16 quarter + lane and lanes 16-31 the same
+    // rows' up projection (staged 64 rows further on), so lanes l and l + 16
+    // hold the two halves of one output.
+    const bool up_lane = p.swiglu && lane >= 16;
+    const int row_in_tile = p.swiglu ? quarter * 16 + (lane & 15) : quarter * 32 + lane;  // output row
+    const int smem_row = p.swiglu ? row_in_tile + (up_lane ? BM / 2 : 0) : row_in_tile;
+    const __half* scales = up_lane ? p.scales2 : p.scales;
+    const __half* biases = up_lane ? p.biases2 : p.biases;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     pdl_wait();
     uint32_t tile_count = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tile_count) {
       const int nt = tile / p.m_tiles, mt = tile % p.m_tiles;
-      const int row = nt * BM + row_in_tile;
+      const int row = nt * p.tile_rows + row_in_tile;
       const bool row_ok = row < p.N;
-      const __half* srow = p.scales + (size_t)(row_ok ? row : 0) * p.sb_groups;
-      const __half* brow = p.biases + (size_t)(row_ok ? row : 0) * p.sb_groups;
+      const __half* srow = scales + (size_t)(row_ok ? row : 0) * p.sb_groups;
+      const __half* brow = biases + (size_t)(row_ok ? row : 0) * p.sb_groups;
       // This warp dequantizes every other k block of the tile in full (the
       // other warp of its lane quarter takes the rest), so each warp has two
       // MMA block-times per block of its own.
@@ -246,7 +271,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t wd[Cfg::WORDS];
         {
           const uint4* src =
-              reinterpret_cast<const uint4*>(smem + Cfg::OFF_WP + s * Cfg::WP_STAGE + row_in_tile * Cfg::WP_ROW);
+              reinterpret_cast<const uint4*>(smem + Cfg::OFF_WP + s * Cfg::WP_STAGE + smem_row * Cfg::WP_ROW);
 #pragma unroll
           for (int i = 0; i < Cfg::WORDS / 4; ++i) {
             const uint4 a = src[i];
@@ -328,6 +353,30 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t v[16];
         tmem_ld_32x32b_x16(tmem + lane_base + D_COL + cb * 16, v);
         tmem_wait_ld();
+        if (p.swiglu) {
+          // lane l < 16 finishes tokens 0-7 of the block and lane l + 16
+          // tokens 8-15: each sends its partner the half the partner needs
+          float g[8], u[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float mine_lo = __uint_as_float(v[q]), mine_hi = __uint_as_float(v[q + 8]);
+            const float other = __shfl_xor_sync(0xffffffffu, up_lane ? mine_lo : mine_hi, 16);
+            g[q] = up_lane ? other : mine_lo;
+            u[q] = up_lane ? mine_hi : other;
+          }
+          if (!row_ok || *abort_flag) continue;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int tok = mt * BT + cb * 16 + (up_lane ? 8 : 0) + q;
+            if (tok < p.M) {
+              const size_t idx = (size_t)tok * p.N + row;
+              const float h = swiglu_f16(g[q], u[q]);
+              if (p.y_f32) reinterpret_cast<float*>(p.y)[idx] = h;
+              else reinterpret_cast<__half*>(p.y)[idx] = __float2half_rn(h);
+            }
+          }
+          continue;
+        }
         if (!row_ok || *abort_flag) continue;
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
@@ -380,20 +429,28 @@ cudaError_t launch_cfg(const PrefillArgs& a, cudaStream_t stream, bool pdl, std:
   p.groups = (int)(a.K / kGroup);
   p.gsh = a.group_size / kGroup;
   p.sb_groups = (int)(a.K / a.group_size);
-  p.n_tiles = (int)((a.N + BM - 1) / BM);
+  p.swiglu = a.swiglu ? 1 : 0;
+  p.tile_rows = a.swiglu ? BM / 2 : BM;
+  p.n_tiles = (int)((a.N + p.tile_rows - 1) / p.tile_rows);
   p.m_tiles = (int)((a.M + BT - 1) / BT);
   p.y_f32 = a.y_f32 ? 1 : 0;
   p.y = a.y;
   p.scales = reinterpret_cast<const __half*>(a.scales);
   p.biases = reinterpret_cast<const __half*>(a.biases);
+  p.scales2 = reinterpret_cast<const __half*>(a.swiglu ? a.scales2 : a.scales);
+  p.biases2 = reinterpret_cast<const __half*>(a.swiglu ? a.biases2 : a.biases);
   p.status = a.status;
-  CUtensorMap tx, tw;
+  CUtensorMap tx, tw, tw2;
   if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M,
                       (uint64_t)(a.x_ld ? a.x_ld : a.K) * 2, kGroup, BT, CU_TENSOR_MAP_SWIZZLE_128B, err))
     return cudaErrorInvalidValue;
   const uint64_t row_bytes = (uint64_t)a.K * BITS / 8;
-  if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.N, row_bytes, Cfg::WP_ROW, BM,
-                      CU_TENSOR_MAP_SWIZZLE_NONE, err))
+  if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.N, row_bytes, Cfg::WP_ROW,
+                      p.tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+    return cudaErrorInvalidValue;
+  tw2 = tw;  // unused unless SwiGLU
+  if (a.swiglu && !encode_tmap_2d(&tw2, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w2, row_bytes, (uint64_t)a.N, row_bytes,
+                                  Cfg::WP_ROW, p.tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE, err))
     return cudaErrorInvalidValue;
   const int tiles = p.n_tiles * p.m_tiles;
   int grid = di.sm_count < tiles ? di.sm_count : tiles;
@@ -407,7 +464,7 @@ cudaError_t launch_cfg(const PrefillArgs& a, cudaStream_t stream, bool pdl, std:
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, qmm_prefill_kernel<BITS>, tx, tw, p);
+  return cudaLaunchKernelEx(&cfg, qmm_prefill_kernel<BITS>, tx, tw, tw2, p);
 }
 }  // namespace
 

@@ -161,6 +161,19 @@ __device__ __forceinline__ uint32_t lop3_expand(uint32_t w) {
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "r"(0x000F000Fu), "r"(0x64006400u));
   return r;
 }
+// SwiGLU of one output, op by op as the reference evaluates it on fp16
+// arrays: gate and up rounded to fp16 (the two matmuls' outputs), then
+// sigmoid(gate), gate * sigmoid(gate) and that times up, each rounded to fp16.
+__device__ __forceinline__ float swiglu_f16(float g, float u) {
+  const float gh = __half2float(__float2half_rn(g));
+  const float uh = __half2float(__float2half_rn(u));
+  // exp clamped at e^80: the fast divide stays in range, and sigmoid there is
+  // below the smallest fp16 anyway
+  const float sg = __half2float(__float2half_rn(__fdividef(1.f, 1.f + __expf(fminf(-gh, 80.f)))));
+  const float silu = __half2float(__float2half_rn(gh * sg));
+  return __half2float(__float2half_rn(silu * uh));
+}
+
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));

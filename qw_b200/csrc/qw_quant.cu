@@ -115,6 +115,14 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ src, __half* __restr
     dst[i] = __float2half_rn(src[i]);
 }
 
+// y = silu(gate) * up on fp16 arrays, each op rounded to fp16 (the fused
+// kernels' epilogue, for gate and up computed apart).
+__global__ void swiglu_kernel(const __half* __restrict__ gate, const __half* __restrict__ up,
+                              __half* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = __float2half_rn(swiglu_f16(__half2float(gate[i]), __half2float(up[i])));
+}
+
 int grid_for(int64_t work, int threads) {
   int64_t blocks = (work + threads - 1) / threads;
   if (blocks > 148 * 16) blocks = 148 * 16;
@@ -169,6 +177,13 @@ cudaError_t launch_affine_epilogue(void* y, const void* linear_bias, const float
   const int threads = 256;
   affine_epilogue_kernel<<<grid_for(M * N, threads), threads, 0, stream>>>(
       (__half*)y, (const __half*)linear_bias, global_scale, M, N);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu(const void* gate, const void* up, void* y, int64_t n, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const int threads = 256;
+  swiglu_kernel<<<grid_for(n, threads), threads, 0, stream>>>((const __half*)gate, (const __half*)up, (__half*)y, n);
   return cudaGetLastError();
 }
 

@@ -21,10 +21,17 @@
 //   helper warps  turn the stage's x into the MMA B fragments every consumer
 //                 warp needs (permuted, odd k pre-scaled by 1/16) and the
 //                 per-group sums X and Z of the fold below.
-//   8 consumers   16 weight rows and all 8 groups of a unit each.  With up to
-//                 8 tokens a consumer copies unit j+1's weights out of the
-//                 ring group by group while it computes unit j, so a weight
-//                 slot is released one unit earlier.
+//   8 consumers   16 weight rows and all 8 groups of a unit each (rows
+//                 8c..8c+7 of each 64-row half of the tile for consumer c).
+//                 With up to 8 tokens a consumer copies unit j+1's weights
+//                 out of the ring group by group while it computes unit j,
+//                 so a weight slot is released one unit earlier.
+//
+// SwiGLU ops (an MLP's gate and up projections, activation fused): the top
+// half of a tile is 64 gate rows and the bottom half the same 64 up rows, so
+// each consumer lane ends with a gate sum and its up sum in registers and
+// writes silu(gate) * up, rounded to fp16 after each op as the reference's
+// fp16 arrays are; the 2I projection outputs are never stored.
 //
 // Consumer arithmetic (no per-element dequantisation): a packed word w holds
 // nibbles q0..q7 (k ascending).  lop3(w & 0x000F000F | 0x64006400) is the fp16
@@ -112,8 +119,15 @@ struct SkinnyCfg {
 
 // One quantized matmul of a launch.  The tensor maps live in the kernel's
 // parameter space (__grid_constant__), where TMA may read them.
+//
+// A SwiGLU op (swiglu = 1) is the gate and up projections of an MLP with the
+// activation fused into the epilogue: a tile is 64 gate rows (tm_w, tm_s,
+// tm_b) above the same 64 up rows (tm_w2, tm_s2, tm_b2), so the thread that
+// holds gate row i also holds up row i, and y = silu(gate) * up has N (the
+// intermediate width) columns.
 struct SkinnyOp {
   CUtensorMap tm_w, tm_s, tm_b, tm_x;
+  CUtensorMap tm_w2, tm_s2, tm_b2;  // SwiGLU: the up projection
   int N, K;
   int C;          // chunks along K
   int T;          // row tiles
@@ -121,9 +135,12 @@ struct SkinnyOp {
   int G;          // CTAs that take units of this matmul: the first min(grid, U)
   int sb_tma;     // scales/biases through TMA (needs K % 512 == 0)
   int y_f32;
+  int swiglu;
   void* y;
   const __half* scales;
   const __half* biases;
+  const __half* scales2;  // SwiGLU: the up projection's
+  const __half* biases2;
 };
 
 // A launch runs OPS_MAX >= n_ops matmuls in order, every CTA taking its share
@@ -279,6 +296,13 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
           prefetch_tensormap(&op.tm_s);
           prefetch_tensormap(&op.tm_b);
         }
+        if (op.swiglu) {
+          prefetch_tensormap(&op.tm_w2);
+          if (op.sb_tma) {
+            prefetch_tensormap(&op.tm_s2);
+            prefetch_tensormap(&op.tm_b2);
+          }
+        }
       }
       long long u0;
       const int nunits = units_of(o, &u0);
@@ -297,11 +321,13 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
           __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_WB);
           for (int e = lane; e < Cfg::BN * kGroupsPerStage; e += 32) {
             const int r = e / kGroupsPerStage, g = e % kGroupsPerStage;
-            const int row = t * Cfg::BN + r, grp = c * kGroupsPerStage + g;
+            const bool up = op.swiglu && r >= Cfg::BN / 2;
+            const int row = op.swiglu ? t * (Cfg::BN / 2) + (r % (Cfg::BN / 2)) : t * Cfg::BN + r;
+            const int grp = c * kGroupsPerStage + g;
             __half sv = __float2half(0.f), bv = __float2half(0.f);
             if (row < op.N && grp < G) {
-              sv = op.scales[(size_t)row * G + grp];
-              bv = op.biases[(size_t)row * G + grp];
+              sv = (up ? op.scales2 : op.scales)[(size_t)row * G + grp];
+              bv = (up ? op.biases2 : op.biases)[(size_t)row * G + grp];
             }
             ss[e] = sv;
             sb[e] = bv;
@@ -310,11 +336,31 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
         }
         if (lane == 0) {
           mbar_arrive_expect_tx(&wfull[slot], w_bytes);
-          tma_load_2d_hint(st, &op.tm_w, &wfull[slot], c * 256, t * Cfg::BN, pol_w);
-          tma_load_2d_hint(st + Cfg::W_BOX, &op.tm_w, &wfull[slot], c * 256 + 128, t * Cfg::BN, pol_w);
-          if (op.sb_tma) {
-            tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
-            tma_load_2d_hint(st + Cfg::OFF_WB, &op.tm_b, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
+          if (!op.swiglu) {
+            tma_load_2d_hint(st, &op.tm_w, &wfull[slot], c * 256, t * Cfg::BN, pol_w);
+            tma_load_2d_hint(st + Cfg::W_BOX, &op.tm_w, &wfull[slot], c * 256 + 128, t * Cfg::BN, pol_w);
+            if (op.sb_tma) {
+              tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WB, &op.tm_b, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
+            }
+          } else {
+            // 64 gate rows, then the same 64 up rows (boxes of 64 rows; the
+            // up half starts on a 1024-byte boundary, so the 128-byte swizzle
+            // pattern is the one a 128-row box would have)
+            constexpr int H = Cfg::BN / 2;
+            const int r0 = t * H;
+#pragma unroll
+            for (int bx = 0; bx < 2; ++bx) {
+              tma_load_2d_hint(st + bx * Cfg::W_BOX, &op.tm_w, &wfull[slot], c * 256 + bx * 128, r0, pol_w);
+              tma_load_2d_hint(st + bx * Cfg::W_BOX + H * 128, &op.tm_w2, &wfull[slot], c * 256 + bx * 128, r0,
+                               pol_w);
+            }
+            if (op.sb_tma) {
+              tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WS + H * 16, &op.tm_s2, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WB, &op.tm_b, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WB + H * 16, &op.tm_b2, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
+            }
           }
         }
         __syncwarp();
@@ -443,7 +489,10 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
 
   // ----------------------------------------------------------------- consumers
   const int cw = warp - 2 - Cfg::HW;
-  const int wrow = cw * 16;          // first row of this warp inside the tile
+  // This warp's 16 rows of a tile: rows wrow..wrow+7 of each half (MMA rows
+  // r and r + 8 of a lane are tile rows wrow + r and 64 + wrow + r), so in a
+  // SwiGLU tile a lane holds a gate row and its up row.
+  const int wrow = cw * 8;
   const int r = lane / 4, s4 = lane % 4;
   pdl_wait();
 
@@ -457,17 +506,52 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
 #pragma unroll
   for (int q = 0; q < NT; ++q) best[q][0] = best[q][1] = 0ull;
 
+  // y (and the greedy-token keys) of this lane's outputs of row tile `tile`
+  auto store_tile = [&](const SkinnyOp& op, int tile, const float (&v)[NT][4]) {
+    if (op.swiglu) {
+      const int row = tile * (Cfg::BN / 2) + wrow + r;  // gate in v[.][0..1], up in v[.][2..3]
+#pragma unroll
+      for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int n = tt * 8 + 2 * s4 + j;
+          if (n < p.M && row < op.N && op.y) {
+            const float h = swiglu_f16(v[tt][j], v[tt][j + 2]);
+            const size_t idx = (size_t)n * op.N + row;
+            if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = h;
+            else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(h);
+          }
+        }
+      return;
+    }
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int n = tt * 8 + 2 * s4 + (e & 1);
+        const int row = tile * Cfg::BN + wrow + r + ((e & 2) ? Cfg::BN / 2 : 0);
+        if (n < p.M && row < op.N) {
+          const size_t idx = (size_t)n * op.N + row;
+          if (!op.y) {
+          } else if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = v[tt][e];
+          else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(v[tt][e]);
+          if (p.amax) best[tt][e & 1] = umax64(best[tt][e & 1], amax_key(v[tt][e], row));
+        }
+      }
+  };
+
   // ldmatrix lane addressing: matrix mi = lane/8 covers rows 8*(mi&1).. of
   // chunk (mi>>1) of the group; per-lane offsets (groups 0-3 of box 0; box 1
   // adds W_BOX) hoisted out of the loop.
   const int lm_mi = lane / 8;
-  const int lm_row = wrow + (lane % 8) + 8 * (lm_mi & 1);
+  const int lm_row = wrow + (lane % 8) + (Cfg::BN / 2) * (lm_mi & 1);
   const int lm_sw = lm_row & 7;
   uint32_t lm_off[4];
 #pragma unroll
   for (int g4 = 0; g4 < 4; ++g4) lm_off[g4] = lm_row * 128 + (((g4 * 2 + (lm_mi >> 1)) ^ lm_sw) << 4);
-  // scale/bias rows r and r+8 of this warp, all 8 groups (16 bytes each)
+  // scale/bias rows of MMA rows r and r+8 of this warp, all 8 groups (16 bytes each)
   const uint32_t sb_off = (wrow + r) * 16;
+  constexpr uint32_t kSbHi = (Cfg::BN / 2) * 16;
   // B fragments: a lane whose token column is >= M reads token M-1's (a
   // shared-memory broadcast).  MMA output columns depend only on their own B
   // column, so those columns are never mixed into a written result.
@@ -516,9 +600,9 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
     for (int gi = 0; gi < 8; ++gi)
       ldmatrix_x4(wb + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
     sv_lo = lds128(wb + Cfg::OFF_WS + sb_off);
-    sv_hi = lds128(wb + Cfg::OFF_WS + sb_off + 8 * 16);
+    sv_hi = lds128(wb + Cfg::OFF_WS + sb_off + kSbHi);
     bv_lo = lds128(wb + Cfg::OFF_WB + sb_off);
-    bv_hi = lds128(wb + Cfg::OFF_WB + sb_off + 8 * 16);
+    bv_hi = lds128(wb + Cfg::OFF_WB + sb_off + kSbHi);
     release_wslot();
   };
   if (total > 0) copy_unit();
@@ -592,9 +676,9 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
       }
       if (has_next) {
         sv_lo = lds128(wb_next + Cfg::OFF_WS + sb_off);
-        sv_hi = lds128(wb_next + Cfg::OFF_WS + sb_off + 8 * 16);
+        sv_hi = lds128(wb_next + Cfg::OFF_WS + sb_off + kSbHi);
         bv_lo = lds128(wb_next + Cfg::OFF_WB + sb_off);
-        bv_hi = lds128(wb_next + Cfg::OFF_WB + sb_off + 8 * 16);
+        bv_hi = lds128(wb_next + Cfg::OFF_WB + sb_off + kSbHi);
         release_wslot();
       }
       __syncwarp();
@@ -613,7 +697,6 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
       if (!seg_end) continue;
       const bool whole = (seg_begin == 0) && (c == 0);
 
-      const int row0 = t_done * Cfg::BN + wrow + r;
       if (p.split > 1) {
         // Cluster split-K: this CTA's only segment.  Non-leaders store their
         // partial into the leader's shared memory and arrive on its barrier;
@@ -630,7 +713,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
             for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh) {
-                const int rl = wrow + r + 8 * hh;
+                const int rl = wrow + r + (Cfg::BN / 2) * hh;
                 const uint32_t a = rrecv + (rl * Cfg::MPAD + tt * 8 + 2 * s4) * 4;
                 asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(acc[tt][2 * hh]),
                              "f"(acc[tt][2 * hh + 1])
@@ -653,7 +736,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
               for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
-                  const int rl = wrow + r + 8 * hh;
+                  const int rl = wrow + r + (Cfg::BN / 2) * hh;
                   float2 v;
                   asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];"
                                : "=f"(v.x), "=f"(v.y)
@@ -662,39 +745,11 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
                   acc[tt][2 * hh + 1] += v.y;
                 }
             }
-#pragma unroll
-            for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int n = tt * 8 + 2 * s4 + (e & 1);
-                const int row = row0 + ((e & 2) ? 8 : 0);
-                if (n < p.M && row < op.N) {
-                  const size_t idx = (size_t)n * op.N + row;
-                  if (!op.y) {
-                  } else if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = acc[tt][e];
-                  else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(acc[tt][e]);
-                  if (p.amax) best[tt][e & 1] = umax64(best[tt][e & 1], amax_key(acc[tt][e], row));
-                }
-              }
+            store_tile(op, t_done, acc);
           }
         }
       } else if (whole) {
-        if (!*abort_flag) {
-#pragma unroll
-          for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int n = tt * 8 + 2 * s4 + (e & 1);
-              const int row = row0 + ((e & 2) ? 8 : 0);
-              if (n < p.M && row < op.N) {
-                const size_t idx = (size_t)n * op.N + row;
-                if (!op.y) {
-                } else if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = acc[tt][e];
-                else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(acc[tt][e]);
-                if (p.amax) best[tt][e & 1] = umax64(best[tt][e & 1], amax_key(acc[tt][e], row));
-              }
-            }
-        }
+        if (!*abort_flag) store_tile(op, t_done, acc);
       } else {
         // Split tile: publish this CTA's partial; the last contributor to
         // arrive adds the partials in CTA order.  A segment that is not this
@@ -710,7 +765,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int n = tt * 8 + 2 * s4 + (e & 1);
-              const int rl = wrow + r + ((e & 2) ? 8 : 0);
+              const int rl = wrow + r + ((e & 2) ? Cfg::BN / 2 : 0);
               mine[rl * Cfg::MPAD + n] = acc[tt][e];
             }
         }
@@ -753,27 +808,11 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const int n = tt * 8 + 2 * s4 + (e & 1);
-                const int rl = wrow + r + ((e & 2) ? 8 : 0);
+                const int rl = wrow + r + ((e & 2) ? Cfg::BN / 2 : 0);
                 tot[tt][e] += __ldcg(src + rl * Cfg::MPAD + n);
               }
           }
-          if (!*abort_flag) {
-            const int rowf = tf * Cfg::BN + wrow + r;
-#pragma unroll
-            for (int tt = 0; tt < NT; ++tt)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int n = tt * 8 + 2 * s4 + (e & 1);
-                const int row = rowf + ((e & 2) ? 8 : 0);
-                if (n < p.M && row < op.N) {
-                  const size_t idx = (size_t)n * op.N + row;
-                  if (!op.y) {
-                  } else if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = tot[tt][e];
-                  else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(tot[tt][e]);
-                  if (p.amax) best[tt][e & 1] = umax64(best[tt][e & 1], amax_key(tot[tt][e], row));
-                }
-              }
-          }
+          if (!*abort_flag) store_tile(op, tf, tot);
         }
       }
       // fin_flag and the partial slots are rewritten only after this barrier
@@ -834,20 +873,32 @@ bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
   op->N = (int)a.N;
   op->K = (int)a.K;
   op->C = (int)((a.K + kChunkK - 1) / kChunkK);
-  op->T = (int)((a.N + Cfg::BN - 1) / Cfg::BN);
+  // a SwiGLU tile holds 64 output rows (64 gate + 64 up weight rows)
+  const int tile_rows = a.swiglu ? Cfg::BN / 2 : Cfg::BN;
+  op->T = (int)((a.N + tile_rows - 1) / tile_rows);
   op->U = (long long)op->T * op->C;
   op->sb_tma = (a.K % kChunkK == 0) ? 1 : 0;
   op->y_f32 = a.y_f32 ? 1 : 0;
+  op->swiglu = a.swiglu ? 1 : 0;
   op->y = a.y;
   op->scales = reinterpret_cast<const __half*>(a.scales);
   op->biases = reinterpret_cast<const __half*>(a.biases);
+  op->scales2 = reinterpret_cast<const __half*>(a.swiglu ? a.scales2 : a.scales);
+  op->biases2 = reinterpret_cast<const __half*>(a.swiglu ? a.biases2 : a.biases);
   if ((size_t)op->T > kMaxCounters) {
     *err = "too many row tiles for the skinny path's counter block";
     return false;
   }
   if (!encode_tmap_2d(&op->tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
-                      (uint64_t)(a.K / 2), 128, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_128B, err))
+                      (uint64_t)(a.K / 2), 128, tile_rows, CU_TENSOR_MAP_SWIZZLE_128B, err))
     return false;
+  if (a.swiglu) {
+    if (!encode_tmap_2d(&op->tm_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w2, (uint64_t)(a.K / 2), (uint64_t)a.N,
+                        (uint64_t)(a.K / 2), 128, tile_rows, CU_TENSOR_MAP_SWIZZLE_128B, err))
+      return false;
+  } else {
+    op->tm_w2 = op->tm_w;  // unused
+  }
   {
     // x viewed as [K/64 groups][M tokens][64 halves]: one box = 8 groups x M tokens
     const uint64_t dims[3] = {(uint64_t)kGroup, (uint64_t)a.M, (uint64_t)(a.K / kGroup)};
@@ -857,17 +908,15 @@ bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
                         CU_TENSOR_MAP_SWIZZLE_128B, err))
       return false;
   }
+  op->tm_s = op->tm_b = op->tm_s2 = op->tm_b2 = op->tm_w;  // unused unless encoded below
   if (op->sb_tma) {
     const uint64_t G64 = (uint64_t)(a.K / kGroup);
-    if (!encode_tmap_2d(&op->tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.scales, G64, (uint64_t)a.N, G64 * 2,
-                        kGroupsPerStage, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
-      return false;
-    if (!encode_tmap_2d(&op->tm_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.biases, G64, (uint64_t)a.N, G64 * 2,
-                        kGroupsPerStage, Cfg::BN, CU_TENSOR_MAP_SWIZZLE_NONE, err))
-      return false;
-  } else {
-    op->tm_s = op->tm_w;  // unused
-    op->tm_b = op->tm_w;
+    const void* srcs[4] = {a.scales, a.biases, a.scales2, a.biases2};
+    CUtensorMap* maps[4] = {&op->tm_s, &op->tm_b, &op->tm_s2, &op->tm_b2};
+    for (int i = 0; i < (a.swiglu ? 4 : 2); ++i)
+      if (!encode_tmap_2d(maps[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, srcs[i], G64, (uint64_t)a.N, G64 * 2,
+                          kGroupsPerStage, tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+        return false;
   }
   return true;
 }
@@ -1013,7 +1062,8 @@ size_t skinny_scratch_bytes(const SkinnyArgs& a, int device) {
 
 size_t skinny_zeroed_bytes(const SkinnyArgs& a) {
   static_assert(SkinnyCfg<1>::BN == 128 && SkinnyCfg<8>::BN == 128 && SkinnyCfg<16>::BN == 128, "row tile");
-  const size_t tiles = (size_t)((a.N + 127) / 128);
+  const int64_t tile_rows = a.swiglu ? 64 : 128;
+  const size_t tiles = (size_t)((a.N + tile_rows - 1) / tile_rows);
   return kGbarBytes + (tiles < kMaxCounters ? tiles : kMaxCounters) * sizeof(unsigned int);
 }
 

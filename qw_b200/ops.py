@@ -99,6 +99,47 @@ def quantized_matmul_chain(ops, group_size: int = 64, bits: int = 4, mode: str =
     _lib.check(L.qw_quantized_matmul_chain(arr, len(ops), group_size, bits, _mode(mode), _stream(ops[0][0])))
 
 
+def quantized_matmul_swiglu(x: torch.Tensor, w_gate, scales_gate, biases_gate, w_up, scales_up, biases_up,
+                            group_size: int = 64, bits: int = 4, mode: str = "affine",
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """silu(x @ dequantize(gate).T) * (x @ dequantize(up).T) in one kernel: the
+    gate/up projections of Mlp::forward_hidden (qwen3_next.rs:463-487) and
+    compiled_swiglu_activation (mlx_cxx_bridge.cpp:1205-1216), with the
+    reference's fp16 rounding after each op."""
+    if out is None:
+        out = torch.empty(*x.shape[:-1], w_gate.shape[0], dtype=torch.float16, device=x.device)
+    L = _lib.load()
+    _lib.check(L.qw_quantized_matmul_swiglu(_arr(x), _arr(w_gate), _arr(scales_gate), _arr(biases_gate),
+                                            _arr(w_up), _arr(scales_up), _arr(biases_up), 1, group_size, bits,
+                                            _mode(mode), _arr(out), _stream(x)))
+    return out
+
+
+def compiled_swiglu_activation(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None):
+    """silu(gate) * up on fp16 tensors (lib.rs:627, mlx_cxx_bridge.cpp:1255)."""
+    if out is None:
+        out = torch.empty_like(gate)
+    _lib.check(_lib.load().qw_swiglu_activation(_arr(gate), _arr(up), _arr(out), _stream(gate)))
+    return out
+
+
+def swiglu_mlp(x: torch.Tensor, w_gate, scales_gate, biases_gate, w_up, scales_up, biases_up, w_down, scales_down,
+               biases_down, group_size: int = 64, bits: int = 4, mode: str = "affine",
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """down(silu(gate(x)) * up(x)) for quantized projections: the reference's
+    compiled_moe_expert_forward (lib.rs:1636-1652, mlx_cxx_bridge.cpp:4238)."""
+    if out is None:
+        out = torch.empty(*x.shape[:-1], w_down.shape[0], dtype=torch.float16, device=x.device)
+    L = _lib.load()
+    _lib.check(L.qw_swiglu_mlp(_arr(x), _arr(w_gate), _arr(scales_gate), _arr(biases_gate), _arr(w_up),
+                               _arr(scales_up), _arr(biases_up), _arr(w_down), _arr(scales_down),
+                               _arr(biases_down), group_size, bits, _mode(mode), _arr(out), _stream(x)))
+    return out
+
+
+compiled_moe_expert_forward = swiglu_mlp
+
+
 def quantized_linear_forward(x, w, scales, biases, linear_bias=None, group_size: int = 64, bits: int = 4,
                              mode: str = "affine", out=None) -> torch.Tensor:
     """Quantized linear layer forward (lib.rs:591-601)."""
@@ -185,5 +226,45 @@ class QuantizedLinear:
                                                          self.bits, self.mode, out=out)
         return quantized_linear_forward(x, self.weight, self.scales, self.biases, self.bias, self.group_size,
                                         self.bits, self.mode, out=out)
+
+    __call__ = forward
+
+
+class QuantizedMlp:
+    """Dense SwiGLU MLP over three QuantizedLinear projections, after the
+    reference's ``Mlp`` (qwen3_next.rs:449-487).  The gate and up projections
+    run as one fused kernel when ``fuse_mlp_input_projections``
+    (qwen3_next.rs:406-447) would fuse them: same group size, bits and mode,
+    no linear biases and no global scales; otherwise as two matmuls followed
+    by the activation (the reference's Separate arm).  A checkpoint that
+    stores them concatenated is split into two row views by ``from_fused``."""
+
+    def __init__(self, gate: QuantizedLinear, up: QuantizedLinear, down: QuantizedLinear):
+        self.gate, self.up, self.down = gate, up, down
+        self.fused = (gate.group_size == up.group_size and gate.bits == up.bits and gate.mode == up.mode
+                      and gate.bias is None and up.bias is None
+                      and gate.global_scale is None and up.global_scale is None
+                      and gate.out_features == up.out_features)
+
+    @classmethod
+    def from_fused(cls, gate_up: QuantizedLinear, intermediate_size: int, down: QuantizedLinear):
+        """Gate and up stored as one [2I, ...] projection (rows 0..I-1 gate)."""
+        def half(t, i):
+            return None if t is None else t[i * intermediate_size:(i + 1) * intermediate_size]
+        g = QuantizedLinear(half(gate_up.weight, 0), half(gate_up.scales, 0), half(gate_up.biases, 0),
+                            gate_up.group_size, gate_up.bits, gate_up.mode)
+        u = QuantizedLinear(half(gate_up.weight, 1), half(gate_up.scales, 1), half(gate_up.biases, 1),
+                            gate_up.group_size, gate_up.bits, gate_up.mode)
+        return cls(g, u, down)
+
+    def forward_hidden(self, x: torch.Tensor, out=None) -> torch.Tensor:
+        g, u = self.gate, self.up
+        if self.fused:
+            return quantized_matmul_swiglu(x, g.weight, g.scales, g.biases, u.weight, u.scales, u.biases,
+                                           g.group_size, g.bits, g.mode, out=out)
+        return compiled_swiglu_activation(g(x), u(x), out=out)
+
+    def forward(self, x: torch.Tensor, out=None) -> torch.Tensor:
+        return self.down(self.forward_hidden(x), out=out)
 
     __call__ = forward

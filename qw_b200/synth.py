@@ -76,9 +76,11 @@ def rng(seed: int, layer: int, tid: int) -> np.random.Generator:
     return np.random.default_rng([seed, layer, tid])
 
 
-def weight_fp16(N: int, K: int, seed: int = 0, layer: int = 0, tid: int = 0) -> np.ndarray:
+def weight_fp16(N: int, K: int, seed: int = 0, layer: int = 0, tid: int = 0, std: float = 0.02) -> np.ndarray:
+    """N x K fp16 ~ N(0, std).  std = K ** -0.5 keeps activations at unit
+    scale through a stack without norms (the SwiGLU stacks of the tests)."""
     g = rng(seed, layer, tid)
-    return (g.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+    return (g.standard_normal((N, K), dtype=np.float32) * np.float32(std)).astype(np.float16)
 
 
 def activations(M: int, K: int, seed: int = 0, tid: int = 99) -> np.ndarray:

@@ -116,22 +116,27 @@ def shard_shape(lin: synth.Linear, P: int) -> Tuple[int, int]:
 class LinearStack:
     """The decode linear stack on one rank: per layer qkv -> o -> gate_up ->
     down, then lm_head.  The stack keeps the data dependencies of a decoder
-    layer without its non-linear parts (attention, norms and SwiGLU are outside
-    this path): o consumes the rank's q plane of its qkv output, down consumes
-    the rank's gate plane of its gate_up output, and each layer's down output
-    is the next layer's input.
+    layer without attention and norms: o consumes the rank's q plane of its
+    qkv output, down consumes silu(gate) * up of the rank's gate and up planes
+    (or, without a `swiglu` callable, the gate plane as it is), and each
+    layer's down output is the next layer's input.
 
     `matmul(x, (wq, s, b), out_f32)` runs one quantized matmul; `allreduce(t)`
     sums an fp32 array over ranks and returns it; `to_half(t)` rounds fp32 to
-    fp16.  Row-parallel shards need every rank to run the same sequence of
-    collectives, which this fixed order guarantees.
+    fp16; `swiglu(x, (wq, s, b))` (optional) returns silu(gate) * up of the
+    rank's gate_up shard, whose first half of rows is its gate plane and
+    second half the matching up rows, so the activation needs no exchange
+    between ranks.  Row-parallel shards need every rank to run the same
+    sequence of collectives, which this fixed order guarantees.
     """
 
     def __init__(self, layers: Sequence[Dict[str, tuple]], lm_head: tuple, P: int, rank: int,
-                 matmul: Callable, allreduce: Callable, to_half: Callable, dims: StackDims = BASELINE):
+                 matmul: Callable, allreduce: Callable, to_half: Callable, dims: StackDims = BASELINE,
+                 swiglu: Callable = None):
         self.layers, self.lm_head = layers, lm_head
         self.P, self.rank, self.dims = P, rank, dims
         self.matmul, self.allreduce, self.to_half = matmul, allreduce, to_half
+        self.swiglu = swiglu
 
     def _rowpar(self, x, w):
         if self.P == 1:
@@ -143,6 +148,8 @@ class LinearStack:
         inter_local = self.dims.inter // self.P
         qkv = self.matmul(h, w["qkv"], False)
         o = self._rowpar(_contig(qkv[..., :q_local]), w["o"])
+        if self.swiglu is not None:
+            return self._rowpar(self.swiglu(o, w["gate_up"]), w["down"])
         gu = self.matmul(o, w["gate_up"], False)
         return self._rowpar(_contig(gu[..., :inter_local]), w["down"])
 
@@ -150,6 +157,12 @@ class LinearStack:
         for w in self.layers:
             h = self.layer(h, w)
         return self.matmul(h, self.lm_head, False)
+
+
+def gate_up_halves(w):
+    """(gate, up) triples of a rank's gate_up shard (rows: gate plane, then up)."""
+    n = w[0].shape[0] // 2
+    return tuple(t[:n] for t in w), tuple(t[n:] for t in w)
 
 
 def _contig(t):

@@ -195,8 +195,10 @@ def test_linear_forward_bias_and_global_scale():
 
 def test_invalid_call_raises_with_message():
     wq, s, b = quantized(64, 128)
-    with pytest.raises(qw_b200._lib.QwError, match="bits=8"):
-        qw_b200.quantized_matmul(dev(synth.activations(1, 128)), dev_u32(wq), dev(s), dev(b), bits=8)
+    # 2-bit codes: the packing matches (8 words of 16 codes per row) but the width is unsupported
+    with pytest.raises(qw_b200._lib.QwError, match="bits=2"):
+        qw_b200.quantized_matmul(dev(synth.activations(1, 128)), dev_u32(np.ascontiguousarray(wq[:, :8])),
+                                 dev(s), dev(b), bits=2)
 
 
 def test_split_tiles_across_changing_grids():

@@ -35,7 +35,8 @@ def _free_port():
 def _weights():
     layers = []
     for l in range(LAYERS):
-        layers.append({lin.name: oracle.quantize(synth.weight_fp16(lin.N, lin.K, seed=3, layer=l, tid=lin.tid))
+        layers.append({lin.name: oracle.quantize(synth.weight_fp16(lin.N, lin.K, seed=3, layer=l, tid=lin.tid,
+                                                                   std=lin.K ** -0.5))
                        for lin in DIMS.linears()})
     lm = DIMS.lm_head()
     return layers, oracle.quantize(synth.weight_fp16(lm.N, lm.K, seed=3, layer=99, tid=lm.tid))
@@ -69,7 +70,10 @@ def _rank_main(rank, world, port, x, out_q):
             dist.all_reduce(t)
             return t
 
-        stack = tp.LinearStack(mine, lm_mine, world, rank, mm, allreduce, lambda t: t.half(), DIMS)
+        def swiglu(xx, w):
+            return qw_b200.quantized_matmul_swiglu(xx, *[t for half in tp.gate_up_halves(w) for t in half])
+
+        stack = tp.LinearStack(mine, lm_mine, world, rank, mm, allreduce, lambda t: t.half(), DIMS, swiglu=swiglu)
         for M in (1, 16, 64):
             y = stack.forward(torch.from_numpy(x[:M]).to(dev))
             torch.cuda.synchronize()
@@ -123,9 +127,15 @@ def test_tp_stack_matches_oracle(world):
     def gmm(xx, w, out_f32):
         return qw_b200.quantized_matmul(xx, *w, out_dtype=torch.float32 if out_f32 else torch.float16)
 
+    def gswiglu(xx, w):
+        return qw_b200.quantized_matmul_swiglu(xx, *[t for half in tp.gate_up_halves(w) for t in half])
+
+    def oswiglu(xx, w):
+        return oracle.quantized_matmul_swiglu(xx, *tp.gate_up_halves(w))
+
     one_gpu = tp.LinearStack([{n: to_dev(w) for n, w in d.items()} for d in layers], to_dev(lm_w), 1, 0, gmm,
-                             None, None, DIMS)
-    ref_stack = tp.LinearStack(layers, lm_w, 1, 0, omm, None, None, DIMS)
+                             None, None, DIMS, swiglu=gswiglu)
+    ref_stack = tp.LinearStack(layers, lm_w, 1, 0, omm, None, None, DIMS, swiglu=oswiglu)
     n_ops = 4 * LAYERS + 1
     for M in (1, 16, 64):
         full = tp.gather_columns([got[(r, M)] for r in range(world)], DIMS.lm_head(), DIMS).astype(np.float32)

@@ -215,3 +215,42 @@ def test_golden_quantizer_inputs_regenerate():
         np.testing.assert_array_equal(wq, g["wq"])
         np.testing.assert_array_equal(s.view(np.uint16), g["scales"].view(np.uint16))
         np.testing.assert_array_equal(synth.activations(M, K, seed=seed), g["x"])
+
+
+def test_swiglu_known_answer():
+    """The reference's activation test input (ffi_tests.rs:1536-1548: gate
+    [1, 2, 3, 4], x = 2 everywhere, positive sum) against silu(g) * x in
+    float64, within the fp16 rounding of the three ops."""
+    gate = np.array([[1.0, 2.0, 3.0, 4.0]], np.float16)
+    x = np.full((1, 4), 2.0, np.float16)
+    out = oracle.swiglu(gate, x)
+    g = gate.astype(np.float64)
+    exact = g / (1.0 + np.exp(-g)) * 2.0
+    assert out.dtype == np.float16 and out.shape == (1, 4)
+    assert float(out.astype(np.float64).sum()) > 0.0
+    np.testing.assert_allclose(out.astype(np.float64), exact, rtol=2e-3)
+
+
+def test_swiglu_special_values():
+    """Large negative gates give zero (sigmoid underflows), large positive
+    ones pass gate * up through; zeros stay zero."""
+    gate = np.array([-65504.0, -100.0, -20.0, 0.0, 20.0, 100.0], np.float16)
+    up = np.array([1.0, 1.0, 1.0, 5.0, 1.0, 1.0], np.float16)
+    out = oracle.swiglu(gate, up).astype(np.float64)
+    assert out[0] == 0.0 and out[1] == 0.0 and out[3] == 0.0
+    assert abs(out[2]) < 1e-6
+    assert out[4] == 20.0 and out[5] == 100.0
+
+
+def test_swiglu_matmul_is_op_by_op():
+    """quantized_matmul_swiglu is the two fp16 matmuls followed by the
+    activation (compiled and uncompiled forms agree, ffi_tests.rs:3020-3060)."""
+    gate = oracle.quantize(synth.weight_fp16(72, 256, seed=1))
+    up = oracle.quantize(synth.weight_fp16(72, 256, seed=2))
+    x = synth.activations(3, 256, seed=3)
+    h = oracle.quantized_matmul_swiglu(x, gate, up)
+    g = oracle.quantized_matmul(x, *gate).astype(np.float32)
+    u = oracle.quantized_matmul(x, *up).astype(np.float32)
+    sig = (1.0 / (1.0 + np.exp(-g))).astype(np.float16).astype(np.float32)
+    ref = ((g * sig).astype(np.float16).astype(np.float32) * u).astype(np.float16)
+    np.testing.assert_array_equal(h.view(np.uint16), ref.view(np.uint16))

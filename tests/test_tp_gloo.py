@@ -31,7 +31,7 @@ def _weights():
     for l in range(LAYERS):
         d = {}
         for lin in DIMS.linears():
-            w = synth.weight_fp16(lin.N, lin.K, seed=7, layer=l, tid=lin.tid)
+            w = synth.weight_fp16(lin.N, lin.K, seed=7, layer=l, tid=lin.tid, std=lin.K ** -0.5)
             d[lin.name] = oracle.quantize(w)
         layers.append(d)
     lm = DIMS.lm_head()
@@ -44,9 +44,13 @@ def _oracle_mm(x, w, out_f32):
     return y32 if out_f32 else y
 
 
+def _oracle_swiglu(x, w):
+    return oracle.quantized_matmul_swiglu(x, *tp.gate_up_halves(w))
+
+
 def _reference_logits(x):
     layers, lm_w = _weights()
-    stack = tp.LinearStack(layers, lm_w, 1, 0, _oracle_mm, None, None, DIMS)
+    stack = tp.LinearStack(layers, lm_w, 1, 0, _oracle_mm, None, None, DIMS, swiglu=_oracle_swiglu)
     return stack.forward(x)
 
 
@@ -69,7 +73,7 @@ def _rank_main(rank, world, port, x, out_q, fail_rank):
             return t.numpy()
 
         stack = tp.LinearStack(mine, lm_mine, world, rank, _oracle_mm, allreduce,
-                               lambda a: a.astype(np.float16), DIMS)
+                               lambda a: a.astype(np.float16), DIMS, swiglu=_oracle_swiglu)
         t0 = time.time()
         out_q.put((rank, "ok", stack.forward(x), time.time() - t0))
     except Exception as e:  # noqa: BLE001 - reported to the parent
