@@ -330,22 +330,32 @@ def reduce_max(torch, v, dist_on):
     return float(t.item())
 
 
-def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50):
-    """One quantized matmul, rotating `copies` weight sets (> L2) between launches."""
+def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50, swiglu=False):
+    """One quantized matmul, rotating `copies` weight sets (> L2) between launches.
+    swiglu=True runs the fused SwiGLU over the two row halves of each N-row set
+    (N/2 outputs per row of x)."""
     sets = [make_weights(torch, qw, N, K, seed=7000 + i, dev=dev) for i in range(copies)]
     x = torch.randn(M, K, device=dev).half()
-    y = torch.empty(M, N, dtype=torch.float16, device=dev)
+    y = torch.empty(M, N // 2 if swiglu else N, dtype=torch.float16, device=dev)
+    if swiglu:
+        calls = [tuple(t for half in tp.gate_up_halves(w) for t in half) for w in sets]
     s = torch.cuda.Stream(dev)
-    with torch.cuda.stream(s):
-        for i in range(copies * 2):
+
+    def call(i):
+        if swiglu:
+            qw.quantized_matmul_swiglu(x, *calls[i % copies], out=y)
+        else:
             w = sets[i % copies]
             qw.quantized_matmul(x, w[0], w[1], w[2], out=y)
+
+    with torch.cuda.stream(s):
+        for i in range(copies * 2):
+            call(i)
     s.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s):
         for i in range(copies):
-            w = sets[i % copies]
-            qw.quantized_matmul(x, w[0], w[1], w[2], out=y)
+            call(i)
     with torch.cuda.stream(s):
         g.replay()
     s.synchronize()
@@ -357,7 +367,7 @@ def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50):
         e1.record(s)
     s.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / (iters * copies)
-    nbytes = synth.algorithmic_bytes(M, N, K)
+    nbytes = synth.algorithmic_bytes(M, N, K) - (2 * M * (N // 2) if swiglu else 0)  # SwiGLU writes N/2
     del g, sets
     torch.cuda.empty_cache()
     return us, nbytes / (us * 1e-6) / 1e9
@@ -454,6 +464,15 @@ def run_ours(args):
                 extra[f"qmm_17408x5120_m{M}"] = {"us": round(us, 2), "GBps": round(gbs, 1),
                                                  "frac_hbm": round(gbs / hbm_peak, 4),
                                                  "frac_8TBps": round(gbs / 8000.0, 4)}
+            # the MLP input: gate and up 17408 x 5120 each, SwiGLU fused, against
+            # the unfused 34816-row matmul of the same weights
+            for M in (1, 16):
+                us_f, gbs_f = kernel_microbench(torch, qw, M, 2 * synth.INTER, synth.HIDDEN, dev, copies=4,
+                                                swiglu=True)
+                us_p, _ = kernel_microbench(torch, qw, M, 2 * synth.INTER, synth.HIDDEN, dev, copies=4)
+                extra[f"swiglu_gate_up_m{M}"] = {"us": round(us_f, 2), "GBps": round(gbs_f, 1),
+                                                 "frac_hbm": round(gbs_f / hbm_peak, 4),
+                                                 "unfused_matmul_us": round(us_p, 2)}
 
     result = {
         "metric": METRIC,

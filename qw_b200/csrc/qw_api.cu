@@ -9,6 +9,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <utility>
 #include <vector>
 #include <algorithm>
@@ -54,22 +55,75 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   });
   return fn;
 }
+
+// Encoded descriptors by their arguments.  A descriptor is a function of its
+// arguments only, and a decode loop encodes the same weight, scale and bias
+// maps every step; the cache (per host thread, no locking) spares it those
+// driver calls.
+struct TmapKey {
+  uint64_t base;
+  uint64_t dims[3];
+  uint64_t strides[2];
+  uint32_t box[3];
+  int32_t rank, dtype, swizzle, pad0, pad1;  // explicit padding: 80 bytes, no implicit holes
+  bool operator==(const TmapKey& o) const { return std::memcmp(this, &o, sizeof(TmapKey)) == 0; }
+};
+static_assert(sizeof(TmapKey) == 80, "TmapKey has no implicit padding");
+struct TmapKeyHash {
+  size_t operator()(const TmapKey& k) const {
+    const unsigned char* b = reinterpret_cast<const unsigned char*>(&k);
+    uint64_t h = 1469598103934665603ull;  // FNV-1a
+    for (size_t i = 0; i < sizeof(TmapKey); ++i) h = (h ^ b[i]) * 1099511628211ull;
+    return (size_t)h;
+  }
+};
+constexpr size_t kTmapCacheMax = 4096;
+
+bool encode_cached(int rank, CUtensorMapDataType dtype, const void* base, const cuuint64_t* dims,
+                   const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swizzle, CUtensorMap* map,
+                   CUresult* rc) {
+  thread_local std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
+  TmapKey k;
+  std::memset(&k, 0, sizeof(k));
+  k.base = reinterpret_cast<uint64_t>(base);
+  for (int i = 0; i < rank; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+    if (i + 1 < rank) k.strides[i] = strides[i];
+  }
+  k.rank = rank;
+  k.dtype = (int32_t)dtype;
+  k.swizzle = (int32_t)swizzle;
+  auto it = cache.find(k);
+  if (it != cache.end()) {
+    *map = it->second;
+    *rc = CUDA_SUCCESS;
+    return true;
+  }
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  *rc = fn(map, dtype, rank, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (*rc == CUDA_SUCCESS) {
+    if (cache.size() >= kTmapCacheMax) cache.clear();
+    cache.emplace(k, *map);
+  }
+  return true;
+}
 }  // namespace
 
 bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
                     uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle,
                     std::string* err) {
-  auto fn = get_encode_fn();
-  if (!fn) {
-    *err = "cuTensorMapEncodeTiled is not available from the driver";
-    return false;
-  }
   const cuuint64_t dims[2] = {dim0, dim1};
   const cuuint64_t strides[1] = {stride1_bytes};
   const cuuint32_t box[2] = {box0, box1};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = CUDA_SUCCESS;
+  if (!encode_cached(2, dtype, base, dims, strides, box, swizzle, map, &r)) {
+    *err = "cuTensorMapEncodeTiled is not available from the driver";
+    return false;
+  }
   if (r != CUDA_SUCCESS) {
     *err = "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ") for dims " + std::to_string(dim0) +
            "x" + std::to_string(dim1) + " stride " + std::to_string(stride1_bytes);
@@ -81,17 +135,14 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* bas
 bool encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
                     const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle,
                     std::string* err) {
-  auto fn = get_encode_fn();
-  if (!fn) {
-    *err = "cuTensorMapEncodeTiled is not available from the driver";
-    return false;
-  }
   const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
   const cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
   const cuuint32_t b[3] = {box[0], box[1], box[2]};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, dtype, 3, const_cast<void*>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = CUDA_SUCCESS;
+  if (!encode_cached(3, dtype, base, d, st, b, swizzle, map, &r)) {
+    *err = "cuTensorMapEncodeTiled is not available from the driver";
+    return false;
+  }
   if (r != CUDA_SUCCESS) {
     *err = "cuTensorMapEncodeTiled (3-D) failed (code " + std::to_string((int)r) + ")";
     return false;
