@@ -373,6 +373,33 @@ def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50, swiglu=False)
     return us, nbytes / (us * 1e-6) / 1e9
 
 
+def graph_time_us(torch, fn, dev, iters=20):
+    """Device time of fn() per call, captured once in a CUDA graph of `iters` calls."""
+    s = torch.cuda.Stream(dev)
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(iters):
+            fn()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            g.replay()
+    s.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(reps):
+            g.replay()
+        e1.record(s)
+    s.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1000.0 / (iters * reps)
+
+
 def cpu_stack_rate(ws, lm, threads, passes=2):
     """The oracle (C, OpenMP, `threads` threads) over the whole stack's
     quantized weights copied to the host (the same bytes the GPU streams), M=1.
@@ -464,6 +491,13 @@ def run_ours(args):
                 extra[f"qmm_17408x5120_m{M}"] = {"us": round(us, 2), "GBps": round(gbs, 1),
                                                  "frac_hbm": round(gbs / hbm_peak, 4),
                                                  "frac_8TBps": round(gbs / 8000.0, 4)}
+            # the DFlash2 candidate step: lm_head at M=16 then the top 16 of each row
+            xl = torch.randn(16, synth.HIDDEN, device=dev).half()
+            lg = torch.empty(16, lm[0].shape[0], dtype=torch.float16, device=dev)
+            us_mm = graph_time_us(torch, lambda: qw.quantized_matmul(xl, *lm, out=lg), dev)
+            us_tk = graph_time_us(torch, lambda: qw.quantized_matmul_topk(xl, *lm, 16, logits=lg), dev)
+            extra["lm_head_top16_m16"] = {"us": round(us_tk, 2), "matmul_only_us": round(us_mm, 2),
+                                          "topk_us": round(us_tk - us_mm, 2)}
             # the MLP input: gate and up 17408 x 5120 each, SwiGLU fused, against
             # the unfused 34816-row matmul of the same weights
             for M in (1, 16):

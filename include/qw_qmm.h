@@ -108,6 +108,28 @@ int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_ar
                                const qw_array* biases, int group_size, int bits, const char* mode, qw_array* logits,
                                qw_array* idx, void* stream);
 
+/* The k largest logits of each row and their indices: logits f16 [..., N]
+ * (row-contiguous); idx u32 [..., k]; values f16 [..., k] (nullable), sorted
+ * by value descending, lower index first among equal values (one of the
+ * outcomes argpartition allows: the exact top-k set, ties at the k-th value
+ * resolved toward lower indices).  Values compare by their fp16 bit pattern
+ * made order-preserving (so -0 sorts below +0).  1 <= k < N, as the
+ * reference's caller requires; k above 1024 returns QW_EUNSUPPORTED.
+ * Replaces: argpartition(logits, -k, -1) + slice + take_along_axis in
+ * top_k_candidate_logits (crates/runtime/src/qwen3_5_dflash.rs:1236-1266;
+ * lib.rs:950, :876; mlx_cxx_bridge.cpp:2753, :2633). */
+int qw_topk(const qw_array* logits, int k, qw_array* idx, qw_array* values, void* stream);
+
+/* The LM-head projection followed by qw_topk: logits = x @ dequantize(w).T
+ * (f16 [..., N]) into `logits`, or into a per-(device, stream) buffer the
+ * library keeps when logits is null, then the top k of each row.
+ * Replaces: project_logits (qwen3_5.rs:1038-1044) followed by
+ * top_k_candidate_logits (qwen3_5_dflash.rs:1236-1266), the DFlash2
+ * candidate step (qwen3_5_dflash.rs:1412). */
+int qw_quantized_matmul_topk(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
+                             int group_size, int bits, const char* mode, int k, qw_array* logits, qw_array* idx,
+                             qw_array* values, void* stream);
+
 /* SwiGLU input projections of a dense MLP, activation fused:
  *   y = silu(g) * u,  g = x @ dequantize(w_gate).T,  u = x @ dequantize(w_up).T,
  * evaluated as the reference does on fp16 arrays: g and u rounded to fp16,

@@ -141,5 +141,27 @@ def quantized_matmul_swiglu(x, gate, up, group_size: int = 64, bits: int = 4, nt
     return swiglu(g, u)
 
 
+def topk(logits, k: int):
+    """(indices int64 [..., k], values fp16 [..., k]): the k largest fp16
+    logits of each row, descending, lower index first among equal values --
+    one outcome of argpartition(logits, -k) + take_along_axis as
+    top_k_candidate_logits uses them (crates/runtime/src/qwen3_5_dflash.rs:
+    1236-1266).  Values compare by their order-preserving fp16 key (-0 below
+    +0; NaN by bit pattern).  Requires 1 <= k < N (qwen3_5_dflash.rs:1248-1253)."""
+    a = np.ascontiguousarray(logits, dtype=np.float16)
+    N = a.shape[-1]
+    if not 1 <= k < N:
+        raise ValueError(f"k={k} must be in 1..{N - 1}")
+    rows = a.reshape(-1, N)
+    b = rows.view(np.uint16).astype(np.uint32)
+    key = np.where(b & 0x8000, (~b) & 0xFFFF, b | 0x8000)
+    idx = np.empty((rows.shape[0], k), dtype=np.int64)
+    for m in range(rows.shape[0]):
+        order = np.lexsort((np.arange(N), -key[m].astype(np.int64)))  # key descending, then index
+        idx[m] = order[:k]
+    vals = np.take_along_axis(rows, idx, axis=1)
+    return idx.reshape(*a.shape[:-1], k), vals.reshape(*a.shape[:-1], k)
+
+
 def max_threads() -> int:
     return int(lib().qwo_max_threads())

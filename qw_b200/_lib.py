@@ -50,6 +50,8 @@ SIGNATURES = {
     "qw_quantized_matmul": ([_PA, _PA, _PA, _PA, _I, _I, _I, ctypes.c_char_p, _PA, _P], _I),
     "qw_quantized_matmul_argmax": ([_PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, _PA, _PA, _P], _I),
     "qw_quantized_matmul_chain": ([ctypes.POINTER(QwQmmOp), _I, _I, _I, ctypes.c_char_p, _P], _I),
+    "qw_topk": ([_PA, _I, _PA, _PA, _P], _I),
+    "qw_quantized_matmul_topk": ([_PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, _I, _PA, _PA, _PA, _P], _I),
     "qw_quantized_matmul_swiglu": ([_PA, _PA, _PA, _PA, _PA, _PA, _PA, _I, _I, _I, ctypes.c_char_p, _PA, _P], _I),
     "qw_swiglu_activation": ([_PA, _PA, _PA, _P], _I),
     "qw_swiglu_mlp": ([_PA, _PA, _PA, _PA, _PA, _PA, _PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, _PA, _P], _I),

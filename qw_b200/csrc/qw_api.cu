@@ -719,6 +719,87 @@ int qw_swiglu_mlp(const qw_array* x, const qw_array* w_gate, const qw_array* sca
   return run_qmm(&h, w_down, scales_down, biases_down, 1, group_size, bits, mode, y, stream_v);
 }
 
+// Checks shared by the top-k entry points: logits f16 [..., N] contiguous,
+// idx u32 and values f16 (nullable) [..., k] with the same leading dims.
+static int check_topk(const qw_array* logits, int64_t N, int k, const qw_array* idx, const qw_array* values,
+                      int64_t* M) {
+  int rc;
+  if ((rc = check_array(idx, "idx")) || (values && (rc = check_array(values, "values")))) return rc;
+  if (k < 1 || (int64_t)k >= N)
+    return fail(QW_EINVAL, "k=" + std::to_string(k) + " must be in 1.." + std::to_string(N - 1) +
+                               " for rows of " + std::to_string(N) + " logits");
+  if (k > topk_max_k())
+    return fail(QW_EUNSUPPORTED, "k=" + std::to_string(k) + " is above the supported " +
+                                     std::to_string(topk_max_k()));
+  if (N > topk_max_n())
+    return fail(QW_EUNSUPPORTED, "rows of " + std::to_string(N) + " logits are above the supported " +
+                                     std::to_string(topk_max_n()));
+  *M = numel(logits) / N;
+  if (idx->dtype != QW_U32 || idx->shape[idx->ndim - 1] != k || numel(idx) != *M * k)
+    return fail(QW_EINVAL, "idx must be uint32 [..., k] with the leading dimensions of the logits");
+  if (values && (values->dtype != QW_F16 || values->shape[values->ndim - 1] != k || numel(values) != *M * k))
+    return fail(QW_EINVAL, "values must be float16 [..., k] with the leading dimensions of the logits");
+  if (!aligned(idx->data, 4) || (values && !aligned(values->data, 2)))
+    return fail(QW_EINVAL, "idx or values misaligned");
+  return QW_OK;
+}
+
+int qw_topk(const qw_array* logits, int k, qw_array* idx, qw_array* values, void* stream) {
+  set_error("");
+  int rc;
+  if ((rc = check_array(logits, "logits"))) return rc;
+  if (logits->dtype != QW_F16) return fail(QW_EUNSUPPORTED, "logits must be float16");
+  const int64_t N = logits->shape[logits->ndim - 1];
+  int64_t M = 0;
+  if ((rc = check_topk(logits, N, k, idx, values, &M))) return rc;
+  const cudaError_t ce =
+      launch_topk_rows(logits->data, N, M, N, k, (uint32_t*)idx->data, values ? values->data : nullptr,
+                       as_stream(stream));
+  return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "top-k launch");
+}
+
+int qw_quantized_matmul_topk(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
+                             int group_size, int bits, const char* mode, int k, qw_array* logits, qw_array* idx,
+                             qw_array* values, void* stream_v) {
+  set_error("");
+  int rc;
+  if ((rc = check_array(w, "w"))) return rc;
+  if (w->ndim != 2) return fail(QW_EUNSUPPORTED, "w must be 2-D [N, K*bits/32]");
+  if (!x) return fail(QW_EINVAL, "x is null");
+  if (x->ndim < 1 || x->ndim > 4) return fail(QW_EINVAL, "x must have 1 to 4 dimensions");
+  const int64_t N = w->shape[0];
+  const int64_t K = x->shape[x->ndim - 1];
+  const int64_t M = K ? numel(x) / K : 0;
+  qw_array lg{};
+  if (logits) {
+    lg = *logits;
+  } else {
+    // logits in this stream's activation buffer
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+    std::string err;
+    void* buf = nullptr;
+    const size_t bytes = (size_t)(M * N) * 2;
+    if (bytes && !activation_for(dev, as_stream(stream_v), bytes, &buf, &err)) return fail(QW_ENOMEM, err);
+    lg.data = buf;
+    lg.dtype = QW_F16;
+    lg.ndim = 2;
+    lg.shape[0] = M;
+    lg.shape[1] = N;
+    lg.strides[0] = N;
+    lg.strides[1] = 1;
+  }
+  if (lg.dtype != QW_F16) return fail(QW_EINVAL, "logits must be float16");
+  int64_t Mk = 0;
+  if ((rc = check_topk(&lg, N, k, idx, values, &Mk))) return rc;
+  if ((rc = run_qmm(x, w, scales, biases, 1, group_size, bits, mode, &lg, stream_v))) return rc;
+  if (M == 0) return QW_OK;
+  const cudaError_t ce = launch_topk_rows(lg.data, N, M, N, k, (uint32_t*)idx->data,
+                                          values ? values->data : nullptr, as_stream(stream_v));
+  return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "top-k launch");
+}
+
 static int linear_common(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
                          const qw_array* global_scale, const qw_array* linear_bias, int group_size, int bits,
                          const char* mode, qw_array* y, void* stream) {

@@ -109,6 +109,13 @@ cudaError_t launch_argmax_finalize(const unsigned long long* keys, uint32_t* idx
 // Greedy token of each row of fp16 logits [M][N] (lowest index among equal maxima).
 cudaError_t launch_argmax_rows(const void* logits, int64_t M, int64_t N, uint32_t* idx, cudaStream_t stream);
 
+// The k largest fp16 values of each of M rows of N (rows ld apart), sorted
+// descending, lower index first among equal values; 1 <= k <= topk_max_k(), k < N.
+int topk_max_k();
+int64_t topk_max_n();
+cudaError_t launch_topk_rows(const void* logits, int64_t ld, int64_t M, int64_t N, int k, uint32_t* idx,
+                             void* values, cudaStream_t stream);
+
 // Quantize / dequantize kernels (affine, 4-bit, group 64 for now).
 cudaError_t launch_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N,
                               int64_t K, int group_size, int bits, int rounding, cudaStream_t stream);

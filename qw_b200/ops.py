@@ -98,6 +98,34 @@ def quantized_matmul_argmax(x: torch.Tensor, w: torch.Tensor, scales: torch.Tens
     return idx.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
 
 
+def topk(logits: torch.Tensor, k: int, values: bool = True):
+    """(indices int64 [..., k], values fp16 [..., k] or None): the k largest
+    logits of each row, descending, lower index first among equal values --
+    argpartition(logits, -k) + take_along_axis as top_k_candidate_logits
+    (qwen3_5_dflash.rs:1236-1266) uses them, 1 <= k < N."""
+    lead = logits.shape[:-1]
+    idx = torch.empty(*lead, k, dtype=torch.int32, device=logits.device)
+    val = torch.empty(*lead, k, dtype=torch.float16, device=logits.device) if values else None
+    _lib.check(_lib.load().qw_topk(_arr(logits), int(k), _arr(idx), _arr(val), _stream(logits)))
+    return idx.to(torch.int64) & 0xFFFFFFFF, val
+
+
+def quantized_matmul_topk(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: Optional[torch.Tensor],
+                          k: int, group_size: int = 64, bits: int = 4, mode: str = "affine",
+                          logits: Optional[torch.Tensor] = None, values: bool = True):
+    """The LM-head projection then the top k of each row (project_logits then
+    top_k_candidate_logits, qwen3_5.rs:1038, qwen3_5_dflash.rs:1412);
+    returns (indices int64, values fp16 or None).  ``logits`` (optional)
+    receives the fp16 logits."""
+    lead = x.shape[:-1]
+    idx = torch.empty(*lead, k, dtype=torch.int32, device=x.device)
+    val = torch.empty(*lead, k, dtype=torch.float16, device=x.device) if values else None
+    _lib.check(_lib.load().qw_quantized_matmul_topk(_arr(x), _arr(w), _arr(scales), _arr(biases), group_size, bits,
+                                                    _mode(mode), int(k), _arr(logits), _arr(idx), _arr(val),
+                                                    _stream(x)))
+    return idx.to(torch.int64) & 0xFFFFFFFF, val
+
+
 def quantized_matmul_chain(ops, group_size: int = 64, bits: int = 4, mode: str = "affine") -> None:
     """Runs [(x, w, scales, biases, y), ...] in order, each y = x @ dequantize(w).T
     written into its preallocated ``y``; an op's x may be an earlier op's y.

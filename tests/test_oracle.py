@@ -254,3 +254,36 @@ def test_swiglu_matmul_is_op_by_op():
     sig = (1.0 / (1.0 + np.exp(-g))).astype(np.float16).astype(np.float32)
     ref = ((g * sig).astype(np.float16).astype(np.float32) * u).astype(np.float16)
     np.testing.assert_array_equal(h.view(np.uint16), ref.view(np.uint16))
+
+
+def test_topk_reference_candidate_vectors():
+    """The reference's candidate test vectors (qwen3_5_dflash.rs:3884-3928):
+    four peaks over a flat floor, in the compact domain (80,922 logits at
+    -1000) and the full vocabulary (248,320 at -2000), give exactly the peaks.
+    The id remapping between the two domains is the DFlash drafter's, outside
+    this path, so each domain is checked on its own ids."""
+    peaks = {0: 40.0, 80_000: 50.0, 80_001: 60.0, 80_921: 70.0}
+    for n, floor in ((80_922, -1000.0), (248_320, -2000.0)):
+        logits = np.full((1, 1, n), floor, np.float16)
+        for i, v in peaks.items():
+            logits[0, 0, i] = v
+        idx, vals = oracle.topk(logits, len(peaks))
+        assert idx.shape == (1, 1, 4)
+        assert dict(zip(idx[0, 0].tolist(), vals[0, 0].astype(float).tolist())) == peaks
+        assert idx[0, 0].tolist() == [80_921, 80_001, 80_000, 0]  # descending by value
+
+
+def test_topk_bounds_and_ties():
+    """k must lie in 1..N-1 (qwen3_5_dflash.rs:3931-3938); equal values keep
+    the lower indices, and -0 sorts below +0."""
+    z = np.zeros((1, 1, 4), np.float16)
+    for bad in (0, 4, 5):
+        with pytest.raises(ValueError):
+            oracle.topk(z, bad)
+    idx, _ = oracle.topk(z, 1)
+    assert idx.tolist() == [[[0]]]
+    row = np.array([[1, 3, 3, 2, 3, 3, -0.0, 0.0]], np.float16)
+    idx, vals = oracle.topk(row, 3)
+    assert idx.tolist() == [[1, 2, 4]] and vals.astype(float).tolist() == [[3, 3, 3]]
+    idx, _ = oracle.topk(row, 7)
+    assert idx.tolist() == [[1, 2, 4, 5, 3, 0, 7]]
