@@ -21,8 +21,9 @@
 // Every CTA of a cluster takes the same branches (the totals it decides on
 // are the cluster's), so the cluster barriers always pair up; the cluster's
 // CTAs are co-scheduled, so those barriers cannot wait on an absent CTA.
-// Histogram updates are aggregated per warp (__match_any_sync) so that the
-// few crowded bins of a logit distribution do not serialise 32 lanes each.
+// Histograms are kept per warp (shared-memory atomics then contend only
+// within a warp) and summed per CTA.  A CTA's share of a row of up to
+// 262,144 logits stays in registers (4 rounds) after its first read.
 #include <cuda_fp16.h>
 
 #include "qw_internal.h"
@@ -37,39 +38,32 @@ constexpr int kTopkMax = 1024;  // largest k
 constexpr int kPer = 8;         // logits per thread per round
 constexpr int kRound = kTopkThreads * kPer;
 constexpr int kCluster = 8;     // CTAs per row
+constexpr int kCache = 4;       // rounds a thread keeps in registers
 
 __device__ __forceinline__ uint32_t order_key(uint32_t b) {
   return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
 }
 
-// Keys of logits i0 .. i0+7 (0 past the end of the row).
+// Raw fp16 bits of logits i0 .. i0+7 (unspecified past the end of the row:
+// every use checks the index against N).
 template <bool VEC>
-__device__ __forceinline__ void load_keys(const __half* row, int i0, int N, uint32_t (&key)[kPer]) {
-  if (VEC) {
-    if (i0 < N) {  // N % 8 == 0 and the row 16-byte aligned: the whole vector is in range
-      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(row + i0));
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        key[2 * j] = order_key(w[j] & 0xFFFFu);
-        key[2 * j + 1] = order_key(w[j] >> 16);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) key[j] = 0u;
-    }
+__device__ __forceinline__ uint4 load_raw(const __half* row, int i0, int N) {
+  if constexpr (VEC) {  // N % 8 == 0 and the row 16-byte aligned: a vector is wholly in or out of range
+    return i0 < N ? __ldcg(reinterpret_cast<const uint4*>(row + i0)) : make_uint4(0u, 0u, 0u, 0u);
   } else {
+    uint32_t h[kPer];
 #pragma unroll
-    for (int j = 0; j < kPer; ++j)
-      key[j] = (i0 + j < N) ? order_key(__half_as_ushort(row[i0 + j])) : 0u;
+    for (int j = 0; j < kPer; ++j) h[j] = (i0 + j < N) ? __half_as_ushort(row[i0 + j]) : 0u;
+    return make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
   }
 }
 
-__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool active) {
-  const unsigned mask = __ballot_sync(0xffffffffu, active);
-  if (active) {
-    const unsigned peers = __match_any_sync(mask, bin);
-    if ((threadIdx.x & 31) == (unsigned)(__ffs(peers) - 1)) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+__device__ __forceinline__ void keys_of(uint4 v, uint32_t (&key)[kPer]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    key[2 * j] = order_key(w[j] & 0xFFFFu);
+    key[2 * j + 1] = order_key(w[j] >> 16);
   }
 }
 
@@ -143,6 +137,7 @@ template <bool VEC>
 __global__ void __launch_bounds__(kTopkThreads, 1)
     topk_rows_kernel(const __half* __restrict__ logits, int64_t ld, int N, int k, uint32_t* __restrict__ idx_out,
                      __half* __restrict__ val_out) {
+  __shared__ uint32_t whist[kTopkThreads / 32][256];  // per-warp histograms
   __shared__ uint32_t hist[256];      // this CTA's histogram (read by the whole cluster)
   __shared__ uint32_t tot[256];       // the cluster's
   __shared__ uint32_t rcount[1024];   // equal keys per round of this CTA
@@ -155,7 +150,7 @@ __global__ void __launch_bounds__(kTopkThreads, 1)
   const uint32_t crank = cluster_rank();
   const int rowi = blockIdx.x / kCluster;
   const __half* row = logits + (size_t)rowi * ld;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, wid = tid >> 5;
   const int rounds = (N + kRound - 1) / kRound;
   // this CTA's rounds: a contiguous share, so row order is CTA order
   const int r0 = (int)(((int64_t)rounds * crank) / kCluster);
@@ -167,44 +162,80 @@ __global__ void __launch_bounds__(kTopkThreads, 1)
     st_remote(ckey0 + 4 * slot, key);
     st_remote(cidx0 + 4 * slot, i);
   };
-  // the cluster's sum of every CTA's `hist` into `tot`
+  // A pass over this CTA's rounds: body(rd, keys) per round, from the
+  // register copy when the share fits in it.
+  const bool cached = r1 - r0 <= kCache;
+  uint4 cache[kCache];
+#pragma unroll
+  for (int q = 0; q < kCache; ++q)
+    cache[q] = (cached && r0 + q < r1) ? load_raw<VEC>(row, first(r0 + q), N) : make_uint4(0u, 0u, 0u, 0u);
+  auto for_rounds = [&](auto&& body) {
+    if (cached) {
+#pragma unroll
+      for (int q = 0; q < kCache; ++q) {
+        if (r0 + q < r1) {
+          uint32_t key[kPer];
+          keys_of(cache[q], key);
+          body(r0 + q, key);
+        }
+      }
+    } else {
+      for (int rd = r0; rd < r1; ++rd) {
+        uint32_t key[kPer];
+        keys_of(load_raw<VEC>(row, first(rd), N), key);
+        body(rd, key);
+      }
+    }
+  };
+  auto clear_whist = [&]() {
+    for (int b = tid; b < (kTopkThreads / 32) * 256; b += kTopkThreads) (&whist[0][0])[b] = 0;
+  };
+  // this CTA's histogram from the warps', then the cluster's sum into `tot`
   auto reduce_hist = [&]() {
+    __syncthreads();
+    for (int b = tid; b < 256; b += kTopkThreads) {
+      uint32_t v = 0;
+      for (int w = 0; w < kTopkThreads / 32; ++w) v += whist[w][b];
+      hist[b] = v;
+    }
     cluster_sync();  // every CTA's histogram is complete
     for (int b = tid; b < 256; b += kTopkThreads) {
-      uint32_t s = 0;
-      for (uint32_t c = 0; c < kCluster; ++c) s += ld_remote(remote(&hist[b], c));
-      tot[b] = s;
+      uint32_t v[kCluster];
+#pragma unroll
+      for (int c = 0; c < kCluster; ++c) v[c] = ld_remote(remote(&hist[b], (uint32_t)c));
+      uint32_t sum = 0;
+#pragma unroll
+      for (int c = 0; c < kCluster; ++c) sum += v[c];
+      tot[b] = sum;
     }
     cluster_sync();  // every CTA has read every histogram (they may be cleared now)
   };
 
   // 1. high byte
-  for (int b = tid; b < 256; b += kTopkThreads) hist[b] = 0;
+  clear_whist();
   for (int b = tid; b < 1024; b += kTopkThreads) rcount[b] = 0;
   if (tid == 0) {
     ncand = 0;
     n_equal = 0;
   }
   __syncthreads();
-  for (int rd = r0; rd < r1; ++rd) {
-    uint32_t key[kPer];
-    load_keys<VEC>(row, first(rd), N, key);
+  for_rounds([&](int rd, const uint32_t (&key)[kPer]) {
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) hist_add(hist, key[j] >> 8, first(rd) + j < N);
-  }
+    for (int j = 0; j < kPer; ++j)
+      if (first(rd) + j < N) atomicAdd(&whist[wid][key[j] >> 8], 1u);
+  });
   reduce_hist();
   uint32_t above_h;
   const uint32_t H = (uint32_t)bin_from_top(tot, 256, (uint32_t)k, &above_h);
 
   // 2. low byte within H
-  for (int b = tid; b < 256; b += kTopkThreads) hist[b] = 0;
+  clear_whist();
   __syncthreads();
-  for (int rd = r0; rd < r1; ++rd) {
-    uint32_t key[kPer];
-    load_keys<VEC>(row, first(rd), N, key);
+  for_rounds([&](int rd, const uint32_t (&key)[kPer]) {
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) hist_add(hist, key[j] & 255u, first(rd) + j < N && (key[j] >> 8) == H);
-  }
+    for (int j = 0; j < kPer; ++j)
+      if (first(rd) + j < N && (key[j] >> 8) == H) atomicAdd(&whist[wid][key[j] & 255u], 1u);
+  });
   uint32_t above_l;
   reduce_hist();
   const uint32_t L = (uint32_t)bin_from_top(tot, 256, (uint32_t)k - above_h, &above_l);
@@ -216,9 +247,7 @@ __global__ void __launch_bounds__(kTopkThreads, 1)
 
   // 3. collect into CTA 0: keys above T, and the equal keys when all are taken;
   //    otherwise count this CTA's equal keys per round
-  for (int rd = r0; rd < r1; ++rd) {
-    uint32_t key[kPer];
-    load_keys<VEC>(row, first(rd), N, key);
+  for_rounds([&](int rd, const uint32_t (&key)[kPer]) {
     uint32_t c = 0;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
@@ -237,7 +266,7 @@ __global__ void __launch_bounds__(kTopkThreads, 1)
         atomicAdd(&n_equal, c);
       }
     }
-  }
+  });
   if (!take_all_eq) {
     // The `need` lowest indices among the keys equal to T: the CTAs before
     // this one (in row order) hold `before` of them; this CTA takes its
@@ -247,18 +276,9 @@ __global__ void __launch_bounds__(kTopkThreads, 1)
     for (uint32_t c = 0; c < crank; ++c) before += ld_remote(remote(&n_equal, c));
     for (int rd = r0; rd < r1 && before < need; ++rd) {
       const uint32_t in_round = rcount[rd - r0];
-      if (before + in_round <= need) {
-        // the whole round's equal keys are wanted
-        if (in_round) {
-          uint32_t key[kPer];
-          load_keys<VEC>(row, first(rd), N, key);
-#pragma unroll
-          for (int j = 0; j < kPer; ++j)
-            if (first(rd) + j < N && key[j] == T) append(T, (uint32_t)(first(rd) + j));
-        }
-      } else {
+      if (in_round) {
         uint32_t key[kPer];
-        load_keys<VEC>(row, first(rd), N, key);
+        keys_of(load_raw<VEC>(row, first(rd), N), key);
         uint32_t c = 0;
 #pragma unroll
         for (int j = 0; j < kPer; ++j) c += (first(rd) + j < N && key[j] == T) ? 1u : 0u;
