@@ -19,7 +19,9 @@ Extra keys report the single-matrix qmv (M=1) and verify qmm (M=16) GB/s with
 L2 defeated by rotating weight copies, and the M=16 stack.
 
 With torchrun (N > 1) the stack is tensor-parallel: q/k/v/gate/up/lm_head
-column-sharded, o/down row-sharded with an fp32 NCCL allreduce.  Rank 0 prints
+column-sharded, o/down row-sharded, their fp32 partials summed by the
+library's one-shot NVLink peer allreduce with the fp16 cast fused
+(`--tp-allreduce nccl`: ncclAllReduce then a cast, for comparison).  Rank 0 prints
 one JSON line.  `--impl reference` times the reference's CPU path (the oracle
 restatement of MLX's affine quantized_matmul; the reference itself cannot be
 built here) on the host cores.
@@ -168,8 +170,9 @@ class StackRunner:
     one GPU; qkv+o between allreduces under tensor parallelism) to
     qw_quantized_matmul_chain."""
 
-    def __init__(self, torch, qw, ws, lm, M, P, group, chain=False):
+    def __init__(self, torch, qw, ws, lm, M, P, group, chain=False, ar=None):
         self.torch, self.qw, self.ws, self.lm, self.M, self.P, self.group = torch, qw, ws, lm, M, P, group
+        self.ar = ar  # tp.PeerAllreduce, or None for NCCL
         self.chain = chain and M <= 16
         dev = lm[0].device
         H = synth.HIDDEN
@@ -225,13 +228,20 @@ class StackRunner:
     def _mm(self, x, w, out):
         self.qw.quantized_matmul(x, w[0], w[1], w[2], out=out)
 
+    def _reduce(self, out16):
+        """out16 = fp16(sum over ranks of self.part)."""
+        if self.ar is not None:
+            self.ar(self.part, out16)
+        else:
+            self.torch.distributed.all_reduce(self.part, group=self.group)
+            out16.copy_(self.part)
+
     def _rowpar(self, x, w, out16):
         if self.P == 1:
             self._mm(x, w, out16)
             return
         self._mm(x, w, self.part)
-        self.torch.distributed.all_reduce(self.part, group=self.group)
-        out16.copy_(self.part)
+        self._reduce(out16)
 
     def _swiglu(self, x, l, out):
         self.qw.quantized_matmul_swiglu(x, *self.halves[l], out=out)
@@ -244,8 +254,7 @@ class StackRunner:
                 elif a[0] == "swiglu":
                     self._swiglu(self.o, a[1], self.gate)
                 else:
-                    self.torch.distributed.all_reduce(self.part, group=self.group)
-                    a[1].copy_(self.part)
+                    self._reduce(a[1])
             return
         M = self.M
         for l, w in enumerate(self.ws):
@@ -443,18 +452,22 @@ def run_ours(args):
 
     ws, lm = build_stack(torch, qw, P, rank, args.layers, dev)
     torch.cuda.synchronize()
+    ar = None
+    if dist_on and args.tp_allreduce == "peer":
+        from qw_b200 import tp as tpm
+        ar = tpm.PeerAllreduce(2048 * synth.HIDDEN, group=group)  # the largest row-parallel output
     stream = torch.cuda.Stream(dev)
 
     # value: one qw_quantized_matmul per linear (the drop-in path), the step
     # captured once as a CUDA graph with programmatic dependent launch
-    runner = StackRunner(torch, qw, ws, lm, 1, P, group, chain=False)
+    runner = StackRunner(torch, qw, ws, lm, 1, P, group, chain=False, ar=ar)
     ms, clocks = timed_graph(torch, runner, args.steps, args.warmup, stream, dist_on, local)
     step_bytes = synth.stack_bytes(1, layers=args.layers) // P if P > 1 else synth.stack_bytes(1, layers=args.layers)
     tok_s = 1000.0 / ms
     launches = runner.launches_per_step
     e2e_ms, h2d, d2h = timed_e2e(torch, runner, args.steps, args.warmup, stream, dist_on)
     # the same step through qw_quantized_matmul_chain (runs of linears per cooperative launch)
-    chained = StackRunner(torch, qw, ws, lm, 1, P, group, chain=True)
+    chained = StackRunner(torch, qw, ws, lm, 1, P, group, chain=True, ar=ar)
     ms_chain, _ = timed_graph(torch, chained, args.steps, args.warmup, stream, dist_on, local)
     chain_launches = chained.launches_per_step
     del chained
@@ -467,7 +480,7 @@ def run_ours(args):
     if not args.skip_extra:
         # verify-batch stacks (MTP M=4, DFlash2 block M=16): HBM-bound like M=1
         for Mv in (4, 16):
-            rv = StackRunner(torch, qw, ws, lm, Mv, P, group)
+            rv = StackRunner(torch, qw, ws, lm, Mv, P, group, ar=ar)
             msv, _ = timed_graph(torch, rv, max(10, args.steps // 4), args.warmup, stream, dist_on, local)
             bv = synth.stack_bytes(Mv, layers=args.layers) // P
             extra[f"stack_m{Mv}"] = {"tok_s": round(Mv * 1000.0 / msv, 1), "ms_per_step": round(msv, 4),
@@ -476,7 +489,7 @@ def run_ours(args):
                                      "weight_reuse_vs_m1": Mv}
             del rv
         # prefill chunk (M=2048) through the same stack: tensor-bound (tcgen05)
-        rp = StackRunner(torch, qw, ws, lm, 2048, P, group)
+        rp = StackRunner(torch, qw, ws, lm, 2048, P, group, ar=ar)
         msp, _ = timed_graph(torch, rp, 3, 3, stream, dist_on, local)
         fl = synth.stack_flops(2048, layers=args.layers) / P
         extra["stack_prefill_m2048"] = {"tok_s": round(2048 * 1000.0 / msp, 1), "ms_per_step": round(msp, 3),
@@ -523,7 +536,7 @@ def run_ours(args):
         "data": "synthetic: x~N(0,1), W~N(0,0.02) fp16 quantized on GPU (affine, 4-bit, group 64)",
         "config": {"workload": f"decode linear stack M=1, {args.layers} layers (qkv/o/gate_up+SwiGLU/down) + lm_head",
                    "M": 1, "layers": args.layers, "hidden": synth.HIDDEN, "vocab": synth.VOCAB,
-                   "parallelism": f"tp{world}" if world > 1 else "single",
+                   "parallelism": (f"tp{world}, {args.tp_allreduce} allreduce" if world > 1 else "single"),
                    "l2": "inputs larger than L2 (weights %.2f GB per step)" % (synth.stack_bytes(1, args.layers) / 1e9),
                    "graph": "one CUDA graph per step, programmatic dependent launch"},
         "GBps_per_gpu": round(step_bytes / (ms * 1e-3) / 1e9, 1),
@@ -552,6 +565,8 @@ def run_ours(args):
                       f"({secs:.1f} s of CPU work) on the GPU's quantized weights copied to the host"}
     if dist_on:
         torch.distributed.barrier()
+        if ar is not None:
+            ar.close()
         torch.distributed.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
@@ -641,6 +656,8 @@ def main():
     ap.add_argument("--layers", type=int, default=synth.LAYERS)
     ap.add_argument("--skip-extra", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
+                    help="exchange of the row-parallel partial sums under torchrun")
     ap.add_argument("--case", default=None,
                     help="M,N,K: time one quantized matmul shape only (small device footprint, for ncu)")
     args = ap.parse_args()

@@ -180,6 +180,33 @@ int qw_quantized_matmul_static_scratch(const qw_array* x, const qw_array* w, con
                                        const qw_array* biases, int transpose, int group_size, int bits,
                                        const char* mode, qw_array* y, void* stream);
 
+/* ---------------------------------------------------------------- peer allreduce
+ * Tensor parallelism's exchange step: the o and down projections are
+ * row-parallel, each rank's matmul writes fp32 partial sums (y as float32),
+ * and y = fp16(sum over ranks).  One process per GPU of one node; every rank
+ * owns a buffer that all ranks map through CUDA IPC, and one kernel per call
+ * stores the rank's partial into every rank's buffer over NVLink, flags it,
+ * waits (bounded) for every rank's flag and sums in rank order, so every rank
+ * gets bit-identical y.  Calls are stream-ordered and may be captured in a
+ * CUDA graph; all ranks must make the same sequence of calls.  A rank whose
+ * peers never arrive gives up after 2 s: its y is incomplete and
+ * qw_device_status reports QW_ETIMEOUT.  No multicast or NVLS is used.
+ * No counterpart in the reference, which runs on one device; it replaces the
+ * ncclAllReduce(float32, sum) + fp16 cast of the tensor-parallel stack.
+ *
+ * Set-up: qw_allreduce_init on every rank (allocates and zeroes this rank's
+ * buffer for up to max_elems floats per call and returns its IPC handle,
+ * QW_IPC_HANDLE_BYTES bytes); exchange the handles (any host transport);
+ * qw_allreduce_connect with all ranks' handles in rank order; then a
+ * barrier across ranks before the first qw_allreduce_sum. */
+#define QW_IPC_HANDLE_BYTES 64
+typedef struct qw_allreduce qw_allreduce;
+int qw_allreduce_init(int world, int rank, int64_t max_elems, qw_allreduce** comm, unsigned char* handle);
+int qw_allreduce_connect(qw_allreduce* comm, const unsigned char* handles);
+/* y (f16 or f32, any shape) = sum over ranks of partial (f32, same element count). */
+int qw_allreduce_sum(qw_allreduce* comm, const qw_array* partial, qw_array* y, void* stream);
+int qw_allreduce_destroy(qw_allreduce* comm);
+
 /* y = x @ dequantize(w).T (+ linear_bias), linear_bias nullable f16 [N].
  * Replaces: quantized_linear_forward, lib.rs:591-601, mlx_cxx_bridge.cpp:1099-1133. */
 int qw_quantized_linear_forward(const qw_array* x, const qw_array* w, const qw_array* scales,

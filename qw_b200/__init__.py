@@ -5,12 +5,13 @@ tensor-parallel linear stack).
 The compute lives in libqwqmm.so (C ABI in include/qw_qmm.h); this package is
 the Python mirror of the reference's operator surface on torch tensors.
 """
-from .ops import (QuantizedLinear, QuantizedMlp, compiled_moe_expert_forward, compiled_swiglu_activation, dequantize, device_status,
+from .ops import (QuantizedFusedLinear, QuantizedLinear, QuantizedMlp, compiled_moe_expert_forward, compiled_swiglu_activation, dequantize, device_status,
                   quantize_weights, quantized_linear_forward, quantized_linear_forward_global_scale, quantized_matmul,
                   quantized_matmul_argmax, quantized_matmul_chain, quantized_matmul_swiglu, quantized_matmul_topk,
                   swiglu_mlp, topk)
 
 __all__ = [
+    "QuantizedFusedLinear",
     "QuantizedLinear",
     "QuantizedMlp",
     "compiled_moe_expert_forward",

@@ -24,6 +24,8 @@ QW_F16 = 2
 QW_BF16 = 3
 QW_F32 = 4
 
+QW_IPC_HANDLE_BYTES = 64
+
 # Every entry point include/qw_qmm.h declares, with its ctypes signature.
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -51,6 +53,10 @@ SIGNATURES = {
     "qw_quantized_matmul_argmax": ([_PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, _PA, _PA, _P], _I),
     "qw_quantized_matmul_chain": ([ctypes.POINTER(QwQmmOp), _I, _I, _I, ctypes.c_char_p, _P], _I),
     "qw_topk": ([_PA, _I, _PA, _PA, _P], _I),
+    "qw_allreduce_init": ([_I, _I, ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p], _I),
+    "qw_allreduce_connect": ([ctypes.c_void_p, ctypes.c_char_p], _I),
+    "qw_allreduce_sum": ([ctypes.c_void_p, _PA, _PA, _P], _I),
+    "qw_allreduce_destroy": ([ctypes.c_void_p], _I),
     "qw_quantized_matmul_topk": ([_PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, _I, _PA, _PA, _PA, _P], _I),
     "qw_quantized_matmul_swiglu": ([_PA, _PA, _PA, _PA, _PA, _PA, _PA, _I, _I, _I, ctypes.c_char_p, _PA, _P], _I),
     "qw_swiglu_activation": ([_PA, _PA, _PA, _P], _I),

@@ -1,0 +1,190 @@
+// qw_allreduce.cu -- one-shot sum of the row-parallel projections' fp32
+// partials across the GPUs of one node, over NVLink peer memory, with the
+// fp16 rounding of the sum fused (the o and down projections of a
+// tensor-parallel layer: each rank holds y_r = x_r W_r^T over its K-slice,
+// and y = fp16(sum_r y_r)).
+//
+// Each rank owns one buffer that every rank maps (CUDA IPC):
+//   [flags: 2 parities x 8 ranks x 1024 chunks of uint32]
+//   [data:  2 parities x P ranks x n_max floats]
+// CTA b of every rank handles chunk b of the vector (every rank launches the
+// same grid for the same n), so the exchange is per chunk and needs no
+// grid-wide step.  CTA b with epoch e (parity e & 1):
+//   1. stores its chunk of the local partial into slot (parity, rank) of
+//      every rank's buffer (plain stores over NVLink), then, after a CTA
+//      barrier, writes flag (parity, rank, b) = e into every rank's buffer
+//      with system-scope release semantics;
+//   2. waits, bounded, until flags (parity, r, b) of its own buffer reach e
+//      for every rank r (acquire), then sums its chunk over the P slots in
+//      rank order (every rank gets identical y) and writes fp16 (or fp32).
+// The epoch of chunk b lives in device memory (CTA b bumps it), so a call
+// captured in a CUDA graph advances on every replay, and every rank runs the
+// same sequence of calls, so the epochs agree without a host exchange.  Two
+// parities make the reuse safe: a rank can only store call e + 2's chunk
+// after every rank has flagged call e + 1 for it, which each rank does only
+// after its call e finished reading the chunk.
+// No multicast, no NVLS: plain loads and stores to mapped peer memory.  A
+// rank whose peers never flag gives up after the wait bound, records a
+// status and returns (its output is then incomplete).
+#include <cuda_fp16.h>
+
+#include "qw_internal.h"
+#include "qw_ptx.cuh"
+
+namespace qw {
+
+namespace {
+
+constexpr int kArThreads = 256;
+constexpr int kArVec = 4;         // floats per thread per step
+constexpr int kArMaxChunks = 1024;
+constexpr size_t kArFlagBytes = (size_t)2 * kArMaxRanks * kArMaxChunks * sizeof(unsigned int);
+
+struct ArParams {
+  float* data[kArMaxRanks];       // each rank's data area (mapped here)
+  unsigned int* flags[kArMaxRanks];
+  unsigned int* epochs;           // local: one per chunk
+  unsigned int* status;
+  int P, rank;
+  long long n_max;
+};
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <bool OUT_F32>
+__global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p, const float* __restrict__ partial,
+                                                               void* __restrict__ out, long long n, int vec_ok) {
+  __shared__ int s_ok;
+  const int b = blockIdx.x;
+  if (threadIdx.x == 0) s_ok = 1;
+  // this CTA's chunk: contiguous, in units of 4 floats
+  const long long nv = (n + kArVec - 1) / kArVec;
+  const long long per = (nv + gridDim.x - 1) / gridDim.x;
+  const long long v0 = (long long)b * per;
+  const long long v1 = v0 + per < nv ? v0 + per : nv;
+  // The partial is the previous kernel's output, and the epoch was written by
+  // the previous call of this kernel: both complete once the wait returns
+  // (every kernel of these streams waits on its predecessor before it ends).
+  pdl_wait();
+  pdl_launch_dependents();
+  const unsigned int e = p.epochs[b] + 1u;  // only CTA b of these calls touches it
+  const int par = (int)(e & 1u);
+
+  // 1. scatter into slot (par, rank) of every rank, then flag the chunk
+  for (long long v = v0 + threadIdx.x; v < v1; v += kArThreads) {
+    const long long i = v * kArVec;
+    if (vec_ok) {
+      const float4 x = *reinterpret_cast<const float4*>(partial + i);
+      for (int r = 0; r < p.P; ++r)
+        *reinterpret_cast<float4*>(p.data[r] + ((long long)par * p.P + p.rank) * p.n_max + i) = x;
+    } else {
+      for (int j = 0; j < kArVec && i + j < n; ++j) {
+        const float x = partial[i + j];
+        for (int r = 0; r < p.P; ++r) p.data[r][((long long)par * p.P + p.rank) * p.n_max + i + j] = x;
+      }
+    }
+  }
+  __syncthreads();  // every thread's stores precede the flags
+  if (threadIdx.x < p.P) {
+    __threadfence_system();
+    st_release_sys(p.flags[threadIdx.x] + ((size_t)par * kArMaxRanks + p.rank) * kArMaxChunks + b, e);
+  }
+
+  // 2. wait for every rank's flag of this chunk, then sum it
+  if (threadIdx.x < p.P) {
+    const unsigned int* f = p.flags[p.rank] + ((size_t)par * kArMaxRanks + threadIdx.x) * kArMaxChunks + b;
+    if ((int)(ld_acquire_sys(f) - e) < 0) {
+      const uint64_t t0 = globaltimer_ns();
+      while ((int)(ld_acquire_sys(f) - e) < 0) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          record_status(p.status, kDevTimeoutPeer);
+          s_ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (s_ok) {
+    const float* mine = p.data[p.rank] + (long long)par * p.P * p.n_max;
+    for (long long v = v0 + threadIdx.x; v < v1; v += kArThreads) {
+      const long long i = v * kArVec;
+      if (vec_ok) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < p.P; ++r) {  // rank order: every rank sums identically
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(mine + (long long)r * p.n_max + i));
+          s.x += x.x;
+          s.y += x.y;
+          s.z += x.z;
+          s.w += x.w;
+        }
+        if (OUT_F32) {
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + i) = s;
+        } else {
+          __half2* o = reinterpret_cast<__half2*>(reinterpret_cast<__half*>(out) + i);
+          o[0] = __floats2half2_rn(s.x, s.y);
+          o[1] = __floats2half2_rn(s.z, s.w);
+        }
+      } else {
+        for (int j = 0; j < kArVec && i + j < n; ++j) {
+          float s = 0.f;
+          for (int r = 0; r < p.P; ++r) s += __ldcg(mine + (long long)r * p.n_max + i + j);
+          if (OUT_F32) reinterpret_cast<float*>(out)[i + j] = s;
+          else reinterpret_cast<__half*>(out)[i + j] = __float2half_rn(s);
+        }
+      }
+    }
+  }
+  if (threadIdx.x == 0) p.epochs[b] = e;
+}
+
+}  // namespace
+
+size_t allreduce_buffer_bytes(int P, int64_t n_max) {
+  return kArFlagBytes + (size_t)2 * P * (size_t)n_max * sizeof(float);
+}
+
+size_t allreduce_epoch_bytes() { return kArMaxChunks * sizeof(unsigned int); }
+
+cudaError_t launch_allreduce(const ArComm& c, const float* partial, void* out, bool out_f32, bool vec, int64_t n,
+                             int sm_count, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  ArParams p{};
+  for (int r = 0; r < c.P; ++r) {
+    p.data[r] = reinterpret_cast<float*>(static_cast<uint8_t*>(c.peer_bufs[r]) + kArFlagBytes);
+    p.flags[r] = static_cast<unsigned int*>(c.peer_bufs[r]);
+  }
+  p.epochs = c.counters;
+  p.status = c.status;
+  p.P = c.P;
+  p.rank = c.rank;
+  p.n_max = c.n_max;
+  // chunks of about 2 float4 per thread; the grid depends on n only, so
+  // every rank splits a call identically
+  const long long nv = (n + kArVec - 1) / kArVec;
+  long long grid = (nv + kArThreads * 2 - 1) / (kArThreads * 2);
+  if (grid > sm_count) grid = sm_count;
+  if (grid > kArMaxChunks) grid = kArMaxChunks;
+  if (grid < 1) grid = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kArThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int v = vec ? 1 : 0;
+  return out_f32 ? cudaLaunchKernelEx(&cfg, allreduce_kernel<true>, p, partial, out, (long long)n, v)
+                 : cudaLaunchKernelEx(&cfg, allreduce_kernel<false>, p, partial, out, (long long)n, v);
+}
+
+}  // namespace qw

@@ -800,6 +800,103 @@ int qw_quantized_matmul_topk(const qw_array* x, const qw_array* w, const qw_arra
   return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "top-k launch");
 }
 
+// ------------------------------------------------------ peer allreduce
+struct qw_allreduce {
+  ArComm comm;
+  int device = -1;
+  void* own = nullptr;                 // this rank's shared buffer (cudaMalloc)
+  bool opened[kArMaxRanks] = {};       // peer buffers mapped through IPC
+  int sm_count = 0;
+};
+
+int qw_allreduce_init(int world, int rank, int64_t max_elems, qw_allreduce** out, unsigned char* handle) {
+  set_error("");
+  if (!out || !handle) return fail(QW_EINVAL, "out and handle must not be null");
+  *out = nullptr;
+  if (world < 1 || world > kArMaxRanks) return fail(QW_EUNSUPPORTED, "world size must be 1 to 8");
+  if (rank < 0 || rank >= world) return fail(QW_EINVAL, "rank out of range");
+  if (max_elems < 1 || max_elems > ((int64_t)1 << 28)) return fail(QW_EINVAL, "max_elems must be 1 to 2^28");
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  DeviceRes* res = nullptr;
+  std::string err;
+  if (!device_res(dev, &res, &err)) return fail(QW_ENOMEM, err);
+  auto* c = new qw_allreduce();
+  c->device = dev;
+  c->sm_count = device_info(dev).sm_count;
+  c->comm.P = world;
+  c->comm.rank = rank;
+  c->comm.n_max = (max_elems + 3) / 4 * 4;  // keeps every slot 16-byte aligned
+  c->comm.status = res->status;
+  const size_t bytes = allreduce_buffer_bytes(world, c->comm.n_max);
+  if ((ce = cudaMalloc(&c->own, bytes)) != cudaSuccess || (ce = cudaMemset(c->own, 0, bytes)) != cudaSuccess ||
+      (ce = cudaMalloc(reinterpret_cast<void**>(&c->comm.counters), allreduce_epoch_bytes())) != cudaSuccess ||
+      (ce = cudaMemset(c->comm.counters, 0, allreduce_epoch_bytes())) != cudaSuccess) {
+    cudaGetLastError();
+    qw_allreduce_destroy(c);
+    return cuda_fail(ce, "allreduce buffer allocation");
+  }
+  c->comm.peer_bufs[rank] = c->own;
+  cudaIpcMemHandle_t h;
+  if ((ce = cudaIpcGetMemHandle(&h, c->own)) != cudaSuccess) {
+    qw_allreduce_destroy(c);
+    return cuda_fail(ce, "cudaIpcGetMemHandle");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == QW_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof h);
+  *out = c;
+  return QW_OK;
+}
+
+int qw_allreduce_connect(qw_allreduce* c, const unsigned char* handles) {
+  set_error("");
+  if (!c || !handles) return fail(QW_EINVAL, "comm and handles must not be null");
+  for (int r = 0; r < c->comm.P; ++r) {
+    if (r == c->comm.rank || c->opened[r]) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handles + (size_t)r * QW_IPC_HANDLE_BYTES, sizeof h);
+    void* p = nullptr;
+    const cudaError_t ce = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (ce != cudaSuccess) return cuda_fail(ce, ("cudaIpcOpenMemHandle of rank " + std::to_string(r)).c_str());
+    c->comm.peer_bufs[r] = p;
+    c->opened[r] = true;
+  }
+  return QW_OK;
+}
+
+int qw_allreduce_sum(qw_allreduce* c, const qw_array* partial, qw_array* y, void* stream) {
+  set_error("");
+  int rc;
+  if (!c) return fail(QW_EINVAL, "comm is null");
+  if ((rc = check_array(partial, "partial")) || (rc = check_array(y, "y"))) return rc;
+  for (int r = 0; r < c->comm.P; ++r)
+    if (!c->comm.peer_bufs[r]) return fail(QW_EINVAL, "rank " + std::to_string(r) + " is not connected");
+  if (partial->dtype != QW_F32) return fail(QW_EINVAL, "partial must be float32");
+  if (y->dtype != QW_F16 && y->dtype != QW_F32) return fail(QW_EINVAL, "y must be float16 or float32");
+  const int64_t n = numel(partial);
+  if (numel(y) != n) return fail(QW_EINVAL, "y must have as many elements as partial");
+  if (n > c->comm.n_max)
+    return fail(QW_EINVAL, std::to_string(n) + " elements exceed the communicator's " +
+                               std::to_string(c->comm.n_max));
+  const bool y32 = y->dtype == QW_F32;
+  const bool vec = n % 4 == 0 && aligned(partial->data, 16) && aligned(y->data, y32 ? 16 : 8);
+  const cudaError_t ce = launch_allreduce(c->comm, static_cast<const float*>(partial->data), y->data, y32, vec, n,
+                                          c->sm_count, as_stream(stream));
+  return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "allreduce launch");
+}
+
+int qw_allreduce_destroy(qw_allreduce* c) {
+  set_error("");
+  if (!c) return QW_OK;
+  for (int r = 0; r < kArMaxRanks; ++r)
+    if (c->opened[r]) cudaIpcCloseMemHandle(c->comm.peer_bufs[r]);
+  if (c->own) cudaFree(c->own);
+  if (c->comm.counters) cudaFree(c->comm.counters);
+  delete c;
+  return QW_OK;
+}
+
 static int linear_common(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
                          const qw_array* global_scale, const qw_array* linear_bias, int group_size, int bits,
                          const char* mode, qw_array* y, void* stream) {

@@ -116,6 +116,21 @@ int64_t topk_max_n();
 cudaError_t launch_topk_rows(const void* logits, int64_t ld, int64_t M, int64_t N, int k, uint32_t* idx,
                              void* values, cudaStream_t stream);
 
+// One-shot allreduce of fp32 partials over NVLink peer memory (qw_allreduce.cu).
+constexpr int kArMaxRanks = 8;
+struct ArComm {
+  void* peer_bufs[kArMaxRanks];  // every rank's shared buffer, mapped in this process
+  unsigned int* counters;        // local: one epoch per chunk (allreduce_epoch_bytes())
+  unsigned int* status;          // device status word
+  int P = 0, rank = 0;
+  int64_t n_max = 0;
+};
+size_t allreduce_buffer_bytes(int P, int64_t n_max);
+size_t allreduce_epoch_bytes();
+// y[i] = sum over ranks of partial[i], rounded to fp16 (or kept fp32); n <= n_max.
+cudaError_t launch_allreduce(const ArComm& c, const float* partial, void* out, bool out_f32, bool vec, int64_t n,
+                             int sm_count, cudaStream_t stream);
+
 // Quantize / dequantize kernels (affine, 4-bit, group 64 for now).
 cudaError_t launch_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N,
                               int64_t K, int group_size, int bits, int rounding, cudaStream_t stream);

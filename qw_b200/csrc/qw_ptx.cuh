@@ -19,7 +19,7 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 // Status codes a kernel leaves in its device status word (first one wins);
 // the host reads the word with qw_device_status().
 enum : unsigned int { kDevOk = 0, kDevTimeoutFull = 1, kDevTimeoutEmpty = 2, kDevTimeoutTmem = 3,
-                      kDevTimeoutAccum = 4 };
+                      kDevTimeoutAccum = 4, kDevTimeoutPeer = 5 };
 
 __device__ __forceinline__ void record_status(unsigned int* status, unsigned int code) {
   atomicCAS(status, 0u, code);

@@ -273,6 +273,49 @@ class QuantizedLinear:
     __call__ = forward
 
 
+class QuantizedFusedLinear:
+    """Projections of one input fused into one quantized matmul: the planes'
+    weights, scales and biases concatenated along the output rows, the output
+    split back into column views (no copies).  After the reference's
+    FusedQKVLinear (layers.rs:2467-2850: q|k|v concatenated at load,
+    ``forward`` returning (q, k, v)), the GDN z|b|a input projections
+    (qwen3_5.rs:383-435) and the gate|up fusion (qwen3_next.rs:406-447).
+    The views are row-strided when there are several rows; the library's
+    matmuls accept them as x directly."""
+
+    def __init__(self, linear: QuantizedLinear, sizes):
+        if sum(sizes) != linear.out_features:
+            raise ValueError(f"plane sizes {list(sizes)} do not add up to {linear.out_features} rows")
+        self.linear, self.sizes = linear, tuple(int(n) for n in sizes)
+
+    @classmethod
+    def from_linears(cls, linears):
+        """Concatenate quantized linears that share input width, group size,
+        bits and mode (and have no linear bias or global scale)."""
+        first = linears[0]
+        for l in linears:
+            if (l.in_features, l.group_size, l.bits, l.mode) != (first.in_features, first.group_size, first.bits,
+                                                                 first.mode):
+                raise ValueError("fused planes must share input width and quantization")
+            if l.bias is not None or l.global_scale is not None:
+                raise ValueError("fused planes take no linear bias or global scale")
+        cat = lambda ts: torch.cat(ts, 0).contiguous()  # noqa: E731
+        fused = QuantizedLinear(cat([l.weight for l in linears]), cat([l.scales for l in linears]),
+                                cat([l.biases for l in linears]) if first.biases is not None else None,
+                                first.group_size, first.bits, first.mode)
+        return cls(fused, [l.out_features for l in linears])
+
+    def forward(self, x: torch.Tensor, out=None):
+        y = self.linear(x, out=out)
+        views, c = [], 0
+        for n in self.sizes:
+            views.append(y[..., c:c + n])
+            c += n
+        return tuple(views)
+
+    __call__ = forward
+
+
 class QuantizedMlp:
     """Dense SwiGLU MLP over three QuantizedLinear projections, after the
     reference's ``Mlp`` (qwen3_next.rs:449-487).  The gate and up projections

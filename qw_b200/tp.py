@@ -184,3 +184,46 @@ def gather_columns(shards: Sequence, lin: synth.Linear, dims: StackDims = BASELI
         out.extend(np.asarray(s)[..., base_local:base_local + per] for s in shards)
         base_local += per
     return np.concatenate(out, axis=-1)
+
+
+class PeerAllreduce:
+    """fp32 partial sums of a row-parallel projection summed over the ranks of
+    a torch.distributed group (one process per GPU of one node) by the
+    library's one-shot NVLink kernel (qw_allreduce_sum), with the fp16
+    rounding fused: the exchange step of the tensor-parallel stack in place
+    of ncclAllReduce + a cast.  The IPC handles travel over `group` (any
+    backend) once, at construction."""
+
+    def __init__(self, max_elems: int, group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+        self._lib = _lib
+        L = _lib.load()
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        comm = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(_lib.QW_IPC_HANDLE_BYTES)
+        _lib.check(L.qw_allreduce_init(world, rank, int(max_elems), ctypes.byref(comm), handle))
+        self._comm = comm
+        mine = list(handle.raw)
+        gathered = [None] * world
+        dist.all_gather_object(gathered, mine, group=group)
+        blob = bytes(b for h in gathered for b in h)
+        _lib.check(L.qw_allreduce_connect(self._comm, blob))
+        dist.barrier(group=group)
+        self.world, self.rank, self.max_elems = world, rank, int(max_elems)
+
+    def __call__(self, partial, out):
+        """out (fp16 or fp32) = sum over ranks of partial (fp32, same numel)."""
+        from .ops import _arr, _stream
+        self._lib.check(self._lib.load().qw_allreduce_sum(self._comm, _arr(partial), _arr(out), _stream(partial)))
+        return out
+
+    def close(self):
+        if self._comm:
+            self._lib.load().qw_allreduce_destroy(self._comm)
+            self._comm = None
