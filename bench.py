@@ -546,6 +546,9 @@ def run_ours(args):
                 "path": "qw_quantized_matmul per layer via ctypes, eager, pinned host x in / logits out"},
         "gpu_launches": launches * args.steps,
         "clocks": clocks,
+        # a kernel whose bounded wait ran out (a missing peer, a stalled pipeline)
+        # leaves a code here; 0 means every wait of the run completed
+        "device_status": qw.device_status(local, clear=False),
         "extra": extra,
     }
     achieved = step_bytes / (ms * 1e-3) / 1e9

@@ -97,8 +97,13 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p,
     st_release_sys(p.flags[threadIdx.x] + ((size_t)par * kArMaxRanks + p.rank) * kArMaxChunks + b, e);
   }
 
-  // 2. wait for every rank's flag of this chunk, then sum it
-  if (threadIdx.x < p.P) {
+  // 2. wait for every rank's flag of this chunk, then sum it.  Once a call
+  //    has given up (a peer missing), later calls do not wait again: the
+  //    status stays set until the host clears it, and every call returns at
+  //    once, so a broken job ends in its own time instead of 2 s per call.
+  if (threadIdx.x < p.P && *(volatile unsigned int*)p.status == kDevTimeoutPeer) s_ok = 0;
+  __syncthreads();
+  if (threadIdx.x < p.P && s_ok) {
     const unsigned int* f = p.flags[p.rank] + ((size_t)par * kArMaxRanks + threadIdx.x) * kArMaxChunks + b;
     if ((int)(ld_acquire_sys(f) - e) < 0) {
       const uint64_t t0 = globaltimer_ns();
