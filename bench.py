@@ -637,13 +637,29 @@ def run_reference(args):
 
 
 def run_case(args):
-    """One quantized matmul shape, 4 rotating weight copies (> L2 for the
-    BASELINE shapes); prints one JSON line.  Used for ncu captures."""
+    """One kernel on one shape; prints one JSON line.  Used for ncu captures.
+
+    M,N,K          quantized matmul, 4 rotating weight copies (> L2 for the
+                   BASELINE shapes)
+    swiglu:M,I,K   fused SwiGLU gate/up, I rows each (4 rotating copies)
+    topk:M,N,k     top-k of M rows of N fp16 logits"""
     import torch
     import qw_b200 as qw
-    M, N, K = (int(v) for v in args.case.split(","))
+    kind, _, spec = args.case.rpartition(":")
     dev = torch.device("cuda", 0)
-    us, gbs = kernel_microbench(torch, qw, M, N, K, dev, copies=4, iters=args.steps)
+    if kind == "topk":
+        M, N, k = (int(v) for v in spec.split(","))
+        lg = (torch.randn(M, N, device=dev) * 3).half()
+        us = graph_time_us(torch, lambda: qw.topk(lg, k), dev, iters=max(3, args.steps))
+        print(json.dumps({"case": ["topk", M, N, k], "us": round(us, 3),
+                          "GBps_logits_read": round(2.0 * M * N / (us * 1e-6) / 1e9, 1)}), flush=True)
+        return
+    M, N, K = (int(v) for v in spec.split(","))
+    if kind == "swiglu":
+        us, gbs = kernel_microbench(torch, qw, M, 2 * N, K, dev, copies=4, iters=args.steps, swiglu=True)
+        N = 2 * N
+    else:
+        us, gbs = kernel_microbench(torch, qw, M, N, K, dev, copies=4, iters=args.steps)
     hbm_peak, _, src = peaks()
     print(json.dumps({"case": [M, N, K], "us": round(us, 3), "GBps": round(gbs, 1),
                       "frac_hbm": round(gbs / hbm_peak, 4), "peak_source": src,
@@ -662,7 +678,8 @@ def main():
     ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
                     help="exchange of the row-parallel partial sums under torchrun")
     ap.add_argument("--case", default=None,
-                    help="M,N,K: time one quantized matmul shape only (small device footprint, for ncu)")
+                    help="M,N,K | swiglu:M,I,K | topk:M,N,k: time one kernel on one shape only "
+                         "(small device footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
