@@ -177,3 +177,56 @@ def test_misaligned_weights_rejected():
     w_mis = _arr([256, 64], _lib.QW_U32, ptr=0x1004)
     assert _qmm(x, w_mis, s, b, y=y) == _lib.QW_EINVAL
     assert "aligned" in err()
+
+
+# ---- the later entry points' argument checks (all before any device work)
+
+def test_swiglu_requires_matching_gate_and_up():
+    L = _lib.load()
+    x, w, s, b, _ = std_args(N=256)
+    w_up, s_up, b_up = _arr([128, 64], _lib.QW_U32), _arr([128, 8], _lib.QW_F16), _arr([128, 8], _lib.QW_F16)
+    y = _arr([1, 256], _lib.QW_F16)
+    assert L.qw_quantized_matmul_swiglu(x, w, s, b, w_up, s_up, b_up, 1, 64, 4, b"affine", y, None) == \
+        _lib.QW_EINVAL
+    assert "same shape" in err()
+    assert L.qw_quantized_matmul_swiglu(x, w, s, b, w, s, None, 1, 64, 4, b"affine", y, None) == _lib.QW_EINVAL
+    assert "requires biases" in err()
+    assert L.qw_quantized_matmul_swiglu(x, w, s, b, w, s, b, 1, 64, 2, b"affine", y, None) in \
+        (_lib.QW_EINVAL, _lib.QW_EUNSUPPORTED)
+
+
+def test_swiglu_activation_shapes():
+    L = _lib.load()
+    g, u = _arr([2, 8], _lib.QW_F16), _arr([2, 8], _lib.QW_F16)
+    assert L.qw_swiglu_activation(g, _arr([8, 2], _lib.QW_F16), _arr([2, 8], _lib.QW_F16), None) == _lib.QW_EINVAL
+    assert L.qw_swiglu_activation(g, u, _arr([2, 8], _lib.QW_F32), None) == _lib.QW_EUNSUPPORTED
+
+
+@pytest.mark.parametrize("k,code", [(0, _lib.QW_EINVAL), (4096, _lib.QW_EINVAL), (5000, _lib.QW_EINVAL),
+                                    (1025, _lib.QW_EUNSUPPORTED)])
+def test_topk_bounds(k, code):
+    L = _lib.load()
+    logits = _arr([2, 4096], _lib.QW_F16)
+    idx = _arr([2, max(k, 1)], _lib.QW_U32)
+    assert L.qw_topk(logits, k, idx, None, None) == code
+
+
+def test_topk_output_shapes():
+    L = _lib.load()
+    logits = _arr([2, 4096], _lib.QW_F16)
+    assert L.qw_topk(logits, 16, _arr([2, 8], _lib.QW_U32), None, None) == _lib.QW_EINVAL
+    assert L.qw_topk(logits, 16, _arr([2, 16], _lib.QW_F16), None, None) == _lib.QW_EINVAL
+    assert L.qw_topk(logits, 16, _arr([2, 16], _lib.QW_U32), _arr([2, 16], _lib.QW_F32), None) == _lib.QW_EINVAL
+    assert L.qw_topk(_arr([2, 4096], _lib.QW_F32), 16, _arr([2, 16], _lib.QW_U32), None, None) == \
+        _lib.QW_EUNSUPPORTED
+
+
+def test_allreduce_init_bounds():
+    L = _lib.load()
+    comm = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(_lib.QW_IPC_HANDLE_BYTES)
+    assert L.qw_allreduce_init(9, 0, 1024, ctypes.byref(comm), h) == _lib.QW_EUNSUPPORTED
+    assert L.qw_allreduce_init(2, 2, 1024, ctypes.byref(comm), h) == _lib.QW_EINVAL
+    assert L.qw_allreduce_init(2, 0, 0, ctypes.byref(comm), h) == _lib.QW_EINVAL
+    assert L.qw_allreduce_sum(None, _arr([4], _lib.QW_F32), _arr([4], _lib.QW_F16), None) == _lib.QW_EINVAL
+    assert L.qw_allreduce_destroy(None) == _lib.QW_OK
