@@ -39,27 +39,34 @@ namespace {
 
 constexpr int kGroup = 64;
 constexpr int BM = 128;       // weight rows per tile (UMMA M, TMEM lanes)
-constexpr int BT = 256;       // tokens per tile (UMMA N)
-constexpr int STAGES = 4;     // pipeline depth (x box, packed W, TMEM A)
-constexpr int X_STAGE = BT * 128;          // 32 KB
-constexpr int OFF_X = 0;
-// barriers: xfull, wpfull, wpempty, afull, aempty (per stage), dfull, dempty
-constexpr int NBAR = 5 * STAGES + 2;
-// Packed codes of one 64-wide k block: BITS/2 words (4-bit: 8, 8-bit: 16) per row.
-template <int BITS>
+// Packed codes of one 64-wide k block: BITS/2 words (4-bit: 8, 8-bit: 16) per
+// row.  BT tokens per tile (UMMA N): 256 for prefill; 32 for calls of at most
+// 32 rows of x (the configurations without the decode kernel: 8-bit codes,
+// groups of 128, and 17..32 rows), whose narrow x tiles leave room for a
+// deeper pipeline of weight blocks.
+template <int BITS, int BT_>
 struct PfCfg {
+  static constexpr int BT = BT_;
+  static constexpr int STAGES = BT >= 128 ? 4 : 8;  // pipeline depth (x box, packed W, TMEM A)
+  static constexpr int X_STAGE = BT * 128;          // 64 halves of k per token row
   static constexpr int WP_ROW = kGroup * BITS / 8;   // bytes per row per k block
   static constexpr int WORDS = kGroup * BITS / 32;   // packed words per row per k block
   static constexpr int WP_STAGE = BM * WP_ROW;
+  static constexpr int OFF_X = 0;
   static constexpr int OFF_WP = STAGES * X_STAGE;
+  // barriers: xfull, wpfull, wpempty, afull, aempty (per stage), dfull, dempty
+  static constexpr int NBAR = 5 * STAGES + 2;
   static constexpr int OFF_BAR = OFF_WP + STAGES * WP_STAGE;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 64 + 1024;
+  // TMEM: D (BT fp32 columns) at 0, then the A stages (32 columns each)
+  static constexpr uint32_t D_COL = 0;
+  static constexpr uint32_t A_COL = BT >= 128 ? BT : 128;
+  static constexpr uint32_t TMEM_COLS = A_COL + 32 * STAGES <= 256 ? 256 : 512;
+  static_assert(A_COL + 32 * STAGES <= 512, "TMEM columns");
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 constexpr int DQW = 8;             // dequant / epilogue warps: 2 per TMEM lane quarter
 constexpr int THREADS = (2 + DQW) * 32;
-constexpr uint32_t TMEM_COLS = 512;  // D: 256 columns, A stages: 4 x 32
-constexpr uint32_t D_COL = 0;
-constexpr uint32_t A_COL = 256;
 
 struct PrefillParams {
   int M, N, K;
@@ -114,13 +121,18 @@ __device__ __forceinline__ void dequant_group_slow(const uint32_t (&wd)[4], __ha
   }
 }
 
-template <int BITS>
+template <int BITS, int BT_>
 __global__ void __launch_bounds__(THREADS, 1)
     qmm_prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                        const __grid_constant__ CUtensorMap tm_w2, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  using Cfg = PfCfg<BITS>;
+  using Cfg = PfCfg<BITS, BT_>;
+  constexpr int BT = Cfg::BT;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int X_STAGE = Cfg::X_STAGE;
+  constexpr int OFF_X = Cfg::OFF_X;
+  constexpr uint32_t D_COL = Cfg::D_COL, A_COL = Cfg::A_COL, TMEM_COLS = Cfg::TMEM_COLS;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
   uint64_t* xfull = bars;
   uint64_t* wpfull = bars + STAGES;
@@ -409,16 +421,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 bool prefill_available() { return true; }
 
 namespace {
-template <int BITS>
+template <int BITS, int BT>
 cudaError_t launch_cfg(const PrefillArgs& a, cudaStream_t stream, bool pdl, std::string* err) {
-  using Cfg = PfCfg<BITS>;
+  using Cfg = PfCfg<BITS, BT>;
   int dev = 0;
   cudaGetDevice(&dev);
   const DeviceInfo& di = device_info(dev);
   static thread_local int configured_dev = -1;
   if (configured_dev != dev) {
     cudaError_t e =
-        cudaFuncSetAttribute(qmm_prefill_kernel<BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+        cudaFuncSetAttribute(qmm_prefill_kernel<BITS, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
@@ -464,7 +476,7 @@ cudaError_t launch_cfg(const PrefillArgs& a, cudaStream_t stream, bool pdl, std:
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, qmm_prefill_kernel<BITS>, tx, tw, tw2, p);
+  return cudaLaunchKernelEx(&cfg, qmm_prefill_kernel<BITS, BT>, tx, tw, tw2, p);
 }
 }  // namespace
 
@@ -473,7 +485,9 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream, bool pdl, 
     *err = "the prefill kernel takes 4- or 8-bit codes in groups of 64 or 128";
     return cudaErrorInvalidValue;
   }
-  return a.bits == 4 ? launch_cfg<4>(a, stream, pdl, err) : launch_cfg<8>(a, stream, pdl, err);
+  // narrow token tiles for at most 32 rows of x
+  if (a.M <= 32) return a.bits == 4 ? launch_cfg<4, 32>(a, stream, pdl, err) : launch_cfg<8, 32>(a, stream, pdl, err);
+  return a.bits == 4 ? launch_cfg<4, 256>(a, stream, pdl, err) : launch_cfg<8, 256>(a, stream, pdl, err);
 }
 
 }  // namespace qw

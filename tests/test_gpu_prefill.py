@@ -31,7 +31,9 @@ def _clean_status(cuda_dev):
     assert qw_b200.device_status(0) == 0, "a kernel gave up on a bounded wait"
 
 
-@pytest.mark.parametrize("M,N,K", [(17, 128, 64), (64, 256, 512), (256, 384, 1024), (300, 200, 576),
+# M <= 32 runs the 32-token tile (17, 24, 32), above it the 256-token tile
+@pytest.mark.parametrize("M,N,K", [(17, 128, 64), (24, 1000, 5120), (32, 384, 1024), (33, 384, 1024),
+                                   (64, 256, 512), (256, 384, 1024), (300, 200, 576),
                                    (40, 1000, 2048), (513, 136, 5120)])
 def test_prefill_vs_oracle(M, N, K):
     w = synth.weight_fp16(N, K, seed=M + N)

@@ -43,7 +43,7 @@ def test_quantize_and_dequantize_bit_exact(cuda_dev, bits, gs):
 
 
 @pytest.mark.parametrize("bits,gs", CONFIGS)
-@pytest.mark.parametrize("M", [1, 5, 16, 40, 300])
+@pytest.mark.parametrize("M", [1, 5, 16, 32, 33, 40, 300])
 def test_matmul_vs_oracle(cuda_dev, bits, gs, M):
     N, K = 384, 1280 if gs == 64 else 1536
     wq, s, b = oracle.quantize(synth.weight_fp16(N, K, seed=M + bits), group_size=gs, bits=bits)
