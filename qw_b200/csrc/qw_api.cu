@@ -321,9 +321,9 @@ int check_quant_params(const char* mode, bool has_biases, int group_size, int bi
   return QW_OK;
 }
 
-// The checkpoint's configuration (4-bit, groups of 64) has the skinny decode
-// kernel; the other supported ones run on the tensor-core kernel at every M.
-bool skinny_config(int group_size, int bits) { return bits == 4 && group_size == 64; }
+// 4-bit codes (the checkpoint's groups of 64, and groups of 128) have the
+// skinny decode kernel; 8-bit codes run on the tensor-core kernel at every M.
+bool skinny_config(int group_size, int bits) { return bits == 4 && (group_size == 64 || group_size == 128); }
 
 struct WeightDims {
   int64_t N, K, G;
@@ -449,6 +449,7 @@ int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const 
     sa.K = d.K;
     sa.max_ctas = 0;
     sa.status = res->status;
+    sa.group_size = group_size;
     if (up) {
       sa.swiglu = true;
       sa.w2 = (const uint32_t*)up->w->data;
@@ -521,6 +522,7 @@ int check_qmm_call(const qw_array* x, const qw_array* w, const qw_array* scales,
   sa->N = d.N;
   sa->K = d.K;
   sa->x_ld = x_ld;
+  sa->group_size = group_size;
   if (M == 0 || d.N == 0) return QW_OK;
   if (!aligned(x->data, 16)) return fail(QW_EINVAL, "x must be 16-byte aligned");
   if (!aligned(y->data, y->dtype == QW_F32 ? 4 : 2)) return fail(QW_EINVAL, "y is misaligned");
@@ -647,6 +649,7 @@ int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_ar
   sa.max_ctas = 0;
   sa.status = res->status;
   sa.x_ld = x_ld;
+  sa.group_size = group_size;
   Scratch sc;
   if (!scratch_for(dev, stream, skinny_scratch_bytes(sa, dev), &sc, &err)) return fail(QW_ENOMEM, err);
   // keys in the first 256 bytes of the scratch (the chains' tallies use the first 96)

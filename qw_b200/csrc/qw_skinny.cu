@@ -133,7 +133,8 @@ struct SkinnyOp {
   int T;          // row tiles
   long long U;    // T * C
   int G;          // CTAs that take units of this matmul: the first min(grid, U)
-  int sb_tma;     // scales/biases through TMA (needs K % 512 == 0)
+  int sb_tma;     // scales/biases through TMA (needs K % 512 == 0 and groups of 64)
+  int gsh;        // 64-wide groups per quantization group (1: groups of 64, 2: of 128)
   int y_f32;
   int swiglu;
   void* y;
@@ -306,7 +307,8 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
       }
       long long u0;
       const int nunits = units_of(o, &u0);
-      const int G = op.K / kGroup;
+      const int G = op.K / kGroup;  // 64-wide groups of a row
+      const int Gs = G / op.gsh;    // scale and bias columns of a row
       int t = (int)(u0 / op.C), c = (int)(u0 % op.C);
       for (int j = 0; j < nunits; ++j, ++issued) {
         if (issued >= WST && !*abort_flag) {
@@ -314,28 +316,9 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
         }
         if (*abort_flag) break;
         uint8_t* st = wring + slot * Cfg::W_STAGE;
-        if (!op.sb_tma) {
-          // Scales/biases rows are not 16-byte strided (K % 512 != 0): stage
-          // them with plain loads, zero beyond the matrix edge.
-          __half* ss = reinterpret_cast<__half*>(st + Cfg::OFF_WS);
-          __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_WB);
-          for (int e = lane; e < Cfg::BN * kGroupsPerStage; e += 32) {
-            const int r = e / kGroupsPerStage, g = e % kGroupsPerStage;
-            const bool up = op.swiglu && r >= Cfg::BN / 2;
-            const int row = op.swiglu ? t * (Cfg::BN / 2) + (r % (Cfg::BN / 2)) : t * Cfg::BN + r;
-            const int grp = c * kGroupsPerStage + g;
-            __half sv = __float2half(0.f), bv = __float2half(0.f);
-            if (row < op.N && grp < G) {
-              sv = (up ? op.scales2 : op.scales)[(size_t)row * G + grp];
-              bv = (up ? op.biases2 : op.biases)[(size_t)row * G + grp];
-            }
-            ss[e] = sv;
-            sb[e] = bv;
-          }
-          __syncwarp();
-        }
         if (lane == 0) {
-          mbar_arrive_expect_tx(&wfull[slot], w_bytes);
+          if (op.sb_tma) mbar_arrive_expect_tx(&wfull[slot], w_bytes);
+          else mbar_expect_tx(&wfull[slot], w_bytes);
           if (!op.swiglu) {
             tma_load_2d_hint(st, &op.tm_w, &wfull[slot], c * 256, t * Cfg::BN, pol_w);
             tma_load_2d_hint(st + Cfg::W_BOX, &op.tm_w, &wfull[slot], c * 256 + 128, t * Cfg::BN, pol_w);
@@ -362,6 +345,59 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
               tma_load_2d_hint(st + Cfg::OFF_WB + H * 16, &op.tm_b2, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
             }
           }
+        }
+        if (!op.sb_tma) {
+          // Scales/biases staged with plain loads (rows not 16-byte strided
+          // when K % 512 != 0; groups of 128, whose scale serves both 64-wide
+          // groups it covers), zero beyond the matrix edge, after the weight
+          // boxes are on their way; the stage's arrival follows them.
+          __half* ss = reinterpret_cast<__half*>(st + Cfg::OFF_WS);
+          __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_WB);
+          if (op.gsh == 2 && op.K % kChunkK == 0) {
+            // Groups of 128: a chunk holds 4 per row.  One 8-byte load per
+            // row each for scales and biases (all in flight together), each
+            // value then written for both 64-wide groups it covers.
+            uint2 sv4[Cfg::BN / 32], bv4[Cfg::BN / 32];
+#pragma unroll
+            for (int i = 0; i < Cfg::BN / 32; ++i) {
+              const int r = lane + 32 * i;
+              const bool up = op.swiglu && r >= Cfg::BN / 2;
+              const int row = op.swiglu ? t * (Cfg::BN / 2) + (r % (Cfg::BN / 2)) : t * Cfg::BN + r;
+              sv4[i] = bv4[i] = make_uint2(0u, 0u);
+              if (row < op.N) {
+                const size_t off = (size_t)row * Gs + (size_t)c * (kGroupsPerStage / 2);
+                sv4[i] = *reinterpret_cast<const uint2*>((up ? op.scales2 : op.scales) + off);
+                bv4[i] = *reinterpret_cast<const uint2*>((up ? op.biases2 : op.biases) + off);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < Cfg::BN / 32; ++i) {
+              const int r = lane + 32 * i;
+              // halves (h0 h1 h2 h3) -> (h0 h0 h1 h1 h2 h2 h3 h3)
+              *reinterpret_cast<uint4*>(ss + r * kGroupsPerStage) =
+                  make_uint4(prmt(sv4[i].x, 0u, 0x1010u), prmt(sv4[i].x, 0u, 0x3232u), prmt(sv4[i].y, 0u, 0x1010u),
+                             prmt(sv4[i].y, 0u, 0x3232u));
+              *reinterpret_cast<uint4*>(sb + r * kGroupsPerStage) =
+                  make_uint4(prmt(bv4[i].x, 0u, 0x1010u), prmt(bv4[i].x, 0u, 0x3232u), prmt(bv4[i].y, 0u, 0x1010u),
+                             prmt(bv4[i].y, 0u, 0x3232u));
+            }
+          } else {
+            for (int e = lane; e < Cfg::BN * kGroupsPerStage; e += 32) {
+              const int r = e / kGroupsPerStage, g = e % kGroupsPerStage;
+              const bool up = op.swiglu && r >= Cfg::BN / 2;
+              const int row = op.swiglu ? t * (Cfg::BN / 2) + (r % (Cfg::BN / 2)) : t * Cfg::BN + r;
+              const int grp = c * kGroupsPerStage + g;
+              __half sv = __float2half(0.f), bv = __float2half(0.f);
+              if (row < op.N && grp < G) {
+                sv = (up ? op.scales2 : op.scales)[(size_t)row * Gs + grp / op.gsh];
+                bv = (up ? op.biases2 : op.biases)[(size_t)row * Gs + grp / op.gsh];
+              }
+              ss[e] = sv;
+              sb[e] = bv;
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&wfull[slot]);
         }
         __syncwarp();
         if (++slot == WST) {
@@ -877,7 +913,8 @@ bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
   const int tile_rows = a.swiglu ? Cfg::BN / 2 : Cfg::BN;
   op->T = (int)((a.N + tile_rows - 1) / tile_rows);
   op->U = (long long)op->T * op->C;
-  op->sb_tma = (a.K % kChunkK == 0) ? 1 : 0;
+  op->gsh = a.group_size / kGroup;
+  op->sb_tma = (a.K % kChunkK == 0 && op->gsh == 1) ? 1 : 0;
   op->y_f32 = a.y_f32 ? 1 : 0;
   op->swiglu = a.swiglu ? 1 : 0;
   op->y = a.y;

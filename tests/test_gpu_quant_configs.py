@@ -1,9 +1,11 @@
 """The other quantization configurations of QW's per-tensor overrides:
 8-bit codes and groups of 128 (4/128, 8/64, 8/128).  Quantize and dequantize
-are bit-exact with the oracle; the matmul (the tensor-core kernel at every M)
-is within the output tolerance of the oracle, and its fp32 output within
-1e-4 of the float64 product of the bit-exact dequantized weights it uses.
-Entry points that only take 4-bit groups of 64 say so."""
+are bit-exact with the oracle; the matmul is within the output tolerance of
+the oracle, and its fp32 output within 1e-4 of the product it forms: the
+oracle's fp32-formed weights on the decode kernel (4-bit groups of 128 up to
+16 rows), the float64 product of the bit-exact dequantized weights on the
+tensor-core kernel (8-bit codes, and more rows).
+Entry points that only take 4-bit codes say so."""
 import numpy as np
 import pytest
 import torch
@@ -54,8 +56,13 @@ def test_matmul_vs_oracle(cuda_dev, bits, gs, M):
                                    out_dtype=torch.float32)
     torch.cuda.synchronize()
     assert rel_err(y.cpu().numpy(), y_ref) <= TOL
-    y_deq = x.astype(np.float64) @ oracle.dequantize(wq, s, b, group_size=gs, bits=bits).astype(np.float64).T
-    assert rel_err(y32.cpu().numpy(), y_deq) <= 1e-4
+    if bits == 4 and M <= 16:
+        # the decode kernel forms each weight in fp32 as the oracle does
+        assert rel_err(y32.cpu().numpy(), y_ref) <= 1e-4
+    else:
+        # the tensor-core kernel multiplies the bit-exact fp16 dequantized weights
+        y_deq = x.astype(np.float64) @ oracle.dequantize(wq, s, b, group_size=gs, bits=bits).astype(np.float64).T
+        assert rel_err(y32.cpu().numpy(), y_deq) <= 1e-4
 
 
 @pytest.mark.parametrize("bits,gs", CONFIGS)
