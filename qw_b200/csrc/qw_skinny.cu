@@ -1,6 +1,6 @@
-// qw_skinny.cu -- affine 4-bit group-64 quantized matmul for M <= 16 rows of x
-// (decode M=1, MTP verify M=4, DFlash2 block M=16).  HBM-bound: the packed
-// weights are streamed once.
+// qw_skinny.cu -- affine 4-bit quantized matmul (groups of 64 or 128) for
+// M <= 16 rows of x (decode M=1, MTP verify M=4, DFlash2 block M=16).
+// HBM-bound: the packed weights are streamed once.
 //
 // Work decomposition ("stream-K"): the weight matrix is cut into row tiles of
 // BN = 128 rows and the K axis into 512-wide chunks (8 groups).  The T*C
