@@ -127,18 +127,18 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ the GPU arm
-def make_weights(torch, qw, N, K, seed, dev):
+def make_weights(torch, qw, N, K, seed, dev, group_size=64, bits=4):
     """N x K fp16 ~ N(0, 0.02), quantized on the GPU; returns (wq, scales, biases)."""
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
-    wq = torch.empty(N, K // 8, dtype=torch.int32, device=dev)
-    s = torch.empty(N, K // 64, dtype=torch.float16, device=dev)
-    b = torch.empty(N, K // 64, dtype=torch.float16, device=dev)
+    wq = torch.empty(N, K * bits // 32, dtype=torch.int32, device=dev)
+    s = torch.empty(N, K // group_size, dtype=torch.float16, device=dev)
+    b = torch.empty(N, K // group_size, dtype=torch.float16, device=dev)
     rows = max(1, (1 << 27) // K)  # quantize in slabs of ~256 MB of fp16
     for r0 in range(0, N, rows):
         r1 = min(N, r0 + rows)
         w = (torch.randn(r1 - r0, K, generator=g, device=dev, dtype=torch.float32) * 0.02).half()
-        wq_s, s_s, b_s = qw.quantize_weights(w)
+        wq_s, s_s, b_s = qw.quantize_weights(w, group_size=group_size, bits=bits)
         wq[r0:r1].copy_(wq_s)
         s[r0:r1].copy_(s_s)
         b[r0:r1].copy_(b_s)
@@ -339,11 +339,12 @@ def reduce_max(torch, v, dist_on):
     return float(t.item())
 
 
-def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50, swiglu=False):
+def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50, swiglu=False, group_size=64, bits=4):
     """One quantized matmul, rotating `copies` weight sets (> L2) between launches.
     swiglu=True runs the fused SwiGLU over the two row halves of each N-row set
     (N/2 outputs per row of x)."""
-    sets = [make_weights(torch, qw, N, K, seed=7000 + i, dev=dev) for i in range(copies)]
+    sets = [make_weights(torch, qw, N, K, seed=7000 + i, dev=dev, group_size=group_size, bits=bits)
+            for i in range(copies)]
     x = torch.randn(M, K, device=dev).half()
     y = torch.empty(M, N // 2 if swiglu else N, dtype=torch.float16, device=dev)
     if swiglu:
@@ -355,7 +356,7 @@ def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50, swiglu=False)
             qw.quantized_matmul_swiglu(x, *calls[i % copies], out=y)
         else:
             w = sets[i % copies]
-            qw.quantized_matmul(x, w[0], w[1], w[2], out=y)
+            qw.quantized_matmul(x, w[0], w[1], w[2], group_size=group_size, bits=bits, out=y)
 
     with torch.cuda.stream(s):
         for i in range(copies * 2):
@@ -376,7 +377,8 @@ def kernel_microbench(torch, qw, M, N, K, dev, copies=8, iters=50, swiglu=False)
         e1.record(s)
     s.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / (iters * copies)
-    nbytes = synth.algorithmic_bytes(M, N, K) - (2 * M * (N // 2) if swiglu else 0)  # SwiGLU writes N/2
+    nbytes = (N * K * bits // 8 + 4 * N * (K // group_size) + 2 * M * K
+              + 2 * M * (N // 2 if swiglu else N))  # codes, scales + biases, x, y (SwiGLU writes N/2)
     del g, sets
     torch.cuda.empty_cache()
     return us, nbytes / (us * 1e-6) / 1e9
@@ -504,6 +506,12 @@ def run_ours(args):
                 extra[f"qmm_17408x5120_m{M}"] = {"us": round(us, 2), "GBps": round(gbs, 1),
                                                  "frac_hbm": round(gbs / hbm_peak, 4),
                                                  "frac_8TBps": round(gbs / 8000.0, 4)}
+            # the per-tensor override configurations at decode: 4-bit groups of 128
+            # (the decode kernel) and 8-bit groups of 64 (the tensor-core kernel)
+            for bits, gsz in ((4, 128), (8, 64)):
+                us, gbs = kernel_microbench(torch, qw, 1, 17408, 5120, dev, copies=4, group_size=gsz, bits=bits)
+                extra[f"qmm_17408x5120_b{bits}g{gsz}_m1"] = {"us": round(us, 2), "GBps": round(gbs, 1),
+                                                             "frac_hbm": round(gbs / hbm_peak, 4)}
             # the DFlash2 candidate step: lm_head at M=16 then the top 16 of each row
             xl = torch.randn(16, synth.HIDDEN, device=dev).half()
             lg = torch.empty(16, lm[0].shape[0], dtype=torch.float16, device=dev)
