@@ -350,13 +350,14 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
           // Scales/biases staged with plain loads (rows not 16-byte strided
           // when K % 512 != 0; groups of 128, whose scale serves both 64-wide
           // groups it covers), zero beyond the matrix edge, after the weight
-          // boxes are on their way; the stage's arrival follows them.
+          // boxes are on their way; the stage's arrival follows them.  The
+          // stage holds 8 halves (16 bytes) per row.
           __half* ss = reinterpret_cast<__half*>(st + Cfg::OFF_WS);
           __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_WB);
           if (op.gsh == 2 && op.K % kChunkK == 0) {
-            // Groups of 128: a chunk holds 4 per row.  One 8-byte load per
-            // row each for scales and biases (all in flight together), each
-            // value then written for both 64-wide groups it covers.
+            // Groups of 128 with 16-byte strided rows: a chunk holds 4 per
+            // row, one 8-byte load per row each for scales and biases (all in
+            // flight together), each value written for both 64-wide groups.
             uint2 sv4[Cfg::BN / 32], bv4[Cfg::BN / 32];
 #pragma unroll
             for (int i = 0; i < Cfg::BN / 32; ++i) {
@@ -382,18 +383,56 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
                              prmt(bv4[i].y, 0u, 0x3232u));
             }
           } else {
-            for (int e = lane; e < Cfg::BN * kGroupsPerStage; e += 32) {
-              const int r = e / kGroupsPerStage, g = e % kGroupsPerStage;
+            // One row per lane and step, the loads of all four steps in flight
+            // together: the eight 64-wide groups of the chunk as two 8-byte
+            // loads when the row allows (groups of 64, 8-byte aligned, not past
+            // the row's end), one 8-byte load of four group-128 values written
+            // twice each, or element by element at a ragged edge.
+            uint32_t sw[Cfg::BN / 32][4], bw[Cfg::BN / 32][4];
+  #pragma unroll
+            for (int i = 0; i < Cfg::BN / 32; ++i) {
+              const int r = lane + 32 * i;
               const bool up = op.swiglu && r >= Cfg::BN / 2;
               const int row = op.swiglu ? t * (Cfg::BN / 2) + (r % (Cfg::BN / 2)) : t * Cfg::BN + r;
-              const int grp = c * kGroupsPerStage + g;
-              __half sv = __float2half(0.f), bv = __float2half(0.f);
-              if (row < op.N && grp < G) {
-                sv = (up ? op.scales2 : op.scales)[(size_t)row * Gs + grp / op.gsh];
-                bv = (up ? op.biases2 : op.biases)[(size_t)row * Gs + grp / op.gsh];
+              const __half* srow = (up ? op.scales2 : op.scales) + (size_t)row * Gs;
+              const __half* brow = (up ? op.biases2 : op.biases) + (size_t)row * Gs;
+              const int g0 = c * kGroupsPerStage;  // first 64-wide group of the chunk
+  #pragma unroll
+              for (int q = 0; q < 4; ++q) sw[i][q] = bw[i][q] = 0u;
+              if (row >= op.N) continue;
+              if (op.gsh == 1 && g0 + kGroupsPerStage <= G && (((size_t)row * Gs + g0) & 3) == 0) {
+                const uint2 s0 = *reinterpret_cast<const uint2*>(srow + g0);
+                const uint2 s1 = *reinterpret_cast<const uint2*>(srow + g0 + 4);
+                const uint2 b0 = *reinterpret_cast<const uint2*>(brow + g0);
+                const uint2 b1 = *reinterpret_cast<const uint2*>(brow + g0 + 4);
+                sw[i][0] = s0.x; sw[i][1] = s0.y; sw[i][2] = s1.x; sw[i][3] = s1.y;
+                bw[i][0] = b0.x; bw[i][1] = b0.y; bw[i][2] = b1.x; bw[i][3] = b1.y;
+              } else if (op.gsh == 2 && g0 + kGroupsPerStage <= G && (((size_t)row * Gs + g0 / 2) & 3) == 0) {
+                const uint2 s4 = *reinterpret_cast<const uint2*>(srow + g0 / 2);
+                const uint2 b4 = *reinterpret_cast<const uint2*>(brow + g0 / 2);
+                // halves (h0 h1 h2 h3) -> (h0 h0 h1 h1 h2 h2 h3 h3)
+                sw[i][0] = prmt(s4.x, 0u, 0x1010u); sw[i][1] = prmt(s4.x, 0u, 0x3232u);
+                sw[i][2] = prmt(s4.y, 0u, 0x1010u); sw[i][3] = prmt(s4.y, 0u, 0x3232u);
+                bw[i][0] = prmt(b4.x, 0u, 0x1010u); bw[i][1] = prmt(b4.x, 0u, 0x3232u);
+                bw[i][2] = prmt(b4.y, 0u, 0x1010u); bw[i][3] = prmt(b4.y, 0u, 0x3232u);
+              } else {
+  #pragma unroll
+                for (int g = 0; g < kGroupsPerStage; ++g) {
+                  const int grp = g0 + g;
+                  if (grp < G) {
+                    const uint32_t sv = __half_as_ushort(srow[grp / op.gsh]);
+                    const uint32_t bv = __half_as_ushort(brow[grp / op.gsh]);
+                    sw[i][g / 2] |= sv << (16 * (g & 1));
+                    bw[i][g / 2] |= bv << (16 * (g & 1));
+                  }
+                }
               }
-              ss[e] = sv;
-              sb[e] = bv;
+            }
+  #pragma unroll
+            for (int i = 0; i < Cfg::BN / 32; ++i) {
+              const int r = lane + 32 * i;
+              *reinterpret_cast<uint4*>(ss + r * kGroupsPerStage) = make_uint4(sw[i][0], sw[i][1], sw[i][2], sw[i][3]);
+              *reinterpret_cast<uint4*>(sb + r * kGroupsPerStage) = make_uint4(bw[i][0], bw[i][1], bw[i][2], bw[i][3]);
             }
           }
           __syncwarp();
