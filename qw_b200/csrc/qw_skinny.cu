@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
             // the row's end), one 8-byte load of four group-128 values written
             // twice each, or element by element at a ragged edge.
             uint32_t sw[Cfg::BN / 32][4], bw[Cfg::BN / 32][4];
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < Cfg::BN / 32; ++i) {
               const int r = lane + 32 * i;
               const bool up = op.swiglu && r >= Cfg::BN / 2;
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
               const __half* srow = (up ? op.scales2 : op.scales) + (size_t)row * Gs;
               const __half* brow = (up ? op.biases2 : op.biases) + (size_t)row * Gs;
               const int g0 = c * kGroupsPerStage;  // first 64-wide group of the chunk
-  #pragma unroll
+#pragma unroll
               for (int q = 0; q < 4; ++q) sw[i][q] = bw[i][q] = 0u;
               if (row >= op.N) continue;
               if (op.gsh == 1 && g0 + kGroupsPerStage <= G && (((size_t)row * Gs + g0) & 3) == 0) {
@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
                 bw[i][0] = prmt(b4.x, 0u, 0x1010u); bw[i][1] = prmt(b4.x, 0u, 0x3232u);
                 bw[i][2] = prmt(b4.y, 0u, 0x1010u); bw[i][3] = prmt(b4.y, 0u, 0x3232u);
               } else {
-  #pragma unroll
+#pragma unroll
                 for (int g = 0; g < kGroupsPerStage; ++g) {
                   const int grp = g0 + g;
                   if (grp < G) {
@@ -428,7 +428,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
                 }
               }
             }
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < Cfg::BN / 32; ++i) {
               const int r = lane + 32 * i;
               *reinterpret_cast<uint4*>(ss + r * kGroupsPerStage) = make_uint4(sw[i][0], sw[i][1], sw[i][2], sw[i][3]);
