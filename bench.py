@@ -650,6 +650,7 @@ def run_case(args):
     M,N,K          quantized matmul, 4 rotating weight copies (> L2 for the
                    BASELINE shapes)
     swiglu:M,I,K   fused SwiGLU gate/up, I rows each (4 rotating copies)
+    b8:M,N,K       quantized matmul of 8-bit codes (groups of 64)
     topk:M,N,k     top-k of M rows of N fp16 logits"""
     import torch
     import qw_b200 as qw
@@ -667,7 +668,8 @@ def run_case(args):
         us, gbs = kernel_microbench(torch, qw, M, 2 * N, K, dev, copies=4, iters=args.steps, swiglu=True)
         N = 2 * N
     else:
-        us, gbs = kernel_microbench(torch, qw, M, N, K, dev, copies=4, iters=args.steps)
+        us, gbs = kernel_microbench(torch, qw, M, N, K, dev, copies=4, iters=args.steps,
+                                    bits=8 if kind == "b8" else 4)
     hbm_peak, _, src = peaks()
     print(json.dumps({"case": [M, N, K], "us": round(us, 3), "GBps": round(gbs, 1),
                       "frac_hbm": round(gbs / hbm_peak, 4), "peak_source": src,
@@ -686,7 +688,7 @@ def main():
     ap.add_argument("--tp-allreduce", choices=["peer", "nccl"], default="peer",
                     help="exchange of the row-parallel partial sums under torchrun")
     ap.add_argument("--case", default=None,
-                    help="M,N,K | swiglu:M,I,K | topk:M,N,k: time one kernel on one shape only "
+                    help="M,N,K | swiglu:M,I,K | b8:M,N,K | topk:M,N,k: time one kernel on one shape only "
                          "(small device footprint, for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -321,9 +321,12 @@ int check_quant_params(const char* mode, bool has_biases, int group_size, int bi
   return QW_OK;
 }
 
-// 4-bit codes (the checkpoint's groups of 64, and groups of 128) have the
-// skinny decode kernel; 8-bit codes run on the tensor-core kernel at every M.
-bool skinny_config(int group_size, int bits) { return bits == 4 && (group_size == 64 || group_size == 128); }
+// Every supported configuration (4- or 8-bit codes in groups of 64 or 128)
+// has the skinny decode kernel; chained launches take 4-bit codes.
+bool skinny_config(int group_size, int bits) {
+  return (bits == 4 || bits == 8) && (group_size == 64 || group_size == 128);
+}
+bool skinny_chain_config(int group_size, int bits) { return bits == 4 && skinny_config(group_size, bits); }
 
 struct WeightDims {
   int64_t N, K, G;
@@ -450,6 +453,7 @@ int run_qmm(const qw_array* x, const qw_array* w, const qw_array* scales, const 
     sa.max_ctas = 0;
     sa.status = res->status;
     sa.group_size = group_size;
+    sa.bits = bits;
     if (up) {
       sa.swiglu = true;
       sa.w2 = (const uint32_t*)up->w->data;
@@ -523,6 +527,7 @@ int check_qmm_call(const qw_array* x, const qw_array* w, const qw_array* scales,
   sa->K = d.K;
   sa->x_ld = x_ld;
   sa->group_size = group_size;
+  sa->bits = bits;
   if (M == 0 || d.N == 0) return QW_OK;
   if (!aligned(x->data, 16)) return fail(QW_EINVAL, "x must be 16-byte aligned");
   if (!aligned(y->data, y->dtype == QW_F32 ? 4 : 2)) return fail(QW_EINVAL, "y is misaligned");
@@ -560,7 +565,7 @@ int qw_quantized_matmul_chain(const qw_qmm_op* ops, int n_ops, int group_size, i
                                  " rows of x, op 0 has " + std::to_string(args[0].M));
   }
   const int64_t M = args[0].M;
-  if (M > 16 || args[0].M == 0 || !skinny_config(group_size, bits)) {
+  if (M > 16 || args[0].M == 0 || !skinny_chain_config(group_size, bits)) {
     // Prefill-sized (or empty) chains: one launch per matmul, in order.
     for (int i = 0; i < n_ops; ++i) {
       const qw_qmm_op& o = ops[i];
@@ -628,8 +633,7 @@ int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_ar
   std::string err;
   if (M > 16 || !skinny_config(group_size, bits)) {
     if (!logits)
-      return fail(QW_EINVAL, "a logits buffer is required when x has more than 16 rows or the weights are not "
-                             "4-bit in groups of 64");
+      return fail(QW_EINVAL, "a logits buffer is required when x has more than 16 rows");
     if ((rc = run_qmm(x, w, scales, biases, 1, group_size, bits, mode, logits, stream_v))) return rc;
     ce = launch_argmax_rows(logits->data, M, d.N, (uint32_t*)idx->data, stream);
     return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "argmax launch");
@@ -650,6 +654,7 @@ int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_ar
   sa.status = res->status;
   sa.x_ld = x_ld;
   sa.group_size = group_size;
+  sa.bits = bits;
   Scratch sc;
   if (!scratch_for(dev, stream, skinny_scratch_bytes(sa, dev), &sc, &err)) return fail(QW_ENOMEM, err);
   // keys in the first 256 bytes of the scratch (the chains' tallies use the first 96)

@@ -51,7 +51,8 @@ struct SkinnyArgs {
   unsigned int* status;  // device status word
   int64_t x_ld = 0;      // elements from one row of x to the next (0 = K)
   unsigned long long* amax = nullptr;  // greedy-token keys [M], zeroed by the caller (y may be null)
-  int group_size = 64;   // 64 or 128 (4-bit codes)
+  int group_size = 64;   // 64 or 128
+  int bits = 4;          // 4 or 8
   // SwiGLU (gate and up of an MLP, activation fused): w/scales/biases are the
   // gate projection's, w2/scales2/biases2 the up projection's, both [N] rows,
   // and y [M][N] = silu(x gate^T) * (x up^T).

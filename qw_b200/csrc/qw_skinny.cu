@@ -73,19 +73,23 @@ constexpr int align1k(int v) { return (v + 1023) / 1024 * 1024; }
 //     kernel's bytes-in-flight budget against HBM latency.
 //   small ring (SST stages): the unit's x box and what the helper warps derive
 //     from it (MMA B fragments, per-group X / Z sums).  x comes from L2.
-template <int MT>
+template <int MT, int BITS = 4>
 struct SkinnyCfg {
   static constexpr int NT = (MT + 7) / 8;       // n8 MMA column tiles
   static constexpr int MPAD_ = 8 * NT;
   static constexpr int CW = 8;                  // consumer warps: 16 rows x all 8 groups of a unit each
   static constexpr int HW = MT == 1 ? 1 : (MT <= 8 ? 2 : 3);  // helper warps
   static constexpr int BN = 128;                // rows per tile
-  static constexpr int WST = MT == 1 ? 5 : (MT <= 8 ? 4 : 3);
-  static constexpr int SST = MT == 1 ? 4 : (MT <= 8 ? 3 : 2);
+  // A stage's 512-wide chunk is 256 bytes of 4-bit codes per row (two SW128
+  // boxes of 128 bytes) or 512 bytes of 8-bit codes (four boxes), so 8-bit
+  // stages are twice as large and the rings shallower.
+  static constexpr int NBOX = BITS == 8 ? 4 : 2;
+  static constexpr int WST = BITS == 8 ? (MT == 1 ? 3 : 2) : (MT == 1 ? 5 : (MT <= 8 ? 4 : 3));
+  static constexpr int SST = BITS == 8 ? 2 : (MT == 1 ? 4 : (MT <= 8 ? 3 : 2));
   static constexpr int W_BOX = BN * 128;
   static constexpr int SB_BYTES = BN * 16;
-  static constexpr int W_STAGE = 2 * W_BOX + 2 * SB_BYTES;  // W boxes, scales, biases
-  static constexpr int OFF_WS = 2 * W_BOX;
+  static constexpr int W_STAGE = NBOX * W_BOX + 2 * SB_BYTES;  // W boxes, scales, biases
+  static constexpr int OFF_WS = NBOX * W_BOX;
   static constexpr int OFF_WB = OFF_WS + SB_BYTES;
   static constexpr int X_BYTES = kGroupsPerStage * MT * 128;
   static constexpr int BF_TOK = MT;
@@ -173,6 +177,11 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
@@ -220,10 +229,10 @@ __device__ __forceinline__ bool wait_matmuls_done(const unsigned int* gbar, unsi
   return true;
 }
 
-template <int MT, int OPS_MAX>
-__global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyCfg<MT>::MAXREG)
+template <int MT, int OPS_MAX, int BITS>
+__global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__((SkinnyCfg<MT, BITS>::MAXREG))
     qmm_skinny_kernel(const __grid_constant__ SkinnyLaunch<OPS_MAX> p) {
-  using Cfg = SkinnyCfg<MT>;
+  using Cfg = SkinnyCfg<MT, BITS>;
   constexpr int NT = Cfg::NT;
   constexpr int WST = Cfg::WST;
   constexpr int SST = Cfg::SST;
@@ -290,7 +299,7 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
     uint32_t phase = 0;
     for (int o = 0; o < (OPS_MAX == 1 ? 1 : p.n_ops); ++o) {
       const SkinnyOp& op = p.op[OPS_MAX == 1 ? 0 : o];
-      const uint32_t w_bytes = 2 * Cfg::W_BOX + (op.sb_tma ? 2 * Cfg::SB_BYTES : 0);
+      const uint32_t w_bytes = Cfg::NBOX * Cfg::W_BOX + (op.sb_tma ? 2 * Cfg::SB_BYTES : 0);
       if (lane == 0) {
         prefetch_tensormap(&op.tm_w);
         if (op.sb_tma) {
@@ -319,9 +328,12 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
         if (lane == 0) {
           if (op.sb_tma) mbar_arrive_expect_tx(&wfull[slot], w_bytes);
           else mbar_expect_tx(&wfull[slot], w_bytes);
+          // byte column of the chunk: 512 codes of BITS bits
+          const int cx = c * (Cfg::NBOX * 128);
           if (!op.swiglu) {
-            tma_load_2d_hint(st, &op.tm_w, &wfull[slot], c * 256, t * Cfg::BN, pol_w);
-            tma_load_2d_hint(st + Cfg::W_BOX, &op.tm_w, &wfull[slot], c * 256 + 128, t * Cfg::BN, pol_w);
+#pragma unroll
+            for (int bx = 0; bx < Cfg::NBOX; ++bx)
+              tma_load_2d_hint(st + bx * Cfg::W_BOX, &op.tm_w, &wfull[slot], cx + bx * 128, t * Cfg::BN, pol_w);
             if (op.sb_tma) {
               tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
               tma_load_2d_hint(st + Cfg::OFF_WB, &op.tm_b, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
@@ -333,10 +345,9 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
             constexpr int H = Cfg::BN / 2;
             const int r0 = t * H;
 #pragma unroll
-            for (int bx = 0; bx < 2; ++bx) {
-              tma_load_2d_hint(st + bx * Cfg::W_BOX, &op.tm_w, &wfull[slot], c * 256 + bx * 128, r0, pol_w);
-              tma_load_2d_hint(st + bx * Cfg::W_BOX + H * 128, &op.tm_w2, &wfull[slot], c * 256 + bx * 128, r0,
-                               pol_w);
+            for (int bx = 0; bx < Cfg::NBOX; ++bx) {
+              tma_load_2d_hint(st + bx * Cfg::W_BOX, &op.tm_w, &wfull[slot], cx + bx * 128, r0, pol_w);
+              tma_load_2d_hint(st + bx * Cfg::W_BOX + H * 128, &op.tm_w2, &wfull[slot], cx + bx * 128, r0, pol_w);
             }
             if (op.sb_tma) {
               tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
@@ -520,6 +531,29 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
           const int gi = MT == 1 ? gn : gn / p.M;
           const int n = MT == 1 ? 0 : gn - gi * p.M;
           const int line = gn;  // box layout [group][token][64 halves]
+          if (BITS == 8) {
+            // Byte codes: MMA block q of the group (k 16q..16q+15) takes, in
+            // lane (token, s), x[16q + 4s .. 16q + 4s + 3] as its two B words,
+            // unscaled; the four blocks' words are stored in q order.
+            uint2 xb[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              xb[q] = lds64(xbase + line * 128 + (((2 * q + (s >> 1)) ^ (line & 7)) << 4) + 8 * (s & 1));
+            const uint32_t fa = bf + ((gi * Cfg::BF_TOK + n) * 4 + s) * 32;
+            sts128(fa, make_uint4(xb[0].x, xb[0].y, xb[1].x, xb[1].y));
+            sts128(fa + 16, make_uint4(xb[2].x, xb[2].y, xb[3].x, xb[3].y));
+            float xs = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&xb[q].x));
+              const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&xb[q].y));
+              xs += (f0.x + f0.y) + (f1.x + f1.y);
+            }
+            xs += __shfl_xor_sync(0xffffffffu, xs, 1);
+            xs += __shfl_xor_sync(0xffffffffu, xs, 2);
+            if (s == 0) sts_f32x2(xz + (gi * Cfg::XZ_COLS + n) * 8, xs, 1024.f * xs);
+            continue;
+          }
           const uint4 xv0 = lds128(xbase + line * 128 + ((s ^ (line & 7)) << 4));
           const uint4 xv1 = lds128(xbase + line * 128 + (((4 + s) ^ (line & 7)) << 4));
           // B fragment of MMA jj: (x[8s+jj], x[8s+jj+4]) and the same 32 further
@@ -657,9 +691,17 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
   // earlier and the shared-memory latency of the copy is hidden behind the
   // MMAs.  (With 16 tokens the register file has no room for this overlap:
   // those warps copy each unit's share when they start it.)
-  constexpr bool kRoll = MT <= 8;
-  uint32_t A[8][4];
+  //
+  // 8-bit codes take twice the registers per unit, so their warps hold two
+  // groups at a time instead: a group is two ldmatrix.x4 loads (64 bytes of
+  // each of 16 rows; load li of the unit covers 16-byte chunks 2(li % 4) and
+  // 2(li % 4) + 1 of box li / 4), group gi + 1 is loaded while group gi is
+  // computed, and the slot is released once the last group's loads are
+  // issued.
+  constexpr bool kRoll = BITS == 4 && MT <= 8;
+  uint32_t A[BITS == 8 ? 4 : 8][4];
   uint4 sv_lo, sv_hi, bv_lo, bv_hi;
+  uint32_t wb_cur = 0;  // 8-bit: the slot of the unit being computed
   auto release_wslot = [&]() {
     __syncwarp();
     if (lane == 0) mbar_arrive(&wempty[wslot]);
@@ -671,14 +713,21 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
   auto copy_unit = [&]() {
     if (!*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
     const uint32_t wb = wring_u + wslot * Cfg::W_STAGE;
+    if (BITS == 8) {
+      wb_cur = wb;
 #pragma unroll
-    for (int gi = 0; gi < 8; ++gi)
-      ldmatrix_x4(wb + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
+      for (int li = 0; li < 2; ++li)  // group 0
+        ldmatrix_x4(wb + lm_off[li], A[li][0], A[li][1], A[li][2], A[li][3]);
+    } else {
+#pragma unroll
+      for (int gi = 0; gi < 8; ++gi)
+        ldmatrix_x4(wb + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
+    }
     sv_lo = lds128(wb + Cfg::OFF_WS + sb_off);
     sv_hi = lds128(wb + Cfg::OFF_WS + sb_off + kSbHi);
     bv_lo = lds128(wb + Cfg::OFF_WB + sb_off);
     bv_hi = lds128(wb + Cfg::OFF_WB + sb_off + kSbHi);
-    release_wslot();
+    if (BITS != 8) release_wslot();
   };
   if (total > 0) copy_unit();
 
@@ -710,13 +759,40 @@ __global__ void __launch_bounds__(SkinnyCfg<MT>::THREADS, 1) __maxnreg__(SkinnyC
           }
           // expanded A registers: e[jj][i] for word i
           uint32_t e[4][4];
+          if (BITS == 8) {
+            // Byte codes: word d of a lane holds codes 4s4..4s4+3 of its
+            // 16-byte chunk; prmt pairs bytes with 0x64 into the exact fp16
+            // values 1024 + q.  MMA block q (k 16q..16q+15 of the group) is
+            // chunk q of the group: the group's load q/2, words (0, 1) or
+            // (2, 3) for the low and high row halves.
+            const int ab = (gi & 1) * 2;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t w8 = A[gi][i] >> 8;
-            e[0][i] = lop3_and_or(A[gi][i], 0x000F000Fu);
-            e[1][i] = lop3_and_or(A[gi][i], 0x00F000F0u);
-            e[2][i] = lop3_and_or(w8, 0x000F000Fu);
-            e[3][i] = lop3_and_or(w8, 0x00F000F0u);
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t lo = A[ab + q / 2][(q & 1) * 2], hi = A[ab + q / 2][(q & 1) * 2 + 1];
+              e[q][0] = prmt(lo, 0x64646464u, 0x5140u);
+              e[q][1] = prmt(hi, 0x64646464u, 0x5140u);
+              e[q][2] = prmt(lo, 0x64646464u, 0x5342u);
+              e[q][3] = prmt(hi, 0x64646464u, 0x5342u);
+            }
+            if (gi + 1 < 8) {
+              const int nb = ((gi + 1) & 1) * 2;
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                const int li = 2 * (gi + 1) + j;
+                ldmatrix_x4(wb_cur + (li / 4) * Cfg::W_BOX + lm_off[li % 4], A[nb + j][0], A[nb + j][1],
+                            A[nb + j][2], A[nb + j][3]);
+              }
+              if (gi + 1 == 7) release_wslot();  // every load of the unit is issued
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t w8 = A[gi][i] >> 8;
+              e[0][i] = lop3_and_or(A[gi][i], 0x000F000Fu);
+              e[1][i] = lop3_and_or(A[gi][i], 0x00F000F0u);
+              e[2][i] = lop3_and_or(w8, 0x000F000Fu);
+              e[3][i] = lop3_and_or(w8, 0x00F000F0u);
+            }
           }
           if (has_next) {
             if (gi == 0 && !*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull))
@@ -942,9 +1018,9 @@ constexpr size_t kGbarBytes = 256;
 static_assert(kSkinnyChainMax * sizeof(unsigned int) <= kGbarBytes, "per-matmul tallies fit");
 
 // One matmul's descriptor: tensor maps and schedule-independent sizes.
-template <int MT>
+template <int MT, int BITS>
 bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
-  using Cfg = SkinnyCfg<MT>;
+  using Cfg = SkinnyCfg<MT, BITS>;
   op->N = (int)a.N;
   op->K = (int)a.K;
   op->C = (int)((a.K + kChunkK - 1) / kChunkK);
@@ -965,12 +1041,13 @@ bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
     *err = "too many row tiles for the skinny path's counter block";
     return false;
   }
-  if (!encode_tmap_2d(&op->tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, (uint64_t)(a.K / 2), (uint64_t)a.N,
-                      (uint64_t)(a.K / 2), 128, tile_rows, CU_TENSOR_MAP_SWIZZLE_128B, err))
+  const uint64_t row_bytes = (uint64_t)a.K * BITS / 8;
+  if (!encode_tmap_2d(&op->tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, row_bytes, (uint64_t)a.N, row_bytes, 128,
+                      tile_rows, CU_TENSOR_MAP_SWIZZLE_128B, err))
     return false;
   if (a.swiglu) {
-    if (!encode_tmap_2d(&op->tm_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w2, (uint64_t)(a.K / 2), (uint64_t)a.N,
-                        (uint64_t)(a.K / 2), 128, tile_rows, CU_TENSOR_MAP_SWIZZLE_128B, err))
+    if (!encode_tmap_2d(&op->tm_w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w2, row_bytes, (uint64_t)a.N, row_bytes, 128,
+                        tile_rows, CU_TENSOR_MAP_SWIZZLE_128B, err))
       return false;
   } else {
     op->tm_w2 = op->tm_w;  // unused
@@ -997,30 +1074,30 @@ bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
   return true;
 }
 
-template <int MT, int OPS_MAX>
+template <int MT, int OPS_MAX, int BITS>
 cudaError_t set_smem_attr(int dev) {
   static thread_local int configured_dev = -1;
   // cudaFuncSetAttribute is per device; cheap enough to repeat on change.
   if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(qmm_skinny_kernel<MT, OPS_MAX>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SkinnyCfg<MT>::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(qmm_skinny_kernel<MT, OPS_MAX, BITS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SkinnyCfg<MT, BITS>::SMEM);
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
   return cudaSuccess;
 }
 
-template <int MT>
+template <int MT, int BITS>
 cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                        std::string* err) {
-  using Cfg = SkinnyCfg<MT>;
+  using Cfg = SkinnyCfg<MT, BITS>;
   int dev = 0;
   cudaGetDevice(&dev);
   const DeviceInfo& di = device_info(dev);
-  cudaError_t e = set_smem_attr<MT, 1>(dev);
+  cudaError_t e = set_smem_attr<MT, 1, BITS>(dev);
   if (e != cudaSuccess) return e;
   SkinnyLaunch<1> p{};
-  if (!make_op<MT>(a, &p.op[0], err)) return cudaErrorInvalidValue;
+  if (!make_op<MT, BITS>(a, &p.op[0], err)) return cudaErrorInvalidValue;
   p.n_ops = 1;
   p.M = (int)a.M;
   const SkinnyOp& op = p.op[0];
@@ -1084,7 +1161,7 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   }
   cfg.attrs = attr;
   cfg.numAttrs = nattr;
-  return cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, 1>, p);
+  return cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, 1, BITS>, p);
 }
 
 // A chain of up to kSkinnyChainMax matmuls in one cooperative launch of one
@@ -1092,18 +1169,18 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
 template <int MT>
 cudaError_t launch_chain_cfg(const SkinnyArgs* ops, int n, const Scratch& scratch, cudaStream_t stream,
                              std::string* err) {
-  using Cfg = SkinnyCfg<MT>;
+  using Cfg = SkinnyCfg<MT, 4>;  // chains take 4-bit codes
   int dev = 0;
   cudaGetDevice(&dev);
   const DeviceInfo& di = device_info(dev);
-  cudaError_t e = set_smem_attr<MT, kSkinnyChainMax>(dev);
+  cudaError_t e = set_smem_attr<MT, kSkinnyChainMax, 4>(dev);
   if (e != cudaSuccess) return e;
   static SkinnyLaunch<kSkinnyChainMax> p;  // large: build it outside the stack (copied at launch)
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
   p = SkinnyLaunch<kSkinnyChainMax>{};
   for (int i = 0; i < n; ++i)
-    if (!make_op<MT>(ops[i], &p.op[i], err)) return cudaErrorInvalidValue;
+    if (!make_op<MT, 4>(ops[i], &p.op[i], err)) return cudaErrorInvalidValue;
   p.n_ops = n;
   p.M = (int)ops[0].M;
   p.G = di.sm_count;
@@ -1134,7 +1211,7 @@ cudaError_t launch_chain_cfg(const SkinnyArgs* ops, int n, const Scratch& scratc
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, kSkinnyChainMax>, p);
+  return cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, kSkinnyChainMax, 4>, p);
 }
 
 }  // namespace
@@ -1155,9 +1232,14 @@ size_t skinny_zeroed_bytes(const SkinnyArgs& a) {
 
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                           std::string* err) {
-  if (a.M == 1) return launch_cfg<1>(a, scratch, stream, pdl, err);
-  if (a.M <= 8) return launch_cfg<8>(a, scratch, stream, pdl, err);
-  return launch_cfg<16>(a, scratch, stream, pdl, err);
+  if (a.bits == 8) {
+    if (a.M == 1) return launch_cfg<1, 8>(a, scratch, stream, pdl, err);
+    if (a.M <= 8) return launch_cfg<8, 8>(a, scratch, stream, pdl, err);
+    return launch_cfg<16, 8>(a, scratch, stream, pdl, err);
+  }
+  if (a.M == 1) return launch_cfg<1, 4>(a, scratch, stream, pdl, err);
+  if (a.M <= 8) return launch_cfg<8, 4>(a, scratch, stream, pdl, err);
+  return launch_cfg<16, 4>(a, scratch, stream, pdl, err);
 }
 
 cudaError_t launch_skinny_chain(const SkinnyArgs* ops, int n, const Scratch& scratch, cudaStream_t stream,
@@ -1167,6 +1249,11 @@ cudaError_t launch_skinny_chain(const SkinnyArgs* ops, int n, const Scratch& scr
     return cudaErrorInvalidValue;
   }
   const int64_t M = ops[0].M;
+  for (int i = 0; i < n; ++i)
+    if (ops[i].bits != 4) {
+      *err = "a chained launch takes 4-bit codes";
+      return cudaErrorInvalidValue;
+    }
   for (int i = 1; i < n; ++i)
     if (ops[i].M != M) {
       *err = "every matmul of a chain must have the same number of rows of x";

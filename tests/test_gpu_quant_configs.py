@@ -2,10 +2,14 @@
 8-bit codes and groups of 128 (4/128, 8/64, 8/128).  Quantize and dequantize
 are bit-exact with the oracle; the matmul is within the output tolerance of
 the oracle, and its fp32 output within 1e-4 of the product it forms: the
-oracle's fp32-formed weights on the decode kernel (4-bit groups of 128 up to
-16 rows), the float64 product of the bit-exact dequantized weights on the
-tensor-core kernel (8-bit codes, and more rows).
-Entry points that only take 4-bit codes say so."""
+oracle's fp32-formed weights on the decode kernel (up to 16 rows), the
+float64 product of the bit-exact dequantized weights on the tensor-core
+kernel (more rows).  The decode kernel's 8-bit codes are also checked at the
+model's shapes and at ragged edges (K not a multiple of its 512-wide chunk,
+N not a multiple of its 128-row tile).  Entry points that only take 4-bit
+codes say so."""
+import functools
+
 import numpy as np
 import pytest
 import torch
@@ -56,7 +60,7 @@ def test_matmul_vs_oracle(cuda_dev, bits, gs, M):
                                    out_dtype=torch.float32)
     torch.cuda.synchronize()
     assert rel_err(y.cpu().numpy(), y_ref) <= TOL
-    if bits == 4 and M <= 16:
+    if M <= 16:
         # the decode kernel forms each weight in fp32 as the oracle does
         assert rel_err(y32.cpu().numpy(), y_ref) <= 1e-4
     else:
@@ -93,14 +97,47 @@ def test_other_configs_in_chains_argmax_and_static_scratch(cuda_dev):
     torch.cuda.synchronize()
     assert torch.equal(y_chain, y)
     assert idx.tolist() == logits.float().cpu().numpy().argmax(axis=1).tolist()
+    # up to 16 rows the greedy token needs no logits buffer (the decode
+    # kernel's epilogue); more rows do
+    idx2 = qw_b200.quantized_matmul_argmax(x, w_d, s_d, b_d, group_size=64, bits=8)
+    assert idx2.tolist() == idx.tolist()
+    x40 = dev(synth.activations(40, K, seed=9))
     with pytest.raises(_lib.QwError) as e:
-        qw_b200.quantized_matmul_argmax(x, w_d, s_d, b_d, group_size=64, bits=8)
+        qw_b200.quantized_matmul_argmax(x40, w_d, s_d, b_d, group_size=64, bits=8)
     assert e.value.code == _lib.QW_EINVAL
     L = _lib.load()
     from qw_b200.ops import _arr, _mode, _stream
     rc = L.qw_quantized_matmul_static_scratch(_arr(x), _arr(w_d), _arr(s_d), _arr(b_d), 1, 64, 8, _mode("affine"),
                                               _arr(y), _stream(x))
     assert rc == _lib.QW_EUNSUPPORTED
+
+
+@functools.lru_cache(maxsize=4)
+def _weights8(N, K, gs):
+    return oracle.quantize(synth.weight_fp16(N, K, seed=N + K), group_size=gs, bits=8)
+
+
+@pytest.mark.parametrize("gs", [64, 128])
+@pytest.mark.parametrize("N,K", [(1000, 2048), (5120, 17408), (17408, 5120), (300, 576), (130, 64)])
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16])
+def test_decode_kernel_8bit_shapes(cuda_dev, gs, N, K, M):
+    """8-bit codes on the decode kernel: the projections of the model's MLP
+    (split over clusters or stream-K, scales through TMA or staged), a row
+    tile cut by N, and K of one group or with a partial last chunk."""
+    if K % gs:
+        pytest.skip("K is not a multiple of the group")
+    wq, s, b = _weights8(N, K, gs)
+    x = synth.activations(M, K, seed=K + M)
+    y_ref, y32_ref = oracle.quantized_matmul(x, wq, s, b, group_size=gs, bits=8, want_f32=True)
+    w_d, s_d, b_d = dev_u32(wq), dev(s), dev(b)
+    y = qw_b200.quantized_matmul(dev(x), w_d, s_d, b_d, group_size=gs, bits=8)
+    y32 = qw_b200.quantized_matmul(dev(x), w_d, s_d, b_d, group_size=gs, bits=8, out_dtype=torch.float32)
+    idx = qw_b200.quantized_matmul_argmax(dev(x), w_d, s_d, b_d, group_size=gs, bits=8)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), y32_ref) <= TOL
+    assert rel_err(y32.cpu().numpy(), y32_ref) <= 1e-4
+    yh = y.cpu().numpy()
+    assert idx.tolist() == yh.astype(np.float32).argmax(axis=1).tolist()
 
 
 @pytest.fixture(autouse=True)

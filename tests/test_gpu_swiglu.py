@@ -49,12 +49,12 @@ def on_dev(p):
 
 def expected_mm(x, p, gs=64, bits=4):
     """The oracle's fp16 output of the kernel that runs this call: the decode
-    kernel (at most 16 rows, 4-bit groups of 64) forms each weight in fp32;
-    the tensor-core kernel multiplies the fp16 weights of dequantize
-    (rounding twice) with fp32 sums."""
+    kernel (at most 16 rows) forms each weight in fp32; the tensor-core
+    kernel multiplies the fp16 weights of dequantize (rounding twice) with
+    fp32 sums."""
     x = np.asarray(x, np.float16)
-    if x.shape[0] <= 16 and (gs, bits) == (64, 4):
-        return oracle.quantized_matmul(x, *p)
+    if x.shape[0] <= 16:
+        return oracle.quantized_matmul(x, *p, group_size=gs, bits=bits)
     w = oracle.dequantize(*p, group_size=gs, bits=bits).astype(np.float64)
     return (x.astype(np.float64) @ w.T).astype(np.float16)
 
@@ -124,10 +124,10 @@ def test_fused_checkpoint_halves(cuda_dev):
 
 
 @pytest.mark.parametrize("bits,gs", [(4, 128), (8, 64), (8, 128)])
-@pytest.mark.parametrize("M", [1, 40])
+@pytest.mark.parametrize("M", [1, 9, 40])
 def test_swiglu_other_configs(cuda_dev, bits, gs, M):
-    """Configurations without the skinny kernel take the tensor-core kernel's
-    SwiGLU epilogue at every M."""
+    """The other quantization configurations through both kernels' SwiGLU
+    epilogues (decode kernel up to 16 rows, tensor-core kernel above)."""
     I, K = 200, 1536
     gate, up = proj(I, K, seed=11, gs=gs, bits=bits), proj(I, K, seed=12, gs=gs, bits=bits)
     x = synth.activations(M, K, seed=13)
