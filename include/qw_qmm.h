@@ -85,10 +85,10 @@ typedef struct qw_qmm_op {
  * (transpose = true) would, where op i may read what earlier ops wrote (its x
  * may be an earlier y).  Every op is validated as qw_quantized_matmul
  * validates it, and all x must have the same number of rows M.  With
- * M <= 16 up to 24 matmuls share one cooperative launch of one CTA per SM:
- * a matmul's weights start streaming while the previous matmul finishes,
- * and a grid-wide count of finished CTAs orders the dependent reads.  With
- * larger M it issues one launch per op.
+ * M <= 16 and 4-bit codes up to 24 matmuls share one cooperative launch of
+ * one CTA per SM: a matmul's weights start streaming while the previous
+ * matmul finishes, and a grid-wide count of finished CTAs orders the
+ * dependent reads.  With larger M or 8-bit codes it issues one launch per op.
  * No counterpart in the reference: it fuses a sequence of the reference's
  * quantized_matmul calls (lib.rs:1134-1143) for decode loops whose
  * consecutive linears have nothing in between. */

@@ -1,5 +1,5 @@
-// qw_skinny.cu -- affine 4-bit quantized matmul (groups of 64 or 128) for
-// M <= 16 rows of x (decode M=1, MTP verify M=4, DFlash2 block M=16).
+// qw_skinny.cu -- affine 4- or 8-bit quantized matmul (groups of 64 or 128)
+// for M <= 16 rows of x (decode M=1, MTP verify M=4, DFlash2 block M=16).
 // HBM-bound: the packed weights are streamed once.
 //
 // Work decomposition ("stream-K"): the weight matrix is cut into row tiles of
@@ -12,7 +12,8 @@
 // order (deterministic) and writes y.
 //
 // CTA roles (warp-specialised), per pipeline stage of 128 rows x 512 k:
-//   warp 0        TMA producer of packed W (two 128-byte SW128 boxes, 32 KB),
+//   warp 0        TMA producer of packed W (two 128-byte SW128 boxes, 32 KB;
+//                 four, 64 KB, with 8-bit codes),
 //                 scales and biases (one box each); it does not wait for the
 //                 previous kernel, so under PDL this launch's weight stream
 //                 starts while the previous kernel finishes.
@@ -44,6 +45,11 @@
 //     y += s * (d - Z) + b * X,   Z = 1024 X_even + 64 X_odd,
 // which is sum_k x_k (s q_k + b): the weight formed in fp32 and accumulated in
 // fp32 (the reference semantics).
+//
+// 8-bit codes: a stage's chunk is four SW128 boxes (512 bytes per row), a
+// word holds codes q0..q3, and prmt(w, 0x64646464) pairs each byte with 0x64
+// into the exact fp16 1024 + q, so the MMAs see x unscaled (the helpers only
+// reorder it) and Z = 1024 X.
 #include <cuda_fp16.h>
 
 #include <mutex>
