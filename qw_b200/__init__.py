@@ -1,6 +1,6 @@
 """qw_b200 -- B200-native affine group-quantized matmul for cr0sh/qw's Qwen
-27B linear layers: decode qmv and verify-batch qmm (4-bit), tcgen05 prefill
-qmm (4- and 8-bit), the fused SwiGLU MLP input, the greedy-token and top-k
+27B linear layers: decode qmv, verify-batch qmm and tcgen05 prefill qmm (4-
+and 8-bit codes), the fused SwiGLU MLP input, the greedy-token and top-k
 candidate steps after the LM head, and the tensor-parallel linear stack with
 its NVLink peer allreduce.
 
