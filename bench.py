@@ -580,7 +580,21 @@ def run_ours(args):
             ar.close()
         torch.distributed.destroy_process_group()
     if rank == 0:
+        benchmark_result_line("qw_b200_decode_stack_m1", 1, args.steps, ms * 1e-3 * args.steps)
         print(json.dumps(result), flush=True)
+
+
+def benchmark_result_line(label, tokens_per_repetition, repetitions, elapsed_s):
+    """The reference benchmark's result line (crates/runtime/benches/
+    single_user_throughput.rs:126-131), on stderr so that stdout keeps the
+    single JSON line.  The steps are timed as one bracketed region, so there
+    is no per-step spread: stddev_seconds is nan.  context_tokens is 0: the
+    linear stack has no attention context."""
+    processed = tokens_per_repetition * repetitions
+    print(f"BENCHMARK_RESULT label={label} context_tokens=0 tokens_per_repetition={tokens_per_repetition} "
+          f"processed_tokens={processed} repetitions={repetitions} elapsed_seconds={elapsed_s:.6f} "
+          f"mean_seconds={elapsed_s / repetitions:.6f} stddev_seconds=nan "
+          f"tokens_per_second={processed / elapsed_s:.3f}", file=sys.stderr, flush=True)
 
 
 def run_reference(args):
