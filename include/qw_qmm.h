@@ -199,7 +199,11 @@ int qw_quantized_matmul_static_scratch(const qw_array* x, const qw_array* w, con
  * buffer for up to max_elems floats per call and returns its IPC handle,
  * QW_IPC_HANDLE_BYTES bytes); exchange the handles (any host transport);
  * qw_allreduce_connect with all ranks' handles in rank order; then a
- * barrier across ranks before the first qw_allreduce_sum. */
+ * barrier across ranks before the first qw_allreduce_sum.  Peers store into
+ * every rank's buffer, so qw_allreduce_destroy may run only once every
+ * rank's calls have ended: each rank synchronizes its device, then a barrier
+ * across ranks, then each rank destroys (destroy itself waits for this
+ * device's work only).  Calls of a communicator run on its device. */
 #define QW_IPC_HANDLE_BYTES 64
 typedef struct qw_allreduce qw_allreduce;
 int qw_allreduce_init(int world, int rank, int64_t max_elems, qw_allreduce** comm, unsigned char* handle);

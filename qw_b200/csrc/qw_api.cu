@@ -878,6 +878,9 @@ int qw_allreduce_sum(qw_allreduce* c, const qw_array* partial, qw_array* y, void
   int rc;
   if (!c) return fail(QW_EINVAL, "comm is null");
   if ((rc = check_array(partial, "partial")) || (rc = check_array(y, "y"))) return rc;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != c->device)
+    return fail(QW_EINVAL, "the current device is not the communicator's (device " + std::to_string(c->device) + ")");
   for (int r = 0; r < c->comm.P; ++r)
     if (!c->comm.peer_bufs[r]) return fail(QW_EINVAL, "rank " + std::to_string(r) + " is not connected");
   if (partial->dtype != QW_F32) return fail(QW_EINVAL, "partial must be float32");
@@ -897,10 +900,17 @@ int qw_allreduce_sum(qw_allreduce* c, const qw_array* partial, qw_array* y, void
 int qw_allreduce_destroy(qw_allreduce* c) {
   set_error("");
   if (!c) return QW_OK;
+  // this rank's calls end before its buffers go (the peers' calls are the
+  // caller's to wait for: a barrier across ranks)
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (c->device >= 0 && cudaSetDevice(c->device) == cudaSuccess) cudaDeviceSynchronize();
   for (int r = 0; r < kArMaxRanks; ++r)
     if (c->opened[r]) cudaIpcCloseMemHandle(c->comm.peer_bufs[r]);
   if (c->own) cudaFree(c->own);
   if (c->comm.counters) cudaFree(c->comm.counters);
+  cudaGetLastError();
+  cudaSetDevice(prev);
   delete c;
   return QW_OK;
 }

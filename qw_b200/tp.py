@@ -216,6 +216,8 @@ class PeerAllreduce:
         _lib.check(L.qw_allreduce_connect(self._comm, blob))
         dist.barrier(group=group)
         self.world, self.rank, self.max_elems = world, rank, int(max_elems)
+        self._group = group
+        self._device = torch.cuda.current_device()
 
     def __call__(self, partial, out):
         """out (fp16 or fp32) = sum over ranks of partial (fp32, same numel)."""
@@ -223,7 +225,19 @@ class PeerAllreduce:
         self._lib.check(self._lib.load().qw_allreduce_sum(self._comm, _arr(partial), _arr(out), _stream(partial)))
         return out
 
-    def close(self):
+    def close(self, barrier: bool = True):
+        """Free this rank's buffer and its mappings of the peers' buffers.
+        Peers store into this rank's buffer during their calls (a call that
+        gave up on a missing peer may store late), so no rank may free its
+        buffer before every rank's calls have ended.  With barrier=True this
+        waits for the device's work and then for every rank of the group, so
+        every rank must call close; pass False only when the caller has done
+        both itself."""
         if self._comm:
+            if barrier:
+                import torch
+                import torch.distributed as dist
+                torch.cuda.synchronize(self._device)
+                dist.barrier(group=self._group)
             self._lib.load().qw_allreduce_destroy(self._comm)
             self._comm = None
