@@ -172,8 +172,8 @@ int qw_swiglu_mlp(const qw_array* x, const qw_array* w_gate, const qw_array* sca
  * process exits.  The first call on a device resolves that array's address
  * (make it before any stream capture).  All calls on a device share the
  * array, so calls that overlap on the GPU race; calls on one stream are safe.
- * 4-bit codes in groups of 64 or 128 only.  More than 16 rows, 8-bit codes, or
- * a shape whose scratch exceeds the array, returns QW_EUNSUPPORTED.  A kernel
+ * 4- or 8-bit codes in groups of 64 or 128.  More than 16 rows, or a shape
+ * whose scratch exceeds the array, returns QW_EUNSUPPORTED.  A kernel
  * that gives up on a bounded wait leaves y
  * incomplete without an error code here.
  * No counterpart in the reference: MLX allocates through its own allocator. */

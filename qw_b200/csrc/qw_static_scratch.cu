@@ -35,7 +35,7 @@
 // host threads -- race on the array and may return wrong results.  Calls on
 // one stream are ordered and safe.
 //
-// Limits: 4-bit weights in groups of 64 or 128 (the skinny kernel), 16 rows of x per
+// Limits: 4- or 8-bit weights in groups of 64 or 128 (the skinny kernel), 16 rows of x per
 // call (its tile), and the scratch that the shape needs on this device at
 // most kStaticScratchBytes minus the status word (a 256-byte header, the
 // split-tile counters, 4 bytes per 128 output rows up to 256 KiB, plus two
@@ -108,9 +108,9 @@ extern "C" int qw_quantized_matmul_static_scratch(const qw_array* x, const qw_ar
   int rc = check_qmm_call(x, w, scales, biases, transpose, group_size, bits, mode, y, &sa);
   if (rc != QW_OK) return rc;
   if (sa.M == 0 || sa.N == 0) return QW_OK;
-  if (bits != 4 || (group_size != 64 && group_size != 128))
+  if ((bits != 4 && bits != 8) || (group_size != 64 && group_size != 128))
     return static_fail(QW_EUNSUPPORTED,
-                       "qw_quantized_matmul_static_scratch takes 4-bit weights in groups of 64 or 128");
+                       "qw_quantized_matmul_static_scratch takes 4- or 8-bit weights in groups of 64 or 128");
   if (sa.M > kStaticMaxRows)
     return static_fail(QW_EUNSUPPORTED, "qw_quantized_matmul_static_scratch takes at most " +
                                             std::to_string(kStaticMaxRows) + " rows of x per call, got " +

@@ -107,9 +107,12 @@ def test_other_configs_in_chains_argmax_and_static_scratch(cuda_dev):
     assert e.value.code == _lib.QW_EINVAL
     L = _lib.load()
     from qw_b200.ops import _arr, _mode, _stream
+    y_static = torch.empty_like(y)
     rc = L.qw_quantized_matmul_static_scratch(_arr(x), _arr(w_d), _arr(s_d), _arr(b_d), 1, 64, 8, _mode("affine"),
-                                              _arr(y), _stream(x))
-    assert rc == _lib.QW_EUNSUPPORTED
+                                              _arr(y_static), _stream(x))
+    torch.cuda.synchronize()
+    assert rc == _lib.QW_OK
+    assert torch.equal(y_static, y)
 
 
 @functools.lru_cache(maxsize=4)
