@@ -572,7 +572,7 @@ def run_ours(args):
         result["cpu_baseline"] = {
             "value": round(gbs * 1e9 / synth.stack_bytes(1, args.layers), 4), "unit": "tok/s", "cores": threads,
             "kind": "port", "GBps": round(gbs, 3),
-            "sample": f"the whole {args.layers}-layer stack + lm_head at M=1, twice, through the C oracle with OpenMP "
+            "sample": f"the whole {args.layers}-layer stack + lm_head at M=1, twice, through the C oracle (AVX2, OpenMP) "
                       f"({secs:.1f} s of CPU work) on the GPU's quantized weights copied to the host"}
     if dist_on:
         torch.distributed.barrier()
@@ -605,42 +605,42 @@ def run_reference(args):
         return
     import oracle
     threads = os.cpu_count() or 1
-    # Per step: a slab of rows of one decoder layer, sized so warmup + steps
-    # finish in about two minutes on this host.
+    # Per step: one decoder layer (its four linears at full size, unless that
+    # would not let warmup + steps finish in about two minutes on this host,
+    # in which case the same leading fraction of every linear's rows).
     budget_s = 120.0 / max(1, args.steps + args.warmup)
     lins = synth.layer_linears()
-    mats = {}
-    for lin in lins:
-        w = synth.weight_fp16(512, lin.K, seed=lin.tid)
-        mats[lin.name] = oracle.quantize(w)
+    mats = {lin.name: oracle.quantize(synth.weight_fp16(lin.N, lin.K, seed=lin.tid)) for lin in lins}
     x = {lin.K: synth.activations(1, lin.K, seed=2) for lin in lins}
-    # rate probe
+    # rate probe: the whole layer once
     t0 = time.perf_counter()
     for lin in lins:
         wq, s, b = mats[lin.name]
         oracle.quantized_matmul(x[lin.K], wq, s, b, nthreads=threads)
     probe = time.perf_counter() - t0
-    rows = int(max(16, min(512, 512 * budget_s / max(probe, 1e-6))))
-    rows -= rows % 16
-    rows = max(16, rows)
+    frac = min(1.0, budget_s / max(probe, 1e-6))
+    rows = {lin.name: max(32, int(lin.N * frac) // 32 * 32) for lin in lins}
     for _ in range(args.warmup):
         for lin in lins:
             wq, s, b = mats[lin.name]
-            oracle.quantized_matmul(x[lin.K], wq[:rows], s[:rows], b[:rows], nthreads=threads)
+            r = rows[lin.name]
+            oracle.quantized_matmul(x[lin.K], wq[:r], s[:r], b[:r], nthreads=threads)
     t0 = time.perf_counter()
     nbytes = 0
     for _ in range(args.steps):
         for lin in lins:
             wq, s, b = mats[lin.name]
-            y = oracle.quantized_matmul(x[lin.K], wq[:rows], s[:rows], b[:rows], nthreads=threads)
+            r = rows[lin.name]
+            y = oracle.quantized_matmul(x[lin.K], wq[:r], s[:r], b[:r], nthreads=threads)
             if lin.name == "gate_up":  # the MLP activation on the slab's gate and up halves
-                oracle.swiglu(y[:, : rows // 2], y[:, rows // 2:])
-            nbytes += synth.algorithmic_bytes(1, rows, lin.K)
+                oracle.swiglu(y[:, : r // 2], y[:, r // 2:])
+            nbytes += synth.algorithmic_bytes(1, r, lin.K)
     dt = time.perf_counter() - t0
     gbs = nbytes / dt / 1e9
     tok_s = gbs * 1e9 / synth.stack_bytes(1, args.layers)
-    sample = (f"{rows} rows of each of qkv/o/gate_up/down per step through the C oracle (OpenMP, {threads} threads), "
-              f"SwiGLU on the gate_up slab; "
+    shown = ", ".join(f"{lin.name} {rows[lin.name]}/{lin.N}" for lin in lins)
+    sample = (f"one decoder layer per step (rows {shown}) through the C oracle (AVX2, OpenMP, {threads} threads), "
+              f"SwiGLU on the gate_up rows; "
               f"tok/s = GB/s / {synth.stack_bytes(1, args.layers)} bytes per token")
     out = {
         "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": "tok/s", "n_gpus": world,

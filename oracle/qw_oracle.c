@@ -3,12 +3,16 @@
  * cr0sh/qw calls it.  TEST INFRASTRUCTURE ONLY; see qw_oracle.h for the
  * reference citations, the conventions and the parity status.
  *
- * Build: oracle/Makefile (-O3 -ffp-contract=off -fopenmp).  Contraction is
- * disabled so that every `a*b + c` below is two IEEE fp32 operations, which
- * is what makes the results reproducible bit for bit on any x86-64 host.
+ * Build: oracle/Makefile (-O3 -ffp-contract=off -fopenmp, x86-64-v3).
+ * Contraction is disabled so that every `a*b + c` below is two IEEE fp32
+ * operations, which is what makes the results reproducible bit for bit on
+ * any x86-64 host.  The matmul's full 16-row blocks run in AVX2 intrinsics
+ * with one row per lane, so each row's operations and their order are those
+ * of the scalar loops that handle the last, partial block.
  */
 #include "qw_oracle.h"
 
+#include <immintrin.h>
 #include <math.h>
 #include <pthread.h>
 #include <stdlib.h>
@@ -226,6 +230,116 @@ static void init_f16_table(void) { pthread_once(&f16_table_once, fill_f16_table)
 
 #define QWO_RB 16 /* rows dequantized together; lanes of the inner vector loop */
 
+/* Full blocks of QWO_RB rows in AVX2 (the build's x86-64-v3 baseline).  The
+ * arithmetic is the scalar loops' exactly, only spread over lanes: lane j of
+ * a vector is row nb + j, so every row still forms w = s*q, then + b, and
+ * sums x*w in K order, each step one rounded fp32 operation.
+ *
+ * wblk[k][j] = dequantized weight of row nb + j at column k: the words of the
+ * 16 rows at word index wi are gathered, then each code position p is
+ * shifted out, converted and scaled for all rows at once. */
+static void dequant_block_avx2(const uint32_t* wq, const uint16_t* scales, const uint16_t* biases, int64_t nb,
+                               int64_t kw, int64_t G, int group_size, int bits, float* wblk) {
+  const int pf = 32 / bits;
+  const __m256i mask = _mm256_set1_epi32((int)((1u << bits) - 1u));
+  const __m256i rows = _mm256_setr_epi32(0, 1, 2, 3, 4, 5, 6, 7);
+  const __m256i vidx = _mm256_mullo_epi32(rows, _mm256_set1_epi32((int)kw)); /* word offsets of rows 0..7 */
+  const uint32_t* base = wq + nb * kw;
+  const int64_t wpg = group_size / pf; /* words per group */
+  for (int64_t g = 0; g < G; ++g) {
+    float sv[QWO_RB], bv[QWO_RB];
+    for (int j = 0; j < QWO_RB; ++j) {
+      sv[j] = f16_table[scales[(nb + j) * G + g]];
+      bv[j] = f16_table[biases[(nb + j) * G + g]];
+    }
+    const __m256 s0 = _mm256_loadu_ps(sv), s1 = _mm256_loadu_ps(sv + 8);
+    const __m256 b0 = _mm256_loadu_ps(bv), b1 = _mm256_loadu_ps(bv + 8);
+    for (int64_t wi = g * wpg; wi < (g + 1) * wpg; ++wi) {
+      const __m256i w0 = _mm256_i32gather_epi32((const int*)(base + wi), vidx, 4);
+      const __m256i w1 = _mm256_i32gather_epi32((const int*)(base + 8 * kw + wi), vidx, 4);
+      float* dst = wblk + wi * pf * QWO_RB;
+      for (int p = 0; p < pf; ++p, dst += QWO_RB) {
+        const __m128i sh = _mm_cvtsi32_si128(bits * p);
+        /* codes are at most 255: the signed conversion is exact */
+        const __m256 q0 = _mm256_cvtepi32_ps(_mm256_and_si256(_mm256_srl_epi32(w0, sh), mask));
+        const __m256 q1 = _mm256_cvtepi32_ps(_mm256_and_si256(_mm256_srl_epi32(w1, sh), mask));
+        _mm256_storeu_ps(dst, _mm256_add_ps(_mm256_mul_ps(s0, q0), b0));
+        _mm256_storeu_ps(dst + 8, _mm256_add_ps(_mm256_mul_ps(s1, q1), b1));
+      }
+    }
+  }
+}
+
+/* Up to 4 rows of x: each weight is formed and used at once, with no
+ * dequantized block in memory.  acc[i][j] = sum over k (ascending) of
+ * x[m0 + i][k] * w(nb + j, k), the same steps as dequant_block_avx2 followed
+ * by block_rows_avx2. */
+static void fused_rows_avx2(const float* xf, int64_t K, const uint32_t* wq, const uint16_t* scales,
+                            const uint16_t* biases, int64_t nb, int64_t kw, int64_t G, int group_size, int bits,
+                            int64_t m0, int nm, float acc[4][QWO_RB]) {
+  const int pf = 32 / bits;
+  const __m256i mask = _mm256_set1_epi32((int)((1u << bits) - 1u));
+  const __m256i vidx = _mm256_mullo_epi32(_mm256_setr_epi32(0, 1, 2, 3, 4, 5, 6, 7), _mm256_set1_epi32((int)kw));
+  const uint32_t* base = wq + nb * kw;
+  const int64_t wpg = group_size / pf;
+  const float* xr[4];
+  for (int i = 0; i < 4; ++i) xr[i] = xf + (m0 + (i < nm ? i : 0)) * K;
+  __m256 a[4][2];
+  for (int i = 0; i < 4; ++i) a[i][0] = a[i][1] = _mm256_setzero_ps();
+  for (int64_t g = 0; g < G; ++g) {
+    float sv[QWO_RB], bv[QWO_RB];
+    for (int j = 0; j < QWO_RB; ++j) {
+      sv[j] = f16_table[scales[(nb + j) * G + g]];
+      bv[j] = f16_table[biases[(nb + j) * G + g]];
+    }
+    const __m256 s0 = _mm256_loadu_ps(sv), s1 = _mm256_loadu_ps(sv + 8);
+    const __m256 b0 = _mm256_loadu_ps(bv), b1 = _mm256_loadu_ps(bv + 8);
+    for (int64_t wi = g * wpg; wi < (g + 1) * wpg; ++wi) {
+      const __m256i w0 = _mm256_i32gather_epi32((const int*)(base + wi), vidx, 4);
+      const __m256i w1 = _mm256_i32gather_epi32((const int*)(base + 8 * kw + wi), vidx, 4);
+      for (int p = 0; p < pf; ++p) {
+        const int64_t k = wi * pf + p;
+        const __m128i sh = _mm_cvtsi32_si128(bits * p);
+        const __m256 q0 = _mm256_cvtepi32_ps(_mm256_and_si256(_mm256_srl_epi32(w0, sh), mask));
+        const __m256 q1 = _mm256_cvtepi32_ps(_mm256_and_si256(_mm256_srl_epi32(w1, sh), mask));
+        const __m256 d0 = _mm256_add_ps(_mm256_mul_ps(s0, q0), b0);
+        const __m256 d1 = _mm256_add_ps(_mm256_mul_ps(s1, q1), b1);
+        for (int i = 0; i < nm; ++i) {
+          const __m256 xv = _mm256_broadcast_ss(xr[i] + k);
+          a[i][0] = _mm256_add_ps(a[i][0], _mm256_mul_ps(xv, d0));
+          a[i][1] = _mm256_add_ps(a[i][1], _mm256_mul_ps(xv, d1));
+        }
+      }
+    }
+  }
+  for (int i = 0; i < nm; ++i) {
+    _mm256_storeu_ps(acc[i], a[i][0]);
+    _mm256_storeu_ps(acc[i] + 8, a[i][1]);
+  }
+}
+
+/* acc[m][j] = sum over k (ascending) of x[m][k] * wblk[k][j] for m in
+ * [m0, m0 + nm), nm <= 4: four rows of x share each load of wblk. */
+static void block_rows_avx2(const float* xf, int64_t K, const float* wblk, int64_t m0, int nm,
+                            float acc[4][QWO_RB]) {
+  __m256 a[4][2];
+  for (int i = 0; i < 4; ++i) a[i][0] = a[i][1] = _mm256_setzero_ps();
+  const float* xr[4];
+  for (int i = 0; i < 4; ++i) xr[i] = xf + (m0 + (i < nm ? i : 0)) * K;
+  for (int64_t k = 0; k < K; ++k) {
+    const __m256 w0 = _mm256_loadu_ps(wblk + k * QWO_RB), w1 = _mm256_loadu_ps(wblk + k * QWO_RB + 8);
+    for (int i = 0; i < 4; ++i) {
+      const __m256 xv = _mm256_broadcast_ss(xr[i] + k);
+      a[i][0] = _mm256_add_ps(a[i][0], _mm256_mul_ps(xv, w0));
+      a[i][1] = _mm256_add_ps(a[i][1], _mm256_mul_ps(xv, w1));
+    }
+  }
+  for (int i = 0; i < nm; ++i) {
+    _mm256_storeu_ps(acc[i], a[i][0]);
+    _mm256_storeu_ps(acc[i] + 8, a[i][1]);
+  }
+}
+
 int qwo_quantized_matmul(const uint16_t* x, const uint32_t* wq, const uint16_t* scales,
                          const uint16_t* biases, int64_t M, int64_t N, int64_t K,
                          int group_size, int bits, uint16_t* y, float* y32, int nthreads) {
@@ -254,6 +368,22 @@ int qwo_quantized_matmul(const uint16_t* x, const uint32_t* wq, const uint16_t* 
     for (int64_t nb = 0; nb < N; nb += QWO_RB) {
       if (!wblk) continue;
       const int rb = (int)((N - nb) < QWO_RB ? (N - nb) : QWO_RB);
+      if (rb == QWO_RB) {
+        if (M > 4) dequant_block_avx2(wq, scales, biases, nb, kw, G, group_size, bits, wblk);
+        for (int64_t m0 = 0; m0 < M; m0 += 4) {
+          const int nm = (int)((M - m0) < 4 ? (M - m0) : 4);
+          float acc[4][QWO_RB];
+          if (M > 4) block_rows_avx2(xf, K, wblk, m0, nm, acc);
+          else fused_rows_avx2(xf, K, wq, scales, biases, nb, kw, G, group_size, bits, m0, nm, acc);
+          for (int i = 0; i < nm; ++i)
+            for (int j = 0; j < QWO_RB; ++j) {
+              y[(m0 + i) * N + nb + j] = qwo_f32_to_f16(acc[i][j]);
+              if (y32) y32[(m0 + i) * N + nb + j] = acc[i][j];
+            }
+        }
+        continue;
+      }
+      /* the last, partial block: scalar */
       for (int j = 0; j < QWO_RB; ++j) {
         if (j >= rb) {
           for (int64_t k = 0; k < K; ++k) wblk[k * QWO_RB + j] = 0.0f;
