@@ -180,6 +180,39 @@ def test_c_and_numpy_restatements_agree(N, K):
     assert rel_err(y, y64) < 1e-3
 
 
+def _sequential_f32(x, wq, s, b, gs, bits):
+    """y32 by the oracle's stated arithmetic, one rounded float32 operation
+    at a time: w = s*q, then w + b; then acc = acc + x*w over k ascending."""
+    N = wq.shape[0]
+    per = 32 // bits
+    q = ((wq[:, :, None] >> (bits * np.arange(per, dtype=np.uint32))) & ((1 << bits) - 1)).reshape(N, -1)
+    K = q.shape[1]
+    s32 = np.repeat(s.astype(np.float32), gs, axis=1)
+    b32 = np.repeat(b.astype(np.float32), gs, axis=1)
+    w32 = (s32 * q.astype(np.float32)) + b32
+    x32 = x.astype(np.float32)
+    acc = np.zeros((x.shape[0], N), np.float32)
+    for k in range(K):
+        acc = acc + x32[:, k:k + 1] * w32[None, :, k]
+    return acc
+
+
+@pytest.mark.parametrize("bits,gs", [(4, 64), (4, 128), (8, 64), (8, 128)])
+@pytest.mark.parametrize("M", [1, 3, 4, 5, 9])
+def test_matmul_is_the_stated_float32_sequence(bits, gs, M):
+    """Every path of the oracle's matmul -- the vectorised 16-row blocks
+    (weights formed on the fly up to 4 rows of x, or from a dequantized block
+    above), the scalar last block -- gives, bit for bit, the float32 sequence
+    it is defined as."""
+    N, K = 37, 512  # two full 16-row blocks and a partial one
+    wq, s, b = oracle.quantize(synth.weight_fp16(N, K, seed=bits + gs + M), group_size=gs, bits=bits)
+    x = synth.activations(M, K, seed=M)
+    y, y32 = oracle.quantized_matmul(x, wq, s, b, group_size=gs, bits=bits, want_f32=True)
+    ref = _sequential_f32(x, wq, s, b, gs, bits)
+    np.testing.assert_array_equal(y32.view(np.uint32), ref.view(np.uint32))
+    np.testing.assert_array_equal(y.view(np.uint16), ref.astype(np.float16).view(np.uint16))
+
+
 def test_quantizer_reconstruction_error_is_bounded():
     w = synth.weight_fp16(64, 512, seed=5)
     wq, s, b = oracle.quantize(w)
