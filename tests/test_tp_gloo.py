@@ -1,7 +1,8 @@
 """Tensor-parallel stack logic on CPU: two gloo ranks, each running its shard
 of a (down-scaled) linear stack through the oracle, against the unsharded
 stack.  Also a host-side failure case: a rank that dies before the collective
-must not leave its peer hanging.  No GPU."""
+must not leave its peer hanging; and the peer allreduce's host protocol
+(handle exchange, collective teardown) against a fake library.  No GPU."""
 import os
 import socket
 import time
@@ -156,3 +157,87 @@ def test_failed_rank_does_not_hang_its_peer():
     assert results.get(1, ("", ""))[0] == "error"
     assert results.get(0, ("", ""))[0] == "error", results.get(0)
     assert time.time() - t0 < 100
+
+
+# ------------------------------------------------- peer allreduce host protocol
+class _FakeAllreduceLib:
+    """Stands in for libqwqmm's qw_allreduce_* entry points (no GPU): each
+    rank's IPC handle is 64 bytes of (rank + 1), and calls are logged."""
+
+    def __init__(self, log):
+        self.log = log
+
+    def qw_allreduce_init(self, world, rank, max_elems, comm_ref, handle):
+        import ctypes
+        comm_ref._obj.value = 1000 + rank
+        ctypes.memmove(handle, bytes([rank + 1]) * 64, 64)
+        self.log.append(("init", world, rank, max_elems))
+        return 0
+
+    def qw_allreduce_connect(self, comm, blob):
+        self.log.append(("connect", bytes(blob)))
+        return 0
+
+    def qw_allreduce_destroy(self, comm):
+        self.log.append(("destroy", time.time()))
+        return 0
+
+
+def _protocol_rank(rank, world, port, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    from qw_b200 import _lib
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        log = []
+        fake = _FakeAllreduceLib(log)
+        _lib.load = lambda: fake                          # the fake library
+        torch.cuda.current_device = lambda: 0             # no device here
+        torch.cuda.synchronize = lambda *a, **k: log.append(("sync",))
+        ar = tp.PeerAllreduce(4096)
+        if rank == 0:
+            time.sleep(1.5)  # the other ranks reach close first
+        entered = time.time()
+        ar.close()
+        ar.close()  # a second close does nothing
+        out_q.put((rank, "ok", (log, entered)))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        out_q.put((rank, "error", repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_allreduce_host_protocol():
+    """PeerAllreduce's host side over gloo with a fake library: every rank
+    connects with all ranks' handles in rank order, and no rank frees its
+    buffer (destroy) before every rank has reached close and synchronized."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_protocol_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    deadline = time.time() + 120
+    while len(got) < world and time.time() < deadline:
+        try:
+            r, status, payload = q.get(timeout=5)
+        except Exception:
+            continue
+        assert status == "ok", payload
+        got[r] = payload
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert len(got) == world
+    handles = b"".join(bytes([r + 1]) * 64 for r in range(world))
+    last_entry = max(entered for _, entered in got.values())
+    for r, (log, _) in got.items():
+        kinds = [e[0] for e in log]
+        assert kinds == ["init", "connect", "sync", "destroy"], kinds
+        assert log[0] == ("init", world, r, 4096)
+        assert log[1][1] == handles
+        assert log[3][1] >= last_entry  # freed only after every rank reached close
