@@ -250,6 +250,18 @@ def test_golden_quantizer_inputs_regenerate():
         np.testing.assert_array_equal(synth.activations(M, K, seed=seed), g["x"])
 
 
+def test_full_size_configs_match_their_digests():
+    """BASELINE's single configuration (17408 x 5120 at M = 1 and 16) and an
+    8-bit, group-128 override shape at full size: the oracle's quantized
+    triple and outputs, regenerated from the seeds, hash to the committed
+    digests (tests/golden/baseline_digests.json)."""
+    import json
+    from tests.golden.gen_golden import DIGEST_FILE, digest_cases
+    with open(DIGEST_FILE) as f:
+        committed = json.load(f)
+    assert digest_cases() == committed
+
+
 def test_swiglu_known_answer():
     """The reference's activation test input (ffi_tests.rs:1536-1548: gate
     [1, 2, 3, 4], x = 2 everywhere, positive sum) against silu(g) * x in
