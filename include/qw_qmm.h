@@ -174,8 +174,8 @@ int qw_swiglu_mlp(const qw_array* x, const qw_array* w_gate, const qw_array* sca
  * array, so calls that overlap on the GPU race; calls on one stream are safe.
  * 4- or 8-bit codes in groups of 64 or 128.  More than 16 rows, or a shape
  * whose scratch exceeds the array, returns QW_EUNSUPPORTED.  A kernel
- * that gives up on a bounded wait leaves y
- * incomplete without an error code here.
+ * that gives up on a bounded wait leaves y incomplete and a code in the
+ * array's status word, which qw_device_status reports (it allocates nothing).
  * No counterpart in the reference: MLX allocates through its own allocator. */
 int qw_quantized_matmul_static_scratch(const qw_array* x, const qw_array* w, const qw_array* scales,
                                        const qw_array* biases, int transpose, int group_size, int bits,
@@ -249,9 +249,11 @@ int qw_quantize(const qw_array* w, int group_size, int bits, const char* mode, q
 /* Message of the last failing call on this host thread ("" if none). */
 const char* qw_last_error(void);
 
-/* Reads (and, if clear != 0, resets) the device-side status word that a
- * kernel sets when one of its bounded waits runs out (0 = none).  Synchronises
- * the device. */
+/* Reads (and, if clear != 0, resets) the device-side status words that a
+ * kernel sets when one of its bounded waits runs out (0 = none): the
+ * library's own and the one in qw_quantized_matmul_static_scratch's array;
+ * the first nonzero is returned.  Synchronises the device; allocates
+ * nothing. */
 int qw_device_status(int device, unsigned int* status, int clear);
 
 /* QW_ABI_VERSION of the loaded library. */

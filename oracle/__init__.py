@@ -48,6 +48,8 @@ def lib() -> ctypes.CDLL:
         L.qwo_quantize.argtypes = [p, i64, i64, i32, i32, p, p, p]
         L.qwo_dequantize.argtypes = [p, p, p, i64, i64, i32, i32, i32, p]
         L.qwo_quantized_matmul.argtypes = [p, p, p, p, i64, i64, i64, i32, i32, p, p, i32]
+        L.qwo_dequantize_f32.argtypes = [p, p, p, i64, i64, i32, i32, i32, p]
+        L.qwo_matmul_f16w.argtypes = [p, p, i64, i64, i64, p, p, i32]
         L.qwo_f32_to_f16.argtypes = [ctypes.c_float]
         L.qwo_f32_to_f16.restype = ctypes.c_uint16
         L.qwo_f64_to_f16.argtypes = [ctypes.c_double]
@@ -92,9 +94,71 @@ def dequantize(wq, scales, biases, group_size: int = 64, bits: int = 4, rounding
     return out
 
 
+def dequantize_f32(wq, scales, biases, group_size: int = 64, bits: int = 4, rounding: int = ROUND_TWICE):
+    """dequantize for float32 scales and biases -> float32 [N, K]: ROUND_TWICE
+    forms fp32(fp32(s*q) + b), ROUND_ONCE fmaf(s, q, b).  MLX returns the
+    scales' dtype, so the reference's f32-scale layout test
+    (crates/mlxcel-core/src/ffi_tests.rs:3792-3850) dequantizes to float32."""
+    wq = np.ascontiguousarray(wq, dtype=np.uint32)
+    scales = np.ascontiguousarray(scales, dtype=np.float32)
+    biases = np.ascontiguousarray(biases, dtype=np.float32)
+    N = wq.shape[0]
+    K = wq.shape[1] * 32 // bits
+    out = np.zeros((N, K), dtype=np.float32)
+    _check(lib().qwo_dequantize_f32(_ptr(wq), _ptr(scales), _ptr(biases), N, K, group_size, bits, rounding,
+                                    _ptr(out)), "dequantize_f32")
+    return out
+
+
+def matmul_f16w(x, w16, nthreads: int = 0, want_f32: bool = False):
+    """y = x . w16^T for fp16 weights [N, K]: products and sums in float32,
+    ascending k, one rounding to fp16 at the end."""
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    lead, K = x.shape[:-1], x.shape[-1]
+    x2 = x.reshape(-1, K)
+    w16 = np.ascontiguousarray(w16, dtype=np.float16)
+    M, N = x2.shape[0], w16.shape[0]
+    if w16.shape[1] != K:
+        raise ValueError("w's K does not match x's")
+    y = np.zeros((M, N), dtype=np.float16)
+    y32 = np.zeros((M, N), dtype=np.float32) if want_f32 else None
+    _check(lib().qwo_matmul_f16w(_ptr(x2), _ptr(w16), M, N, K, _ptr(y), _ptr(y32) if y32 is not None else None,
+                                 nthreads), "matmul_f16w")
+    y = y.reshape(*lead, N)
+    return (y, y32.reshape(*lead, N)) if want_f32 else y
+
+
+def quantized_matmul_f16acc(x, wq, scales, biases, group_size: int = 64, bits: int = 4):
+    """The matmul evaluated wholly in fp16, one rounded operation at a time:
+    w = dequantize(..., ROUND_TWICE), then acc = fp16(acc + fp16(x[k] * w[k]))
+    in ascending k.  The reading of "every op in the output dtype" carried
+    through the accumulation; used to bound how far such an evaluation lies
+    from the float32-accumulated results (float32 arithmetic rounded to fp16
+    is the correctly rounded fp16 result for one product or one sum of fp16
+    operands)."""
+    w = dequantize(wq, scales, biases, group_size=group_size, bits=bits).astype(np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float16).astype(np.float32)
+    x2 = x.reshape(-1, x.shape[-1])
+    acc = np.zeros((x2.shape[0], w.shape[0]), dtype=np.float16)
+    for k in range(w.shape[1]):
+        p = (x2[:, k:k + 1] * w[None, :, k]).astype(np.float16)
+        acc = (acc.astype(np.float32) + p.astype(np.float32)).astype(np.float16)
+    return acc.reshape(*x.shape[:-1], w.shape[0])
+
+
 def quantized_matmul(x, wq, scales, biases, group_size: int = 64, bits: int = 4,
-                     nthreads: int = 0, want_f32: bool = False):
-    """y = x . dequantize(w)^T with fp32 accumulation; x fp16 [..., K]."""
+                     nthreads: int = 0, want_f32: bool = False, weights: str = "f32"):
+    """y = x . dequantize(w)^T with fp32 accumulation; x fp16 [..., K].
+
+    weights="f32" forms each weight as s*q + b in float32 (two rounded fp32
+    ops); weights="f16" multiplies the fp16 ROUND_TWICE dequantized weights
+    (the `dequantize` output) instead.  Both accumulate in float32 in
+    ascending k."""
+    if weights == "f16":
+        return matmul_f16w(x, dequantize(wq, scales, biases, group_size=group_size, bits=bits),
+                           nthreads=nthreads, want_f32=want_f32)
+    if weights != "f32":
+        raise ValueError(f"weights must be 'f32' or 'f16', got {weights!r}")
     x = np.ascontiguousarray(x, dtype=np.float16)
     lead = x.shape[:-1]
     K = x.shape[-1]

@@ -218,6 +218,34 @@ int qwo_dequantize(const uint32_t* wq, const uint16_t* scales, const uint16_t* b
   return QWO_OK;
 }
 
+/* float32 scales and biases (MLX dequantize with f32 scales returns f32):
+ * QWO_ROUND_TWICE: w = fp32(fp32(s*q) + b), the two ops of `scales * q +
+ * biases` in float32; QWO_ROUND_ONCE: w = fmaf(s, q, b), rounded once.  The
+ * reference's layout test (ffi_tests.rs:3792-3850) dequantizes such arrays. */
+int qwo_dequantize_f32(const uint32_t* wq, const float* scales, const float* biases, int64_t N, int64_t K,
+                       int group_size, int bits, int rounding, float* out) {
+  const int rc = check_params(N, K, group_size, bits);
+  if (rc != QWO_OK) return rc;
+  if (rounding != QWO_ROUND_TWICE && rounding != QWO_ROUND_ONCE) return QWO_EINVAL;
+  const int64_t kw = K * bits / 32;
+  const int64_t G = K / group_size;
+  for (int64_t n = 0; n < N; ++n) {
+    const uint32_t* qr = wq + n * kw;
+    for (int64_t k = 0; k < K; ++k) {
+      const float s = scales[n * G + k / group_size];
+      const float b = biases[n * G + k / group_size];
+      const float q = (float)nibble_at(qr, k, bits);
+      if (rounding == QWO_ROUND_TWICE) {
+        const float t = s * q;
+        out[n * K + k] = t + b;
+      } else {
+        out[n * K + k] = fmaf(s, q, b);
+      }
+    }
+  }
+  return QWO_OK;
+}
+
 /* -------------------------------------------------------- quantized_matmul */
 
 /* binary16 -> binary32 lookup, filled once from qwo_f16_to_f32. */
@@ -422,6 +450,51 @@ int qwo_quantized_matmul(const uint16_t* x, const uint32_t* wq, const uint16_t* 
           y[m * N + nb + j] = qwo_f32_to_f16(acc[j]);
           if (y32) y32[m * N + nb + j] = acc[j];
         }
+      }
+    }
+    free(wblk);
+  }
+  free(xf);
+  return failed ? QWO_EINVAL : QWO_OK;
+}
+
+/* y fp16 [M][N] = x fp16 [M][K] . w^T for fp16 weights w [N][K] (for example
+ * qwo_dequantize's ROUND_TWICE output), each product and sum one fp32
+ * operation, summed in ascending k: the matmul with the weights formed in
+ * fp16 first instead of fp32. */
+int qwo_matmul_f16w(const uint16_t* x, const uint16_t* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
+                    float* y32, int nthreads) {
+  if (M < 0 || N < 0 || K <= 0) return QWO_EINVAL;
+  if (M == 0 || N == 0) return QWO_OK;
+  init_f16_table();
+  float* xf = (float*)malloc((size_t)(M * K) * sizeof(float));
+  if (!xf) return QWO_EINVAL;
+  qwo_f16_to_f32_array(x, xf, M * K);
+  int nt = nthreads > 0 ? nthreads : qwo_max_threads();
+  (void)nt;
+  int failed = 0;
+#pragma omp parallel num_threads(nt)
+  {
+    float* wblk = (float*)malloc((size_t)K * QWO_RB * sizeof(float));
+    if (!wblk) {
+#pragma omp atomic write
+      failed = 1;
+    }
+#pragma omp for schedule(dynamic, 1)
+    for (int64_t nb = 0; nb < N; nb += QWO_RB) {
+      if (!wblk) continue;
+      const int rb = (int)((N - nb) < QWO_RB ? (N - nb) : QWO_RB);
+      for (int j = 0; j < QWO_RB; ++j)
+        for (int64_t k = 0; k < K; ++k) wblk[k * QWO_RB + j] = j < rb ? f16_table[w[(nb + j) * K + k]] : 0.0f;
+      for (int64_t m0 = 0; m0 < M; m0 += 4) {
+        const int nm = (int)((M - m0) < 4 ? (M - m0) : 4);
+        float acc[4][QWO_RB];
+        block_rows_avx2(xf, K, wblk, m0, nm, acc);
+        for (int i = 0; i < nm; ++i)
+          for (int j = 0; j < rb; ++j) {
+            y[(m0 + i) * N + nb + j] = qwo_f32_to_f16(acc[i][j]);
+            if (y32) y32[(m0 + i) * N + nb + j] = acc[i][j];
+          }
       }
     }
     free(wblk);

@@ -69,6 +69,16 @@ int qwo_dequantize(const uint32_t* wq, const uint16_t* scales, const uint16_t* b
                    int64_t N, int64_t K, int group_size, int bits, int rounding,
                    uint16_t* out);
 
+/* out f32 [N][K] = dequantize(wq, scales, biases) for float32 scales and
+ * biases: ROUND_TWICE w = fp32(fp32(s*q) + b); ROUND_ONCE w = fmaf(s, q, b). */
+int qwo_dequantize_f32(const uint32_t* wq, const float* scales, const float* biases, int64_t N, int64_t K,
+                       int group_size, int bits, int rounding, float* out);
+
+/* y fp16 [M][N] = x fp16 [M][K] . w^T for fp16 weights w [N][K]: products
+ * and sums in fp32, ascending k (the matmul on weights formed in fp16). */
+int qwo_matmul_f16w(const uint16_t* x, const uint16_t* w, int64_t M, int64_t N, int64_t K, uint16_t* y,
+                    float* y32, int nthreads);
+
 /* y fp16 [M][N] = x fp16 [M][K] . dequantize(w)^T (transpose = true form).
  * y32 (nullable) receives the fp32 accumulators before the final rounding.
  * nthreads <= 0 uses every OpenMP thread. */

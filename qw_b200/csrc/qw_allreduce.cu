@@ -17,12 +17,17 @@
 //   2. waits, bounded, until flags (parity, r, b) of its own buffer reach e
 //      for every rank r (acquire), then sums its chunk over the P slots in
 //      rank order (every rank gets identical y) and writes fp16 (or fp32).
-// The epoch of chunk b lives in device memory (CTA b bumps it), so a call
-// captured in a CUDA graph advances on every replay, and every rank runs the
-// same sequence of calls, so the epochs agree without a host exchange.  Two
-// parities make the reuse safe: a rank can only store call e + 2's chunk
-// after every rank has flagged call e + 1 for it, which each rank does only
-// after its call e finished reading the chunk.
+// Every chunk of a call uses the same epoch e (parity e & 1): the call's
+// number, kept in device memory and advanced by the last CTA of the call to
+// finish, so a call captured in a CUDA graph advances on every replay, and
+// every rank runs the same sequence of calls, so the epochs agree without a
+// host exchange.  The grid, and so each chunk's range, depends on n, so
+// calls of different sizes cut the vector differently; a call-wide parity
+// keeps that safe.  Two parities make the reuse safe: a rank stores call
+// e + 2 only after its own call e + 1 completed, which needed every rank's
+// flag of call e + 1 for some chunk, and a rank flags call e + 1 only after
+// its whole call e completed (a call reads its epoch after the previous
+// kernel of the stream completed).
 // No multicast, no NVLS: plain loads and stores to mapped peer memory.  A
 // rank whose peers never flag gives up after the wait bound, records a
 // status and returns (its output is then incomplete).
@@ -43,7 +48,7 @@ constexpr size_t kArFlagBytes = (size_t)2 * kArMaxRanks * kArMaxChunks * sizeof(
 struct ArParams {
   float* data[kArMaxRanks];       // each rank's data area (mapped here)
   unsigned int* flags[kArMaxRanks];
-  unsigned int* epochs;           // local: one per chunk
+  unsigned int* epochs;           // local: [0] the last finished call's epoch, [1] CTAs done in this call
   unsigned int* status;
   int P, rank;
   long long n_max;
@@ -74,7 +79,12 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p,
   // (every kernel of these streams waits on its predecessor before it ends).
   pdl_wait();
   pdl_launch_dependents();
-  const unsigned int e = p.epochs[b] + 1u;  // only CTA b of these calls touches it
+  // Every CTA reads the epoch before it counts itself done below, and the
+  // last CTA to count writes the next one, so all CTAs of a call see the same.
+  __shared__ unsigned int s_e;
+  if (threadIdx.x == 0) s_e = *(volatile unsigned int*)p.epochs + 1u;
+  __syncthreads();
+  const unsigned int e = s_e;
   const int par = (int)(e & 1u);
 
   // 1. scatter into slot (par, rank) of every rank, then flag the chunk
@@ -147,7 +157,13 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p,
       }
     }
   }
-  if (threadIdx.x == 0) p.epochs[b] = e;
+  if (threadIdx.x == 0) {
+    __threadfence();  // this CTA's read of the epoch precedes its count
+    if (atomicAdd(p.epochs + 1, 1u) == gridDim.x - 1) {
+      p.epochs[1] = 0u;
+      *(volatile unsigned int*)p.epochs = e;
+    }
+  }
 }
 
 }  // namespace
@@ -156,7 +172,7 @@ size_t allreduce_buffer_bytes(int P, int64_t n_max) {
   return kArFlagBytes + (size_t)2 * P * (size_t)n_max * sizeof(float);
 }
 
-size_t allreduce_epoch_bytes() { return kArMaxChunks * sizeof(unsigned int); }
+size_t allreduce_epoch_bytes() { return 2 * sizeof(unsigned int); }
 
 cudaError_t launch_allreduce(const ArComm& c, const float* partial, void* out, bool out_f32, bool vec, int64_t n,
                              int sm_count, cudaStream_t stream) {

@@ -1010,24 +1010,28 @@ int qw_device_status(int device, unsigned int* status, int clear) {
   cudaGetDevice(&prev);
   cudaError_t ce = cudaSetDevice(device);
   if (ce != cudaSuccess) return cuda_fail(ce, "cudaSetDevice");
-  DeviceRes* res = nullptr;
-  std::string err;
-  if (!device_res(device, &res, &err)) {
-    cudaSetDevice(prev);
-    return fail(QW_ENOMEM, err);
+  // No allocation here: a device whose status word was never created ran no
+  // kernel that could set it, and the static-scratch array exists already.
+  unsigned int* lib_status = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_res_mu);
+    auto it = g_dev_res.find(device);
+    if (it != g_dev_res.end()) lib_status = it->second.status;
   }
   ce = cudaDeviceSynchronize();
-  unsigned int v = 0;
-  if (ce == cudaSuccess) ce = cudaMemcpy(&v, res->status, sizeof v, cudaMemcpyDeviceToHost);
+  unsigned int v = 0, vs = 0;
+  if (ce == cudaSuccess && lib_status) ce = cudaMemcpy(&v, lib_status, sizeof v, cudaMemcpyDeviceToHost);
   if (ce == cudaSuccess && clear && v != 0) {
-    ce = cudaMemset(res->status, 0, sizeof v);
+    ce = cudaMemset(lib_status, 0, sizeof v);
     // A kernel that gave up may have left split-tile counters raised.
     std::lock_guard<std::mutex> lock(g_res_mu);
     for (auto& kv : g_scratch)
       if (kv.first.first == device && kv.second.base) cudaMemset(kv.second.base, 0, kv.second.bytes);
   }
+  if (ce == cudaSuccess) ce = static_scratch_status(device, &vs, clear != 0);
   cudaSetDevice(prev);
   if (ce != cudaSuccess) return cuda_fail(ce, "reading the device status");
+  if (v == 0) v = vs;
   *status = v;
   return v ? QW_ETIMEOUT : QW_OK;
 }

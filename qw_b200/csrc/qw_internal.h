@@ -133,6 +133,10 @@ size_t allreduce_epoch_bytes();
 cudaError_t launch_allreduce(const ArComm& c, const float* partial, void* out, bool out_f32, bool vec, int64_t n,
                              int sm_count, cudaStream_t stream);
 
+// Status word of the static-scratch entry point's array on `device` (current
+// and synchronized), cleared when `clear`; 0 when no such call ran there.
+cudaError_t static_scratch_status(int device, unsigned int* v, bool clear);
+
 // Quantize / dequantize kernels (affine, 4-bit, group 64 for now).
 cudaError_t launch_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N,
                               int64_t K, int group_size, int bits, int rounding, cudaStream_t stream);

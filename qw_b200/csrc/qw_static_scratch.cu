@@ -42,10 +42,10 @@
 // partial-sum slots of 128 x 16 floats per SM).  On a 148-SM B200 a call needs
 // at most 2.6 MiB.  Other requests return QW_EUNSUPPORTED with a message.
 //
-// Errors: like qw_quantized_matmul's, except for a kernel that gives up on one
-// of its bounded waits: it records the cause in a status word at the start of
-// this array, which no entry point reads back, so such a call shows up only
-// as an incomplete y.
+// Errors: like qw_quantized_matmul's.  A kernel that gives up on one of its
+// bounded waits records the cause in a status word at the start of this
+// array; qw_device_status reads it (and clears it on request) together with
+// the library's own status word, without allocating.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -96,6 +96,23 @@ bool static_scratch_address(int device, void** out, std::string* err) {
 }
 
 }  // namespace
+
+// The static array's status word on `device` (0 if no static-scratch call has
+// run there), cleared when `clear`; allocates nothing.  The caller has made
+// `device` current and synchronized it.
+cudaError_t static_scratch_status(int device, unsigned int* v, bool clear) {
+  *v = 0;
+  void* p = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (device >= 0 && device < kMaxDevices) p = g_static_ptr[device];
+  }
+  if (p == nullptr) return cudaSuccess;  // never resolved: no call ran on this device
+  cudaError_t ce = cudaMemcpy(v, p, sizeof *v, cudaMemcpyDeviceToHost);
+  if (ce == cudaSuccess && clear && *v != 0) ce = cudaMemset(p, 0, sizeof *v);
+  return ce;
+}
+
 }  // namespace qw
 
 using namespace qw;

@@ -2,9 +2,11 @@
 GPU: every rank gets the fp32 partials summed in rank order, bit for bit the
 float32 sum numpy forms in the same order (and its fp16 rounding); sizes that
 are and are not multiples of the 4-float vector; repeated calls, eager and
-replayed from a CUDA graph (the epoch advances on the device); and a rank
-whose peer never calls gives up after the bounded wait with a timeout status
-instead of hanging.  Needs at least 2 GPUs (skipped otherwise); NVLS off."""
+replayed from a CUDA graph (the epoch advances on the device); calls of
+different sizes (so different grids and chunk boundaries) issued back to back
+with no host synchronization while one rank starts each call late; and a
+rank whose peer never calls gives up after the bounded wait with a timeout
+status instead of hanging.  Needs at least 2 GPUs (skipped otherwise); NVLS off."""
 import os
 import socket
 import time
@@ -16,6 +18,9 @@ import torch
 pytestmark = pytest.mark.gpu
 
 SIZES = [5120, 5121, 16 * 5120, 3]
+# Back-to-back calls whose grids differ: 148 chunks (a prefill-sized vector),
+# 3 (one decode row), 40 (sixteen rows), 1, ...
+MIXED = [64 * 5120, 5120, 64 * 5120, 16 * 5120, 3, 5121, 64 * 5120, 16 * 5120, 5120] * 3
 
 
 def _free_port():
@@ -46,8 +51,23 @@ def _rank_main(rank, world, port, out_q, scenario):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     try:
-        ar = tp.PeerAllreduce(max(SIZES))
-        if scenario == "sums":
+        ar = tp.PeerAllreduce(max(SIZES + MIXED))
+        if scenario == "mixed":
+            # every partial uploaded first, then all calls queued on one
+            # stream without a host sync; the last rank starts each call late
+            # (a bounded device spin before it), so the others run ahead
+            parts = [torch.from_numpy(_partial(rank, n, 500 + i)).to(dev) for i, n in enumerate(MIXED)]
+            ys = [torch.empty(n, dtype=torch.float16, device=dev) for n in MIXED]
+            torch.cuda.synchronize()
+            dist.barrier()
+            for i, (part, y) in enumerate(zip(parts, ys)):
+                if rank == world - 1:
+                    torch.cuda._sleep(20000 + 15000 * (i % 4))
+                ar(part, y)
+            torch.cuda.synchronize()
+            out_q.put((rank, "ok", ([y.cpu().numpy() for y in ys], ops.device_status(rank, clear=True))))
+            dist.barrier()
+        elif scenario == "sums":
             results = []
             for step, n in enumerate(SIZES * 2):
                 part = torch.from_numpy(_partial(rank, n, step)).to(dev)
@@ -138,6 +158,22 @@ def test_peer_allreduce_sums_exactly(world):
             ref = _expected(world, 5120, step).astype(np.float16)
             for y in ys:
                 np.testing.assert_array_equal(y.view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_allreduce_mixed_sizes_unsynchronized(world):
+    """Grids of 148, 3, 40 and 1 chunks interleaved: every call's chunks share
+    one epoch and parity, so a rank running ahead never stores into a slot a
+    slower rank is still summing."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    got = _run(world, "mixed")
+    for r in range(world):
+        ys, status = got[r]
+        assert status == 0
+        for i, (n, y) in enumerate(zip(MIXED, ys)):
+            ref = _expected(world, n, 500 + i).astype(np.float16)
+            np.testing.assert_array_equal(y.view(np.uint16), ref.view(np.uint16), err_msg=f"call {i} (n={n})")
 
 
 def test_absent_peer_times_out(cuda_dev):

@@ -110,6 +110,45 @@ def test_single_config_full_size(M):
     assert rel_err(y32, y_ref) <= 1e-3
 
 
+def test_single_config_against_both_weight_conventions():
+    """BASELINE's single configuration (seed 0, M=1) against the oracle in
+    both weight-formation conventions: fp32-formed s*q + b (the decode
+    kernel's arithmetic) and the fp16 `dequantize` weights (MLX's op-by-op
+    output dtype).  Both within the north-star bar.  The kernel's fp32
+    accumulators lie within 1e-4 * rms of the fp32-formed oracle's."""
+    wq, s, b = quantized(17408, 5120, seed=0)
+    x = synth.activations(1, 5120, seed=0)
+    _, y_f32w = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    _, y_f16w = oracle.quantized_matmul(x, wq, s, b, weights="f16", want_f32=True)
+    y = run_qmm(x, wq, s, b)
+    assert rel_err(y, y_f32w) <= TOL
+    assert rel_err(y, y_f16w) <= TOL
+    y32 = run_qmm(x, wq, s, b, out_dtype=torch.float32)
+    assert rel_err(y32, y_f32w) <= 1e-4
+    assert rel_err(y32, y_f16w) <= 4e-3
+
+
+def test_sixteen_and_seventeen_rows_agree_on_shared_rows():
+    """The same 16 rows of x through the decode kernel (M=16, fp32-formed
+    weights) and, with one more row, through the tensor-core kernel (M=17,
+    fp16 ROUND_TWICE weights): a verify batch that grows past 16 rows changes
+    arithmetic, and the shared rows' outputs move by at most 5e-3 * rms
+    (half the north-star bar; the oracle's two conventions differ by 2.8e-3
+    * rms at this shape, plus the fp16 output rounding)."""
+    wq, s, b = quantized(17408, 5120, seed=0)
+    x17 = synth.activations(17, 5120, seed=3)
+    y16 = run_qmm(x17[:16], wq, s, b)
+    y17 = run_qmm(x17, wq, s, b)
+    _, y_ref = oracle.quantized_matmul(x17[:16], wq, s, b, want_f32=True)
+    assert rel_err(y16, y_ref) <= TOL
+    assert rel_err(y17[:16], y_ref) <= TOL
+    d = np.abs(y16.astype(np.float64) - y17[:16].astype(np.float64))
+    assert d.max() <= 5e-3 * np.sqrt(np.mean(y_ref.astype(np.float64) ** 2))
+    y32_16 = run_qmm(x17[:16], wq, s, b, out_dtype=torch.float32)
+    y32_17 = run_qmm(x17, wq, s, b, out_dtype=torch.float32)
+    assert rel_err(y32_16, y32_17[:16]) <= 4e-3
+
+
 @pytest.mark.parametrize("lin", synth.layer_linears() + [synth.LM_HEAD], ids=lambda l: l.name)
 def test_stack_shapes_m1(lin):
     wq, s, b = quantized(lin.N, lin.K, seed=lin.tid)

@@ -124,6 +124,119 @@ def test_dequantize_commutes_with_output_axis_slice():
             np.testing.assert_array_equal(part.view(np.uint16), full[sl].view(np.uint16))
 
 
+def _reference_layout_case():
+    """The exact inputs of crates/mlxcel-core/src/ffi_tests.rs:3792-3850:
+    2 experts x 8 rows x 64 inputs, 4 bits, group 32, word (e, r, c) =
+    0x12345678 + 131e + 17r + c, float32 scales 0.05 + 0.01e + 0.001r +
+    0.0003g and biases -0.2 + 0.02e - 0.003r + 0.0007g (each formed in
+    float32 as the reference's Rust expressions are)."""
+    experts, rows, K, gs = 2, 8, 64, 32
+    packed, groups = K * 4 // 32, K // gs
+    w = np.zeros((experts, rows, packed), dtype=np.uint32)
+    s = np.zeros((experts, rows, groups), dtype=np.float32)
+    b = np.zeros((experts, rows, groups), dtype=np.float32)
+    f = np.float32
+    for e in range(experts):
+        for r in range(rows):
+            for c in range(packed):
+                w[e, r, c] = (0x12345678 + e * 131 + r * 17 + c) & 0xFFFFFFFF
+            for g in range(groups):
+                s[e, r, g] = f(0.05) + f(0.01) * f(e) + f(0.001) * f(r) + f(0.0003) * f(g)
+                b[e, r, g] = f(-0.2) + f(0.02) * f(e) - f(0.003) * f(r) + f(0.0007) * f(g)
+    return w, s, b, gs
+
+
+@pytest.mark.parametrize("rounding", [oracle.ROUND_TWICE, oracle.ROUND_ONCE])
+def test_reference_layout_case_exact_inputs(rounding):
+    """The reference's deterministic dequantize test on its own inputs (group
+    32, float32 scales and biases, [2, 8, 64]): dequantizing each half of the
+    row axis equals the same half of the whole tensor's dequantization, bit
+    for bit; and every element is the stated float32 sequence (s*q then + b,
+    or one fused rounding), checked against numpy."""
+    w, s, b, gs = _reference_layout_case()
+    E, R, _ = w.shape
+    full = oracle.dequantize_f32(w.reshape(E * R, -1), s.reshape(E * R, -1), b.reshape(E * R, -1),
+                                 group_size=gs, rounding=rounding).reshape(E, R, -1)
+    assert full.shape == (2, 8, 64) and full.dtype == np.float32
+    half = R // 2
+    for lo, hi in ((0, half), (half, R)):
+        part = oracle.dequantize_f32(np.ascontiguousarray(w[:, lo:hi]).reshape(E * (hi - lo), -1),
+                                     np.ascontiguousarray(s[:, lo:hi]).reshape(E * (hi - lo), -1),
+                                     np.ascontiguousarray(b[:, lo:hi]).reshape(E * (hi - lo), -1),
+                                     group_size=gs, rounding=rounding).reshape(E, hi - lo, -1)
+        assert part.tobytes() == np.ascontiguousarray(full[:, lo:hi]).tobytes()
+    # element values: nibble k of the row at bits 4*(k % 8) of word k // 8
+    k = np.arange(64)
+    q = ((w[..., k // 8] >> (4 * (k % 8)).astype(np.uint32)) & 0xF).astype(np.float32)
+    sg, bg = np.repeat(s, gs, axis=-1), np.repeat(b, gs, axis=-1)
+    if rounding == oracle.ROUND_TWICE:
+        want = (sg * q).astype(np.float32) + bg
+    else:
+        want = (sg.astype(np.float64) * q + bg).astype(np.float32)  # s*q is exact in float64
+    np.testing.assert_array_equal(full.view(np.uint32), want.astype(np.float32).view(np.uint32))
+
+
+def test_reference_layout_case_in_fp16():
+    """The same words, scales and biases cast to fp16 (the checkpoint's scale
+    dtype): the fp16 dequantization at group 32 commutes with the row slice
+    and matches the numpy restatement bit for bit."""
+    w, s, b, gs = _reference_layout_case()
+    E, R, P = w.shape
+    w2, s2, b2 = w.reshape(E * R, P), s.reshape(E * R, -1).astype(np.float16), b.reshape(E * R, -1).astype(np.float16)
+    full = oracle.dequantize(w2, s2, b2, group_size=gs)
+    np.testing.assert_array_equal(full.view(np.uint16), np_ref.dequantize(w2, s2, b2, group_size=gs).view(np.uint16))
+    for e in range(E):
+        for lo, hi in ((0, R // 2), (R // 2, R)):
+            sl = slice(e * R + lo, e * R + hi)
+            part = oracle.dequantize(np.ascontiguousarray(w2[sl]), np.ascontiguousarray(s2[sl]),
+                                     np.ascontiguousarray(b2[sl]), group_size=gs)
+            np.testing.assert_array_equal(part.view(np.uint16), full[sl].view(np.uint16))
+
+
+def test_weight_formation_modes_are_their_stated_sequences():
+    """weights="f16" multiplies the ROUND_TWICE fp16 weights, summing fp32
+    products in ascending k; quantized_matmul_f16acc rounds every product and
+    every partial sum to fp16.  Both checked against plain Python loops."""
+    w = synth.weight_fp16(9, 192, seed=41)
+    wq, s, b = oracle.quantize(w)
+    x = synth.activations(3, 192, seed=42)
+    w16 = oracle.dequantize(wq, s, b)
+    y16w = oracle.quantized_matmul(x, wq, s, b, weights="f16")
+    y16acc = oracle.quantized_matmul_f16acc(x, wq, s, b)
+    for m in range(3):
+        for n in range(9):
+            acc = np.float32(0)
+            acc16 = np.float16(0)
+            for k in range(192):
+                p = np.float32(x[m, k]) * np.float32(w16[n, k])
+                acc = np.float32(acc + p)
+                acc16 = np.float16(np.float32(acc16) + np.float32(np.float16(p)))
+            assert y16w[m, n].view(np.uint16) == np.float16(acc).view(np.uint16)
+            assert y16acc[m, n].view(np.uint16) == acc16.view(np.uint16)
+
+
+def test_weight_formation_convention_is_inside_the_bar():
+    """How far the two float32-accumulating conventions lie apart at
+    BASELINE's single configuration (x [1, 5120], W [17408, 5120], seed 0):
+    fp32-formed weights (the oracle's default) against the fp16 `dequantize`
+    weights (MLX's op-by-op dtype).  Measured 2.8e-3 * rms; the north-star
+    bar is 1e-2 * rms, so either convention passes against the other.
+    Accumulating in fp16 instead (quantized_matmul_f16acc, every product
+    and partial sum rounded) lands 8.4e-2 * rms away at this K, far outside
+    the bar, which is why the oracle pins float32 accumulation as the north
+    star states; here that is shown on 1024 of the rows."""
+    N, K = 17408, 5120
+    w = synth.weight_fp16(N, K, seed=0)
+    wq, s, b = oracle.quantize(w)
+    x = synth.activations(1, K, seed=0)
+    _, y32 = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    y16w = oracle.quantized_matmul(x, wq, s, b, weights="f16")
+    assert rel_err(y16w, y32) <= 4e-3
+    rows = slice(0, 1024)
+    y16acc = oracle.quantized_matmul_f16acc(x, wq[rows], s[rows], b[rows])
+    assert rel_err(y16acc, y32[:, rows]) > 2e-2
+
+
 def test_packing_invariant_is_enforced():
     """packed_in * 32 == bits * groups * group_size (layers.rs:1568-1570)."""
     with pytest.raises(ValueError):
