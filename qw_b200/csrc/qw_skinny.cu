@@ -34,6 +34,11 @@
 // writes silu(gate) * up, rounded to fp16 after each op as the reference's
 // fp16 arrays are; the 2I projection outputs are never stored.
 //
+// One token with 4-bit codes: the 8 groups of a unit are the 8 columns of
+// the MMAs (group gi's B fragment is x in the lanes of column gi and zero in
+// the others), so one accumulator pair collects the whole unit and the fold
+// below runs once per unit instead of once per group.
+//
 // Consumer arithmetic (no per-element dequantisation): a packed word w holds
 // nibbles q0..q7 (k ascending).  lop3(w & 0x000F000F | 0x64006400) is the fp16
 // pair (1024 + q0, 1024 + q4) and lop3(w & 0x00F000F0 | 0x64006400) is
@@ -90,8 +95,11 @@ struct SkinnyCfg {
   // boxes of 128 bytes) or 512 bytes of 8-bit codes (four boxes), so 8-bit
   // stages are twice as large and the rings shallower.
   static constexpr int NBOX = BITS == 8 ? 4 : 2;
+  // One token with 4-bit codes: the 8 groups of a unit are the 8 columns of
+  // the MMAs (see the consumer), with B fragments masked per group.
+  static constexpr bool COLS = MT == 1 && BITS == 4;
   static constexpr int WST = BITS == 8 ? (MT == 1 ? 3 : 2) : (MT == 1 ? 5 : (MT <= 8 ? 4 : 3));
-  static constexpr int SST = BITS == 8 ? 2 : (MT == 1 ? 4 : (MT <= 8 ? 3 : 2));
+  static constexpr int SST = BITS == 8 ? 2 : (MT == 1 ? (COLS ? 3 : 4) : (MT <= 8 ? 3 : 2));
   static constexpr int W_BOX = BN * 128;
   static constexpr int SB_BYTES = BN * 16;
   static constexpr int W_STAGE = NBOX * W_BOX + 2 * SB_BYTES;  // W boxes, scales, biases
@@ -99,7 +107,10 @@ struct SkinnyCfg {
   static constexpr int OFF_WB = OFF_WS + SB_BYTES;
   static constexpr int X_BYTES = kGroupsPerStage * MT * 128;
   static constexpr int BF_TOK = MT;
-  static constexpr int BF_BYTES = kGroupsPerStage * BF_TOK * 4 * 32;
+  // COLS: per group a 1 KB block [b0 | b1][32 lanes][16 bytes], zero except
+  // the four lanes of MMA column (= group) gi; otherwise per (group, token,
+  // lane column) 32 bytes.
+  static constexpr int BF_BYTES = COLS ? kGroupsPerStage * 1024 : kGroupsPerStage * BF_TOK * 4 * 32;
   static constexpr int XZ_COLS = 8 * NT;
   static constexpr int XZ_BYTES = kGroupsPerStage * XZ_COLS * 8;
   static constexpr int OFF_X = 0;  // within a small stage (1024-aligned for SW128)
@@ -181,6 +192,11 @@ __device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
@@ -509,8 +525,16 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
     // ------------------------------------------------------------- helpers
     const int h = warp - 2;
     pdl_wait();
+    // COLS: the B blocks are zero outside the lanes of their own group's
+    // column, for the whole launch; only those lanes are written per unit.
+    if (Cfg::COLS) {
+      for (int e = h * 32 + lane; e < SST * (Cfg::BF_BYTES / 16); e += Cfg::HW * 32)
+        sts128(smem_u32(sring + (e / (Cfg::BF_BYTES / 16)) * Cfg::S_STAGE + Cfg::OFF_BF) +
+                   (e % (Cfg::BF_BYTES / 16)) * 16,
+               make_uint4(0u, 0u, 0u, 0u));
+    }
     // (X, Z) of token columns >= M stay zero for the whole launch.
-    for (int e = h * 32 + lane; e < SST * kGroupsPerStage * Cfg::XZ_COLS; e += Cfg::HW * 32) {
+    for (int e = h * 32 + lane; !Cfg::COLS && e < SST * kGroupsPerStage * Cfg::XZ_COLS; e += Cfg::HW * 32) {
       const int slot = e / (kGroupsPerStage * Cfg::XZ_COLS);
       const int col = e % Cfg::XZ_COLS;
       if (col >= p.M) {
@@ -573,9 +597,15 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           f1.y = prmt(xv1.y, xv1.w, 0x5410);
           f1.z = hmul2_rn(prmt(xv0.y, xv0.w, 0x7632), 0x2C002C00u);
           f1.w = hmul2_rn(prmt(xv1.y, xv1.w, 0x7632), 0x2C002C00u);
-          const uint32_t fa = bf + ((gi * Cfg::BF_TOK + n) * 4 + s) * 32;
-          sts128(fa, f0);
-          sts128(fa + 16, f1);
+          if (Cfg::COLS) {
+            // lane (row gi, column s) of group gi's block: MMA column gi
+            sts128(bf + gi * 1024 + (gi * 4 + s) * 16, f0);
+            sts128(bf + gi * 1024 + 512 + (gi * 4 + s) * 16, f1);
+          } else {
+            const uint32_t fa = bf + ((gi * Cfg::BF_TOK + n) * 4 + s) * 32;
+            sts128(fa, f0);
+            sts128(fa + 16, f1);
+          }
           // sums over even and odd k of the 16 x values this lane holds
           float xe = 0.f, xo = 0.f;
           const uint32_t wv[8] = {xv0.x, xv0.y, xv0.z, xv0.w, xv1.x, xv1.y, xv1.z, xv1.w};
@@ -589,7 +619,8 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           xo += __shfl_xor_sync(0xffffffffu, xo, 1);
           xe += __shfl_xor_sync(0xffffffffu, xe, 2);
           xo += __shfl_xor_sync(0xffffffffu, xo, 2);
-          if (s == 0) sts_f32x2(xz + (gi * Cfg::XZ_COLS + n) * 8, xe + xo, 1024.f * xe + 64.f * xo);
+          if (s == 0)
+            sts_f32x2(xz + (Cfg::COLS ? gi : gi * Cfg::XZ_COLS + n) * 8, xe + xo, 1024.f * xe + 64.f * xo);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&ready[slot]);
@@ -716,6 +747,21 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
       wphase ^= 1u;
     }
   };
+  // Scales and biases of this lane's rows: all 8 groups (16 bytes a row), or
+  // with COLS the two groups 2 s4, 2 s4 + 1 of its MMA columns (4 bytes).
+  auto load_sb = [&](uint32_t wb) {
+    if (Cfg::COLS) {
+      sv_lo.x = lds32(wb + Cfg::OFF_WS + sb_off + 4 * s4);
+      sv_hi.x = lds32(wb + Cfg::OFF_WS + sb_off + kSbHi + 4 * s4);
+      bv_lo.x = lds32(wb + Cfg::OFF_WB + sb_off + 4 * s4);
+      bv_hi.x = lds32(wb + Cfg::OFF_WB + sb_off + kSbHi + 4 * s4);
+    } else {
+      sv_lo = lds128(wb + Cfg::OFF_WS + sb_off);
+      sv_hi = lds128(wb + Cfg::OFF_WS + sb_off + kSbHi);
+      bv_lo = lds128(wb + Cfg::OFF_WB + sb_off);
+      bv_hi = lds128(wb + Cfg::OFF_WB + sb_off + kSbHi);
+    }
+  };
   auto copy_unit = [&]() {
     if (!*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
     const uint32_t wb = wring_u + wslot * Cfg::W_STAGE;
@@ -729,10 +775,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
       for (int gi = 0; gi < 8; ++gi)
         ldmatrix_x4(wb + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
     }
-    sv_lo = lds128(wb + Cfg::OFF_WS + sb_off);
-    sv_hi = lds128(wb + Cfg::OFF_WS + sb_off + kSbHi);
-    bv_lo = lds128(wb + Cfg::OFF_WB + sb_off);
-    bv_hi = lds128(wb + Cfg::OFF_WB + sb_off + kSbHi);
+    load_sb(wb);
     if (BITS != 8) release_wslot();
   };
   if (total > 0) copy_unit();
@@ -750,7 +793,51 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
       const uint32_t wb_next = wring_u + wslot * Cfg::W_STAGE;
       // compute against the unit's x fragments, refilling A with the next unit
       if (!*abort_flag && !mbar_wait(&ready[sslot], sphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
-      {
+      if constexpr (Cfg::COLS) {
+        // One token, 4-bit codes.  MMA column n of a unit is its group n:
+        // group gi's B block is x's fragment in the lanes of column gi and zero
+        // in the others, so one accumulator pair collects all 8 groups, each in
+        // its own column (d = 1024 X_even + 64 X_odd + sum_k x_k q_k of that
+        // group), and the fold runs once per unit: lane (r, s4) folds groups
+        // 2 s4 and 2 s4 + 1 of rows r and r + 8, and the four lanes of a row
+        // are summed when the row's segment ends.
+        const uint32_t stu = smem_u32(sring + sslot * Cfg::S_STAGE);
+        float dA[4], dB[4];
+#pragma unroll
+        for (int gi = 0; gi < 8; ++gi) {
+          const uint4 b0 = lds128(stu + Cfg::OFF_BF + gi * 1024 + lane * 16);
+          const uint4 b1 = lds128(stu + Cfg::OFF_BF + gi * 1024 + 512 + lane * 16);
+          uint32_t e[4][4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t w8 = A[gi][i] >> 8;
+            e[0][i] = lop3_and_or(A[gi][i], 0x000F000Fu);
+            e[1][i] = lop3_and_or(A[gi][i], 0x00F000F0u);
+            e[2][i] = lop3_and_or(w8, 0x000F000Fu);
+            e[3][i] = lop3_and_or(w8, 0x00F000F0u);
+          }
+          if (has_next) {
+            if (gi == 0 && !*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull))
+              *abort_flag = 1;
+            ldmatrix_x4(wb_next + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
+          }
+          if (gi == 0) {
+            mma_16816_zc(dA, e[0][0], e[0][1], e[0][2], e[0][3], b0.x, b0.y);
+            mma_16816_zc(dB, e[1][0], e[1][1], e[1][2], e[1][3], b0.z, b0.w);
+          } else {
+            mma_16816(dA, e[0][0], e[0][1], e[0][2], e[0][3], b0.x, b0.y);
+            mma_16816(dB, e[1][0], e[1][1], e[1][2], e[1][3], b0.z, b0.w);
+          }
+          mma_16816(dA, e[2][0], e[2][1], e[2][2], e[2][3], b1.x, b1.y);
+          mma_16816(dB, e[3][0], e[3][1], e[3][2], e[3][3], b1.z, b1.w);
+        }
+        // (X, Z) of groups 2 s4 and 2 s4 + 1
+        const float4 v = *reinterpret_cast<const float4*>(sring + sslot * Cfg::S_STAGE + Cfg::OFF_XZ + s4 * 16);
+        acc[0][0] = fmaf(half_lo(sv_lo.x), (dA[0] + dB[0]) - v.y, fmaf(half_lo(bv_lo.x), v.x, acc[0][0]));
+        acc[0][0] = fmaf(half_hi(sv_lo.x), (dA[1] + dB[1]) - v.w, fmaf(half_hi(bv_lo.x), v.z, acc[0][0]));
+        acc[0][2] = fmaf(half_lo(sv_hi.x), (dA[2] + dB[2]) - v.y, fmaf(half_lo(bv_hi.x), v.x, acc[0][2]));
+        acc[0][2] = fmaf(half_hi(sv_hi.x), (dA[3] + dB[3]) - v.w, fmaf(half_hi(bv_hi.x), v.z, acc[0][2]));
+      } else {
         const uint8_t* stp = sring + sslot * Cfg::S_STAGE;
         const uint32_t svl[4] = {sv_lo.x, sv_lo.y, sv_lo.z, sv_lo.w}, svh[4] = {sv_hi.x, sv_hi.y, sv_hi.z, sv_hi.w};
         const uint32_t bvl[4] = {bv_lo.x, bv_lo.y, bv_lo.z, bv_lo.w}, bvh[4] = {bv_hi.x, bv_hi.y, bv_hi.z, bv_hi.w};
@@ -832,10 +919,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
         }
       }
       if (has_next) {
-        sv_lo = lds128(wb_next + Cfg::OFF_WS + sb_off);
-        sv_hi = lds128(wb_next + Cfg::OFF_WS + sb_off + kSbHi);
-        bv_lo = lds128(wb_next + Cfg::OFF_WB + sb_off);
-        bv_hi = lds128(wb_next + Cfg::OFF_WB + sb_off + kSbHi);
+        load_sb(wb_next);
         release_wslot();
       }
       __syncwarp();
@@ -852,6 +936,14 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
         ++t;
       }
       if (!seg_end) continue;
+      if constexpr (Cfg::COLS) {
+        // a row's groups were folded in its four lanes: every lane gets the sum
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          acc[0][e] += __shfl_xor_sync(0xffffffffu, acc[0][e], 1);
+          acc[0][e] += __shfl_xor_sync(0xffffffffu, acc[0][e], 2);
+        }
+      }
       const bool whole = (seg_begin == 0) && (c == 0);
 
       if (p.split > 1) {
