@@ -542,11 +542,7 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "f16 activations, u4 weights, f32 accumulate",
         "data": "synthetic: x~N(0,1), W~N(0,0.02) fp16 quantized on GPU (affine, 4-bit, group 64)",
-        "config": {"workload": f"decode linear stack M=1, {args.layers} layers (qkv/o/gate_up+SwiGLU/down) + lm_head",
-                   "M": 1, "layers": args.layers, "hidden": synth.HIDDEN, "vocab": synth.VOCAB,
-                   "parallelism": (f"tp{world}, {args.tp_allreduce} allreduce" if world > 1 else "single"),
-                   "l2": "inputs larger than L2 (weights %.2f GB per step)" % (synth.stack_bytes(1, args.layers) / 1e9),
-                   "graph": "one CUDA graph per step, programmatic dependent launch"},
+        "config": stack_config(args, world),
         "GBps_per_gpu": round(step_bytes / (ms * 1e-3) / 1e9, 1),
         "roofline": None,
         "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,
@@ -561,10 +557,17 @@ def run_ours(args):
     }
     achieved = step_bytes / (ms * 1e-3) / 1e9
     traffic = profile_traffic("qmm_skinny_m1_stack_step")
+    traffic_note = "ncu DRAM bytes of one 1-GPU decode step"
+    if traffic is not None and (P > 1 or args.layers != synth.LAYERS):
+        # per rank: the 1-GPU 64-layer step's DRAM bytes in the proportion of
+        # the rank's algorithmic bytes (every weight matrix is split evenly)
+        traffic = traffic * step_bytes / synth.stack_bytes(1)
+        traffic_note = (f"per rank: the 1-GPU {synth.LAYERS}-layer capture scaled by the rank's share of the "
+                        f"algorithmic bytes ({args.layers} layers, 1/{P})")
     result["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                           "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
                           "kernel": "qmm_skinny_kernel (every launch of the step)",
-                          "traffic": traffic}
+                          "traffic": None if traffic is None else round(traffic), "traffic_source": traffic_note}
 
     if rank == 0 and world == 1 and not args.skip_cpu:
         threads = os.cpu_count() or 1
@@ -597,59 +600,60 @@ def benchmark_result_line(label, tokens_per_repetition, repetitions, elapsed_s):
           f"tokens_per_second={processed / elapsed_s:.3f}", file=sys.stderr, flush=True)
 
 
+def stack_config(args, world):
+    """The workload description both arms print (identical, so the driver can
+    compare the two lines)."""
+    return {"workload": f"decode linear stack M=1, {args.layers} layers (qkv/o/gate_up+SwiGLU/down) + lm_head",
+            "M": 1, "layers": args.layers, "hidden": synth.HIDDEN, "vocab": synth.VOCAB,
+            "parallelism": (f"tp{world}, {args.tp_allreduce} allreduce" if world > 1 else "single"),
+            "l2": "inputs larger than L2 (weights %.2f GB per step)" % (synth.stack_bytes(1, args.layers) / 1e9),
+            "graph": "one CUDA graph per step, programmatic dependent launch"}
+
+
 def run_reference(args):
-    """The reference's CPU path (oracle restatement) on the host cores."""
+    """The reference's CPU path (the oracle restatement of MLX's affine
+    quantized_matmul) on the host cores: every step is one token through the
+    whole stack, as the GPU arm's step is -- per layer q|k|v, o, gate|up with
+    the SwiGLU activation on its two halves, down, then lm_head -- with one
+    decoder layer's quantized weights used for all layers (one layer is 192 MB,
+    so every layer still streams its weights from DRAM)."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     import oracle
     threads = os.cpu_count() or 1
-    # Per step: one decoder layer (its four linears at full size, unless that
-    # would not let warmup + steps finish in about two minutes on this host,
-    # in which case the same leading fraction of every linear's rows).
-    budget_s = 120.0 / max(1, args.steps + args.warmup)
     lins = synth.layer_linears()
     mats = {lin.name: oracle.quantize(synth.weight_fp16(lin.N, lin.K, seed=lin.tid)) for lin in lins}
-    x = {lin.K: synth.activations(1, lin.K, seed=2) for lin in lins}
-    # rate probe: the whole layer once
-    t0 = time.perf_counter()
-    for lin in lins:
-        wq, s, b = mats[lin.name]
-        oracle.quantized_matmul(x[lin.K], wq, s, b, nthreads=threads)
-    probe = time.perf_counter() - t0
-    frac = min(1.0, budget_s / max(probe, 1e-6))
-    rows = {lin.name: max(32, int(lin.N * frac) // 32 * 32) for lin in lins}
+    lm = oracle.quantize(synth.weight_fp16(synth.LM_HEAD.N, synth.LM_HEAD.K, seed=synth.LM_HEAD.tid))
+    xs = {K: synth.activations(1, K, seed=2) for K in {lin.K for lin in lins}}
+
+    def step():
+        for _ in range(args.layers):
+            for lin in lins:
+                y = oracle.quantized_matmul(xs[lin.K], *mats[lin.name], nthreads=threads)
+                if lin.name == "gate_up":  # the MLP activation on the gate and up halves
+                    oracle.swiglu(y[:, : lin.N // 2], y[:, lin.N // 2:])
+        return oracle.quantized_matmul(xs[synth.HIDDEN], *lm, nthreads=threads)
+
     for _ in range(args.warmup):
-        for lin in lins:
-            wq, s, b = mats[lin.name]
-            r = rows[lin.name]
-            oracle.quantized_matmul(x[lin.K], wq[:r], s[:r], b[:r], nthreads=threads)
+        step()
     t0 = time.perf_counter()
-    nbytes = 0
     for _ in range(args.steps):
-        for lin in lins:
-            wq, s, b = mats[lin.name]
-            r = rows[lin.name]
-            y = oracle.quantized_matmul(x[lin.K], wq[:r], s[:r], b[:r], nthreads=threads)
-            if lin.name == "gate_up":  # the MLP activation on the slab's gate and up halves
-                oracle.swiglu(y[:, : r // 2], y[:, r // 2:])
-            nbytes += synth.algorithmic_bytes(1, r, lin.K)
+        step()
     dt = time.perf_counter() - t0
-    gbs = nbytes / dt / 1e9
-    tok_s = gbs * 1e9 / synth.stack_bytes(1, args.layers)
-    shown = ", ".join(f"{lin.name} {rows[lin.name]}/{lin.N}" for lin in lins)
-    sample = (f"one decoder layer per step (rows {shown}) through the C oracle (AVX2, OpenMP, {threads} threads), "
-              f"SwiGLU on the gate_up rows; "
-              f"tok/s = GB/s / {synth.stack_bytes(1, args.layers)} bytes per token")
+    nbytes = synth.stack_bytes(1, args.layers)
+    tok_s = args.steps / dt
+    sample = (f"the whole {args.layers}-layer stack + lm_head per step (one token, M=1) through the C oracle "
+              f"(AVX2, OpenMP, {threads} threads), SwiGLU on the gate_up halves; one layer's weights serve "
+              f"every layer")
     out = {
         "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1000 / args.steps, 4),
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
         "dtype": "f16 activations, u4 weights, f32 accumulate", "data": "synthetic (seeded)",
-        "config": {"workload": f"decode linear stack M=1, {args.layers} layers + lm_head", "M": 1,
-                   "layers": args.layers, "parallelism": "host cores"},
-        "GBps": round(gbs, 3),
+        "config": stack_config(args, world),
+        "GBps": round(nbytes * args.steps / dt / 1e9, 3),
         "cpu_baseline": {"value": round(tok_s, 4), "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(tok_s, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -89,6 +89,11 @@ typedef struct qw_qmm_op {
  * one CTA per SM: a matmul's weights start streaming while the previous
  * matmul finishes, and a grid-wide count of finished CTAs orders the
  * dependent reads.  With larger M or 8-bit codes it issues one launch per op.
+ * Measured slower than one qw_quantized_matmul call per linear on the
+ * 64-layer decode stack (every chained matmul takes stream-K fix-ups and
+ * the grid-wide wait puts its slowest CTA on the critical path); it helps
+ * runs of short matmuls only (o-shaped 5120 x 6144: 13.4 us each in chains of
+ * 8 against 17.7 us).  Bind qw_quantized_matmul for decode.
  * No counterpart in the reference: it fuses a sequence of the reference's
  * quantized_matmul calls (lib.rs:1134-1143) for decode loops whose
  * consecutive linears have nothing in between. */
