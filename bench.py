@@ -4,8 +4,8 @@
 Headline (BASELINE metric "4-bit qmatmul HBM GB/s & % peak at M=1/16; 27B
 linear-stack tok/s"): decode tokens/s of the 64-layer Qwen 27B linear stack at
 M=1 (q|k|v 5120->8192, o 6144->5120, gate|up 5120->34816, down 17408->5120 per
-layer, then lm_head 5120->151936), synthetic seeded weights quantized on the
-GPU by the library's own quantizer.  The MLP's gate|up projection runs with
+layer, then lm_head 5120->151936 and the greedy token over the vocabulary),
+synthetic seeded weights quantized on the GPU by the library's own quantizer.  The MLP's gate|up projection runs with
 its SwiGLU activation fused (qw_quantized_matmul_swiglu), so down consumes
 silu(gate) * up as in the model.  One step = one token through the stack.
 
@@ -13,8 +13,7 @@ silu(gate) * up as in the model.  One step = one token through the stack.
           the library's launches (programmatic dependent launch between them)
   e2e     the same step through the public C ABI call by call (qw_quantized_matmul
           and qw_quantized_matmul_swiglu via ctypes), x copied from pinned host
-          memory before and the logits
-          read back after, every step
+          memory before and the step's greedy token read back after, every step
 Extra keys report the single-matrix qmv (M=1) and verify qmm (M=16) GB/s with
 L2 defeated by rotating weight copies, and the M=16 stack.
 
@@ -164,7 +163,8 @@ class StackRunner:
 
     Per layer: qkv, o, the MLP's gate and up projections with SwiGLU fused
     (qw_quantized_matmul_swiglu over the two row halves of the rank's gate_up
-    shard), down; then lm_head.  chain=False issues one C-ABI call per
+    shard), down; then lm_head and the greedy token of each row (under tensor
+    parallelism over every rank's vocabulary shard).  chain=False issues one C-ABI call per
     linear (the drop-in path); chain=True hands each run of plain matmuls
     with nothing in between (down of one layer with qkv and o of the next on
     one GPU; qkv+o between allreduces under tensor parallelism) to
@@ -187,7 +187,12 @@ class StackRunner:
         self.part = torch.empty(M, H, dtype=f32, device=dev)
         self.o = torch.empty(M, H, dtype=f16, device=dev)
         self.logits = torch.empty(M, lm[0].shape[0], dtype=f16, device=dev)
-        self.launches_per_step = 4 * len(ws) + 1
+        # the step's result: the greedy token of every row over the whole vocabulary
+        self.token = torch.empty(M, dtype=torch.int32, device=dev)
+        self.vocab_base = (torch.distributed.get_rank(group) if P > 1 else 0) * lm[0].shape[0]
+        # per layer 4 matmuls; lm_head + argmax: the fused epilogue's finalize
+        # (1 GPU) or the peer exchange kernel (tensor-parallel)
+        self.launches_per_step = 4 * len(ws) + 2
         if self.chain:
             self._build_segments()
 
@@ -219,11 +224,11 @@ class StackRunner:
                 cur.append((self.gate, *w["down"], self.part))
                 flush()
                 acts.append(("reduce", self.h))
-        cur.append((self.h, *self.lm, self.logits))
         flush()
+        acts.append(("token", None))
         self.actions = acts
         self.launches_per_step = sum((len(a[1]) + 23) // 24 if a[0] == "chain" else 1
-                                     for a in acts if a[0] != "reduce")
+                                     for a in acts if a[0] != "reduce") + 1
 
     def _mm(self, x, w, out):
         self.qw.quantized_matmul(x, w[0], w[1], w[2], out=out)
@@ -246,6 +251,22 @@ class StackRunner:
     def _swiglu(self, x, l, out):
         self.qw.quantized_matmul_swiglu(x, *self.halves[l], out=out)
 
+    def _token(self):
+        """lm_head and the greedy token of each row over the whole vocabulary
+        into self.token: fused into the decode kernel's epilogue on one GPU,
+        qw_allreduce_argmax over the vocabulary shards with the peer exchange,
+        or the shard's keys and an int64 MAX all-reduce with NCCL."""
+        M = self.M
+        logits = self.logits if M > 16 else None
+        if self.P == 1:
+            self.qw.quantized_matmul_argmax(self.h, *self.lm, logits=self.logits, idx=self.token)
+        elif self.ar is not None:
+            self.ar.argmax(self.h, self.lm, self.vocab_base, idx=self.token, logits=logits)
+        else:
+            self._mm(self.h, self.lm, self.logits)
+            keys = tp.greedy_keys_torch(self.logits, self.vocab_base)
+            self.token.copy_(tp.exchange_greedy_keys(keys, self.group))
+
     def step(self):
         if self.chain:
             for a in self.actions:
@@ -253,6 +274,8 @@ class StackRunner:
                     self.qw.quantized_matmul_chain(a[1])
                 elif a[0] == "swiglu":
                     self._swiglu(self.o, a[1], self.gate)
+                elif a[0] == "token":
+                    self._token()
                 else:
                     self._reduce(a[1])
             return
@@ -267,7 +290,7 @@ class StackRunner:
             self._rowpar(attn, w["o"], self.o)
             self._swiglu(self.o, l, self.gate)
             self._rowpar(self.gate, w["down"], self.h)
-        self._mm(self.h, self.lm, self.logits)
+        self._token()
 
 
 def timed_graph(torch, runner, steps, warmup, stream, dist_on, sampler_index):
@@ -306,12 +329,12 @@ def timed_e2e(torch, runner, steps, warmup, stream, dist_on):
     """Eager C-ABI calls; h2d of x from pinned memory and d2h of logits every step."""
     M = runner.M
     x_host = torch.randn(M, synth.HIDDEN).half().pin_memory()
-    y_host = torch.empty(runner.logits.shape, dtype=torch.float16).pin_memory()
+    y_host = torch.empty(runner.token.shape, dtype=runner.token.dtype).pin_memory()
 
     def one():
         runner.h.copy_(x_host, non_blocking=True)
         runner.step()
-        y_host.copy_(runner.logits, non_blocking=True)
+        y_host.copy_(runner.token, non_blocking=True)  # the greedy token of the step
 
     with torch.cuda.stream(stream):
         for _ in range(warmup):
@@ -328,7 +351,7 @@ def timed_e2e(torch, runner, steps, warmup, stream, dist_on):
         e1.record(stream)
     torch.cuda.synchronize()
     ms = reduce_max(torch, e0.elapsed_time(e1) / steps, dist_on)
-    return ms, x_host.numel() * 2, y_host.numel() * 2
+    return ms, x_host.numel() * 2, y_host.numel() * 4
 
 
 def reduce_max(torch, v, dist_on):
@@ -547,7 +570,7 @@ def run_ours(args):
         "roofline": None,
         "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
-                "path": "qw_quantized_matmul per layer via ctypes, eager, pinned host x in / logits out"},
+                "path": "qw_quantized_matmul per layer via ctypes, eager, pinned host x in / greedy token out"},
         "gpu_launches": launches * args.steps,
         "clocks": clocks,
         # a kernel whose bounded wait ran out (a missing peer, a stalled pipeline)

@@ -217,6 +217,24 @@ int qw_allreduce_connect(qw_allreduce* comm, const unsigned char* handles);
 int qw_allreduce_sum(qw_allreduce* comm, const qw_array* partial, qw_array* y, void* stream);
 int qw_allreduce_destroy(qw_allreduce* comm);
 
+/* Greedy token of a vocabulary-sharded LM head under tensor parallelism:
+ * this rank holds rows [index_base, index_base + N) of the head (w, scales,
+ * biases as in qw_quantized_matmul_argmax) and every rank receives in idx
+ * (uint32 [M]) the global argmax of each row of x over all ranks' logits,
+ * the lowest global index among equal maxima, bit for bit what one GPU
+ * holding the whole head returns.  Each rank reduces its own shard (folded
+ * into the decode kernel's epilogue for M <= 16; logits required above),
+ * then one kernel exchanges one 8-byte (value, index) key per row with every
+ * rank over the communicator's buffers and takes the largest.  A collective
+ * call of the same sequence as qw_allreduce_sum (all ranks, same order, same
+ * M); 2 M <= max_elems.
+ * Replaces: project_logits (crates/runtime/src/qwen3_5.rs:1038-1044) then
+ * argmax_last_axis (lib.rs:2055) on a model split over GPUs, which the
+ * single-device reference does not have. */
+int qw_allreduce_argmax(qw_allreduce* comm, const qw_array* x, const qw_array* w, const qw_array* scales,
+                        const qw_array* biases, int group_size, int bits, const char* mode, int64_t index_base,
+                        qw_array* logits, qw_array* idx, void* stream);
+
 /* y = x @ dequantize(w).T (+ linear_bias), linear_bias nullable f16 [N].
  * Replaces: quantized_linear_forward, lib.rs:591-601, mlx_cxx_bridge.cpp:1099-1133. */
 int qw_quantized_linear_forward(const qw_array* x, const qw_array* w, const qw_array* scales,

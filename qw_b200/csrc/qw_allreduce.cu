@@ -63,12 +63,66 @@ __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) 
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// --- the exchange protocol, shared by the sum and the greedy-token kernels.
+// A call's epoch: every CTA reads it before it counts itself done in
+// ar_finish, and the last CTA to count writes the next one, so all CTAs of
+// a call see the same.
+__device__ __forceinline__ unsigned int ar_epoch(const ArParams& p) {
+  __shared__ unsigned int s_e;
+  if (threadIdx.x == 0) s_e = *(volatile unsigned int*)p.epochs + 1u;
+  __syncthreads();
+  return s_e;
+}
+// After a CTA barrier that orders every thread's stores to the slots before
+// it: flag (parity, rank, chunk b) = e in every rank's buffer.
+__device__ __forceinline__ void ar_flag(const ArParams& p, int par, int b, unsigned int e) {
+  if (threadIdx.x < p.P) {
+    __threadfence_system();
+    st_release_sys(p.flags[threadIdx.x] + ((size_t)par * kArMaxRanks + p.rank) * kArMaxChunks + b, e);
+  }
+}
+// Waits, bounded, for every rank's flag of chunk b in this rank's buffer.
+// Once a call has given up (a peer missing), later calls do not wait again:
+// the status stays set until the host clears it, and every call returns at
+// once, so a broken job ends in its own time instead of 2 s per call.
+// Returns (to every thread) whether the chunk's slots may be read.
+__device__ __forceinline__ bool ar_wait(const ArParams& p, int par, int b, unsigned int e) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (threadIdx.x < p.P && *(volatile unsigned int*)p.status == kDevTimeoutPeer) s_ok = 0;
+  __syncthreads();
+  if (threadIdx.x < p.P && s_ok) {
+    const unsigned int* f = p.flags[p.rank] + ((size_t)par * kArMaxRanks + threadIdx.x) * kArMaxChunks + b;
+    if ((int)(ld_acquire_sys(f) - e) < 0) {
+      const uint64_t t0 = globaltimer_ns();
+      while ((int)(ld_acquire_sys(f) - e) < 0) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          record_status(p.status, kDevTimeoutPeer);
+          s_ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+// Counts this CTA done; the call's last CTA publishes its epoch.
+__device__ __forceinline__ void ar_finish(const ArParams& p, unsigned int e) {
+  if (threadIdx.x == 0) {
+    __threadfence();  // this CTA's read of the epoch precedes its count
+    if (atomicAdd(p.epochs + 1, 1u) == gridDim.x - 1) {
+      p.epochs[1] = 0u;
+      *(volatile unsigned int*)p.epochs = e;
+    }
+  }
+}
+
 template <bool OUT_F32>
 __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p, const float* __restrict__ partial,
                                                                void* __restrict__ out, long long n, int vec_ok) {
-  __shared__ int s_ok;
   const int b = blockIdx.x;
-  if (threadIdx.x == 0) s_ok = 1;
   // this CTA's chunk: contiguous, in units of 4 floats
   const long long nv = (n + kArVec - 1) / kArVec;
   const long long per = (nv + gridDim.x - 1) / gridDim.x;
@@ -79,12 +133,7 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p,
   // (every kernel of these streams waits on its predecessor before it ends).
   pdl_wait();
   pdl_launch_dependents();
-  // Every CTA reads the epoch before it counts itself done below, and the
-  // last CTA to count writes the next one, so all CTAs of a call see the same.
-  __shared__ unsigned int s_e;
-  if (threadIdx.x == 0) s_e = *(volatile unsigned int*)p.epochs + 1u;
-  __syncthreads();
-  const unsigned int e = s_e;
+  const unsigned int e = ar_epoch(p);
   const int par = (int)(e & 1u);
 
   // 1. scatter into slot (par, rank) of every rank, then flag the chunk
@@ -102,32 +151,10 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p,
     }
   }
   __syncthreads();  // every thread's stores precede the flags
-  if (threadIdx.x < p.P) {
-    __threadfence_system();
-    st_release_sys(p.flags[threadIdx.x] + ((size_t)par * kArMaxRanks + p.rank) * kArMaxChunks + b, e);
-  }
+  ar_flag(p, par, b, e);
 
-  // 2. wait for every rank's flag of this chunk, then sum it.  Once a call
-  //    has given up (a peer missing), later calls do not wait again: the
-  //    status stays set until the host clears it, and every call returns at
-  //    once, so a broken job ends in its own time instead of 2 s per call.
-  if (threadIdx.x < p.P && *(volatile unsigned int*)p.status == kDevTimeoutPeer) s_ok = 0;
-  __syncthreads();
-  if (threadIdx.x < p.P && s_ok) {
-    const unsigned int* f = p.flags[p.rank] + ((size_t)par * kArMaxRanks + threadIdx.x) * kArMaxChunks + b;
-    if ((int)(ld_acquire_sys(f) - e) < 0) {
-      const uint64_t t0 = globaltimer_ns();
-      while ((int)(ld_acquire_sys(f) - e) < 0) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          record_status(p.status, kDevTimeoutPeer);
-          s_ok = 0;
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  if (s_ok) {
+  // 2. wait for every rank's flag of this chunk, then sum it
+  if (ar_wait(p, par, b, e)) {
     const float* mine = p.data[p.rank] + (long long)par * p.P * p.n_max;
     for (long long v = v0 + threadIdx.x; v < v1; v += kArThreads) {
       const long long i = v * kArVec;
@@ -157,13 +184,43 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p,
       }
     }
   }
-  if (threadIdx.x == 0) {
-    __threadfence();  // this CTA's read of the epoch precedes its count
-    if (atomicAdd(p.epochs + 1, 1u) == gridDim.x - 1) {
-      p.epochs[1] = 0u;
-      *(volatile unsigned int*)p.epochs = e;
+  ar_finish(p, e);
+}
+
+// Greedy token across vocabulary shards: keys[m] is this rank's best logit of
+// row m as (order-preserving fp16 value << 32) | (2^32 - 1 - local index); the
+// global index is index_base + local index, so the global key is keys[m] -
+// index_base.  One CTA stores its M global keys (as pairs of floats) into
+// slot (parity, rank) of every rank's buffer, flags chunk 0, waits for every
+// rank, and takes the largest key of each row: the largest logit, and among
+// equal logits the lowest global index.
+__global__ void __launch_bounds__(kArThreads) argmax_exchange_kernel(const ArParams p,
+                                                                     const unsigned long long* __restrict__ keys,
+                                                                     unsigned long long index_base,
+                                                                     uint32_t* __restrict__ idx, int M) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const unsigned int e = ar_epoch(p);
+  const int par = (int)(e & 1u);
+  for (int m = threadIdx.x; m < M; m += kArThreads) {
+    const unsigned long long k = keys[m] - index_base;
+    for (int r = 0; r < p.P; ++r)
+      reinterpret_cast<unsigned long long*>(p.data[r] + ((long long)par * p.P + p.rank) * p.n_max)[m] = k;
+  }
+  __syncthreads();
+  ar_flag(p, par, 0, e);
+  if (ar_wait(p, par, 0, e)) {
+    const float* mine = p.data[p.rank] + (long long)par * p.P * p.n_max;
+    for (int m = threadIdx.x; m < M; m += kArThreads) {
+      unsigned long long best = 0ull;
+      for (int r = 0; r < p.P; ++r) {
+        const unsigned long long k = __ldcg(reinterpret_cast<const unsigned long long*>(mine + (long long)r * p.n_max) + m);
+        best = k > best ? k : best;
+      }
+      idx[m] = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull);
     }
   }
+  ar_finish(p, e);
 }
 
 }  // namespace
@@ -174,9 +231,8 @@ size_t allreduce_buffer_bytes(int P, int64_t n_max) {
 
 size_t allreduce_epoch_bytes() { return 2 * sizeof(unsigned int); }
 
-cudaError_t launch_allreduce(const ArComm& c, const float* partial, void* out, bool out_f32, bool vec, int64_t n,
-                             int sm_count, cudaStream_t stream) {
-  if (n == 0) return cudaSuccess;
+namespace {
+ArParams ar_params(const ArComm& c) {
   ArParams p{};
   for (int r = 0; r < c.P; ++r) {
     p.data[r] = reinterpret_cast<float*>(static_cast<uint8_t*>(c.peer_bufs[r]) + kArFlagBytes);
@@ -187,6 +243,30 @@ cudaError_t launch_allreduce(const ArComm& c, const float* partial, void* out, b
   p.P = c.P;
   p.rank = c.rank;
   p.n_max = c.n_max;
+  return p;
+}
+}  // namespace
+
+cudaError_t launch_argmax_exchange(const ArComm& c, const unsigned long long* keys, int64_t index_base,
+                                   uint32_t* idx, int64_t M, cudaStream_t stream) {
+  if (M == 0) return cudaSuccess;
+  const ArParams p = ar_params(c);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kArThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, argmax_exchange_kernel, p, keys, (unsigned long long)index_base, idx, (int)M);
+}
+
+cudaError_t launch_allreduce(const ArComm& c, const float* partial, void* out, bool out_f32, bool vec, int64_t n,
+                             int sm_count, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const ArParams p = ar_params(c);
   // chunks of about 2 float4 per thread; the grid depends on n only, so
   // every rank splits a call identically
   const long long nv = (n + kArVec - 1) / kArVec;

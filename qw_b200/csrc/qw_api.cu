@@ -602,43 +602,57 @@ int qw_quantized_matmul_chain(const qw_qmm_op* ops, int n_ops, int group_size, i
   return QW_OK;
 }
 
-int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_array* scales,
-                               const qw_array* biases, int group_size, int bits, const char* mode, qw_array* logits,
-                               qw_array* idx, void* stream_v) {
-  set_error("");
+namespace {
+
+// Checks of a greedy-token call (qw_quantized_matmul_argmax and
+// qw_allreduce_argmax); on QW_OK fills the weight shape, the rows M of x and
+// x's row step.
+int check_argmax_call(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
+                      int group_size, int bits, const char* mode, const qw_array* logits, const qw_array* idx,
+                      WeightDims* d, int64_t* M_out, int64_t* x_ld) {
   int rc;
   if ((rc = check_quant_params(mode, biases != nullptr, group_size, bits))) return rc;
-  WeightDims d;
-  if ((rc = check_weights(w, scales, biases, group_size, bits, &d))) return rc;
-  int64_t x_ld = 0;
-  if ((rc = check_x_rows(x, d.K, &x_ld)) || (rc = check_array(idx, "idx"))) return rc;
+  if ((rc = check_weights(w, scales, biases, group_size, bits, d))) return rc;
+  if ((rc = check_x_rows(x, d->K, x_ld)) || (rc = check_array(idx, "idx"))) return rc;
   if (logits && (rc = check_array(logits, "logits"))) return rc;
   if (x->dtype != QW_F16) return fail(QW_EUNSUPPORTED, std::string("x must be float16, got ") + dtype_name(x->dtype));
-  if (x->shape[x->ndim - 1] != d.K)
+  if (x->shape[x->ndim - 1] != d->K)
     return fail(QW_EINVAL, "x's last dimension " + std::to_string(x->shape[x->ndim - 1]) +
-                               " does not match the weights' input width " + std::to_string(d.K));
-  const int64_t M = numel(x) / (d.K ? d.K : 1);
+                               " does not match the weights' input width " + std::to_string(d->K));
+  const int64_t M = numel(x) / (d->K ? d->K : 1);
   if (idx->dtype != QW_U32 || numel(idx) != M)
     return fail(QW_EINVAL, "idx must be uint32 with one element per row of x");
-  if (logits && (logits->dtype != QW_F16 || logits->shape[logits->ndim - 1] != d.N || numel(logits) != M * d.N))
+  if (logits && (logits->dtype != QW_F16 || logits->shape[logits->ndim - 1] != d->N || numel(logits) != M * d->N))
     return fail(QW_EINVAL, "logits must be float16 [..., N] with the leading dimensions of x");
-  if (M == 0) return QW_OK;
-  if (d.N == 0) return fail(QW_EINVAL, "argmax over an empty row (N == 0)");
-  if (!aligned(x->data, 16) || !aligned(idx->data, 4) || (logits && !aligned(logits->data, 2)))
+  if (M > 0 && d->N == 0) return fail(QW_EINVAL, "argmax over an empty row (N == 0)");
+  if (M > 0 && (!aligned(x->data, 16) || !aligned(idx->data, 4) || (logits && !aligned(logits->data, 2))))
     return fail(QW_EINVAL, "x must be 16-byte aligned, idx 4-byte aligned");
-  int dev = 0;
-  cudaError_t ce = cudaGetDevice(&dev);
-  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  if (M > 16 || !skinny_config(group_size, bits))
+    if (!logits) return fail(QW_EINVAL, "a logits buffer is required when x has more than 16 rows");
+  *M_out = M;
+  return QW_OK;
+}
+
+// keys[m] = (order-preserving fp16 logit << 32) | (2^32 - 1 - row) of the best
+// row of each of the M rows of x: folded into the decode kernel's epilogue for
+// up to 16 rows (logits written only if given), else the matmul into logits
+// and a row reduction.
+int argmax_keys(const qw_array* x, const qw_array* w, const qw_array* scales, const qw_array* biases,
+                int group_size, int bits, const char* mode, qw_array* logits, const WeightDims& d, int64_t M,
+                int64_t x_ld, unsigned long long* keys, void* stream_v) {
   cudaStream_t stream = as_stream(stream_v);
-  std::string err;
+  cudaError_t ce;
+  int rc;
   if (M > 16 || !skinny_config(group_size, bits)) {
-    if (!logits)
-      return fail(QW_EINVAL, "a logits buffer is required when x has more than 16 rows");
     if ((rc = run_qmm(x, w, scales, biases, 1, group_size, bits, mode, logits, stream_v))) return rc;
-    ce = launch_argmax_rows(logits->data, M, d.N, (uint32_t*)idx->data, stream);
+    ce = launch_argmax_rows_keys(logits->data, M, d.N, keys, stream);
     return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "argmax launch");
   }
+  int dev = 0;
+  ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
   DeviceRes* res = nullptr;
+  std::string err;
   if (!device_res(dev, &res, &err)) return fail(QW_ENOMEM, err);
   SkinnyArgs sa{};
   sa.x = x->data;
@@ -657,13 +671,46 @@ int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_ar
   sa.bits = bits;
   Scratch sc;
   if (!scratch_for(dev, stream, skinny_scratch_bytes(sa, dev), &sc, &err)) return fail(QW_ENOMEM, err);
-  // keys in the first 256 bytes of the scratch (the chains' tallies use the first 96)
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(sc.base) + 128);
   ce = cudaMemsetAsync(keys, 0, (size_t)M * sizeof(unsigned long long), stream);
   if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync");
   sa.amax = keys;
   ce = launch_skinny(sa, sc, stream, pdl_enabled(), &err);
   if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "skinny launch") : fail(QW_ECUDA, err);
+  return QW_OK;
+}
+
+}  // namespace
+
+int qw_quantized_matmul_argmax(const qw_array* x, const qw_array* w, const qw_array* scales,
+                               const qw_array* biases, int group_size, int bits, const char* mode, qw_array* logits,
+                               qw_array* idx, void* stream_v) {
+  set_error("");
+  WeightDims d;
+  int64_t M = 0, x_ld = 0;
+  int rc = check_argmax_call(x, w, scales, biases, group_size, bits, mode, logits, idx, &d, &M, &x_ld);
+  if (rc != QW_OK) return rc;
+  if (M == 0) return QW_OK;
+  cudaStream_t stream = as_stream(stream_v);
+  cudaError_t ce;
+  if (M > 16 || !skinny_config(group_size, bits)) {
+    if ((rc = run_qmm(x, w, scales, biases, 1, group_size, bits, mode, logits, stream_v))) return rc;
+    ce = launch_argmax_rows(logits->data, M, d.N, (uint32_t*)idx->data, stream);
+    return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "argmax launch");
+  }
+  int dev = 0;
+  ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  std::string err;
+  Scratch sc;
+  SkinnyArgs probe{};
+  probe.M = M;
+  probe.N = d.N;
+  probe.K = d.K;
+  if (!scratch_for(dev, stream, skinny_scratch_bytes(probe, dev), &sc, &err)) return fail(QW_ENOMEM, err);
+  // keys in the first 256 bytes of the scratch (the chains' tallies use the first 96)
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(sc.base) + 128);
+  if ((rc = argmax_keys(x, w, scales, biases, group_size, bits, mode, logits, d, M, x_ld, keys, stream_v)))
+    return rc;
   ce = launch_argmax_finalize(keys, (uint32_t*)idx->data, M, stream);
   return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "argmax launch");
 }
@@ -815,6 +862,7 @@ struct qw_allreduce {
   void* own = nullptr;                 // this rank's shared buffer (cudaMalloc)
   bool opened[kArMaxRanks] = {};       // peer buffers mapped through IPC
   int sm_count = 0;
+  unsigned long long* keys = nullptr;  // greedy-token keys of this rank's shard, n_max / 2 rows
 };
 
 int qw_allreduce_init(int world, int rank, int64_t max_elems, qw_allreduce** out, unsigned char* handle) {
@@ -840,7 +888,8 @@ int qw_allreduce_init(int world, int rank, int64_t max_elems, qw_allreduce** out
   const size_t bytes = allreduce_buffer_bytes(world, c->comm.n_max);
   if ((ce = cudaMalloc(&c->own, bytes)) != cudaSuccess || (ce = cudaMemset(c->own, 0, bytes)) != cudaSuccess ||
       (ce = cudaMalloc(reinterpret_cast<void**>(&c->comm.counters), allreduce_epoch_bytes())) != cudaSuccess ||
-      (ce = cudaMemset(c->comm.counters, 0, allreduce_epoch_bytes())) != cudaSuccess) {
+      (ce = cudaMemset(c->comm.counters, 0, allreduce_epoch_bytes())) != cudaSuccess ||
+      (ce = cudaMalloc(reinterpret_cast<void**>(&c->keys), (size_t)(c->comm.n_max / 2 + 1) * 8)) != cudaSuccess) {
     cudaGetLastError();
     qw_allreduce_destroy(c);
     return cuda_fail(ce, "allreduce buffer allocation");
@@ -897,6 +946,33 @@ int qw_allreduce_sum(qw_allreduce* c, const qw_array* partial, qw_array* y, void
   return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "allreduce launch");
 }
 
+int qw_allreduce_argmax(qw_allreduce* c, const qw_array* x, const qw_array* w, const qw_array* scales,
+                        const qw_array* biases, int group_size, int bits, const char* mode, int64_t index_base,
+                        qw_array* logits, qw_array* idx, void* stream) {
+  set_error("");
+  if (!c) return fail(QW_EINVAL, "comm is null");
+  WeightDims d;
+  int64_t M = 0, x_ld = 0;
+  int rc = check_argmax_call(x, w, scales, biases, group_size, bits, mode, logits, idx, &d, &M, &x_ld);
+  if (rc != QW_OK) return rc;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != c->device)
+    return fail(QW_EINVAL, "the current device is not the communicator's (device " + std::to_string(c->device) + ")");
+  for (int r = 0; r < c->comm.P; ++r)
+    if (!c->comm.peer_bufs[r]) return fail(QW_EINVAL, "rank " + std::to_string(r) + " is not connected");
+  if (index_base < 0 || index_base + d.N > (int64_t)0xFFFFFFFF)
+    return fail(QW_EINVAL, "the shard's rows [index_base, index_base + N) must lie below 2^32 - 1");
+  if (2 * M > c->comm.n_max)
+    return fail(QW_EINVAL, std::to_string(M) + " rows exceed the communicator's " +
+                               std::to_string(c->comm.n_max / 2) + " (max_elems / 2)");
+  if (M == 0) return QW_OK;  // nothing is launched, on every rank alike
+  if ((rc = argmax_keys(x, w, scales, biases, group_size, bits, mode, logits, d, M, x_ld, c->keys, stream)))
+    return rc;
+  const cudaError_t ce = launch_argmax_exchange(c->comm, c->keys, index_base, (uint32_t*)idx->data, M,
+                                                as_stream(stream));
+  return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "argmax exchange launch");
+}
+
 int qw_allreduce_destroy(qw_allreduce* c) {
   set_error("");
   if (!c) return QW_OK;
@@ -909,6 +985,7 @@ int qw_allreduce_destroy(qw_allreduce* c) {
     if (c->opened[r]) cudaIpcCloseMemHandle(c->comm.peer_bufs[r]);
   if (c->own) cudaFree(c->own);
   if (c->comm.counters) cudaFree(c->comm.counters);
+  if (c->keys) cudaFree(c->keys);
   cudaGetLastError();
   cudaSetDevice(prev);
   delete c;

@@ -110,6 +110,9 @@ bool prefill_available();
 cudaError_t launch_argmax_finalize(const unsigned long long* keys, uint32_t* idx, int64_t M, cudaStream_t stream);
 // Greedy token of each row of fp16 logits [M][N] (lowest index among equal maxima).
 cudaError_t launch_argmax_rows(const void* logits, int64_t M, int64_t N, uint32_t* idx, cudaStream_t stream);
+// The same as keys: (order-preserving fp16 value << 32) | (2^32 - 1 - index).
+cudaError_t launch_argmax_rows_keys(const void* logits, int64_t M, int64_t N, unsigned long long* keys,
+                                    cudaStream_t stream);
 
 // The k largest fp16 values of each of M rows of N (rows ld apart), sorted
 // descending, lower index first among equal values; 1 <= k <= topk_max_k(), k < N.
@@ -129,6 +132,11 @@ struct ArComm {
 };
 size_t allreduce_buffer_bytes(int P, int64_t n_max);
 size_t allreduce_epoch_bytes();
+// idx[m] = the global greedy token of row m over every rank's vocabulary
+// shard: keys[m] is this rank's best (value, local index) key and its shard
+// starts at row index_base; 2 M <= n_max.
+cudaError_t launch_argmax_exchange(const ArComm& c, const unsigned long long* keys, int64_t index_base,
+                                   uint32_t* idx, int64_t M, cudaStream_t stream);
 // y[i] = sum over ranks of partial[i], rounded to fp16 (or kept fp32); n <= n_max.
 cudaError_t launch_allreduce(const ArComm& c, const float* partial, void* out, bool out_f32, bool vec, int64_t n,
                              int sm_count, cudaStream_t stream);

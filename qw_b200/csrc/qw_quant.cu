@@ -205,7 +205,8 @@ __global__ void argmax_finalize_kernel(const unsigned long long* keys, uint32_t*
 
 // One block per row; keys as in the skinny kernel's epilogue (order-preserving
 // value above, complemented index below), reduced over the block.
-__global__ void argmax_rows_kernel(const __half* logits, int64_t N, uint32_t* idx) {
+// With `keys` set the block writes its row's best key instead of the index.
+__global__ void argmax_rows_kernel(const __half* logits, int64_t N, uint32_t* idx, unsigned long long* keys) {
   const __half* row = logits + (size_t)blockIdx.x * N;
   unsigned long long best = 0ull;
   for (int64_t n = threadIdx.x; n < N; n += blockDim.x) {
@@ -225,7 +226,8 @@ __global__ void argmax_rows_kernel(const __half* logits, int64_t N, uint32_t* id
   if (threadIdx.x == 0) {
     unsigned long long v = 0ull;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v = warp_best[w] > v ? warp_best[w] : v;
-    idx[blockIdx.x] = 0xFFFFFFFFu - (uint32_t)(v & 0xFFFFFFFFull);
+    if (keys) keys[blockIdx.x] = v;
+    else idx[blockIdx.x] = 0xFFFFFFFFu - (uint32_t)(v & 0xFFFFFFFFull);
   }
 }
 
@@ -239,7 +241,14 @@ cudaError_t launch_argmax_finalize(const unsigned long long* keys, uint32_t* idx
 
 cudaError_t launch_argmax_rows(const void* logits, int64_t M, int64_t N, uint32_t* idx, cudaStream_t stream) {
   if (M <= 0) return cudaSuccess;
-  argmax_rows_kernel<<<(unsigned)M, 512, 0, stream>>>(reinterpret_cast<const __half*>(logits), N, idx);
+  argmax_rows_kernel<<<(unsigned)M, 512, 0, stream>>>(reinterpret_cast<const __half*>(logits), N, idx, nullptr);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_rows_keys(const void* logits, int64_t M, int64_t N, unsigned long long* keys,
+                                    cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  argmax_rows_kernel<<<(unsigned)M, 512, 0, stream>>>(reinterpret_cast<const __half*>(logits), N, nullptr, keys);
   return cudaGetLastError();
 }
 

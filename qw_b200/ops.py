@@ -84,18 +84,23 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
 
 def quantized_matmul_argmax(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: Optional[torch.Tensor],
                             group_size: int = 64, bits: int = 4, mode: str = "affine",
-                            logits: Optional[torch.Tensor] = None) -> torch.Tensor:
+                            logits: Optional[torch.Tensor] = None,
+                            idx: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Greedy token per row of x: argmax over the fp16 logits x @ dequantize(w).T
     (project_logits then argmax_last_axis, qwen3_5.rs:1038, lib.rs:2055).
     Returns uint32 indices as int64 (torch has no uint32 arithmetic); pass
-    ``logits`` to also receive the fp16 logits (required above 16 rows)."""
+    ``logits`` to also receive the fp16 logits (required above 16 rows).
+    With ``idx`` (int32 [M], e.g. a buffer of a captured CUDA graph) the
+    indices are written there as the ABI's uint32 and ``idx`` is returned."""
     M = x.numel() // x.shape[-1]
-    idx = torch.empty(M, dtype=torch.int32, device=x.device)
+    out = idx if idx is not None else torch.empty(M, dtype=torch.int32, device=x.device)
     L = _lib.load()
-    ia = _arr(idx)  # int32 storage, passed as the uint32 ids the ABI returns
+    ia = _arr(out)  # int32 storage, passed as the uint32 ids the ABI returns
     _lib.check(L.qw_quantized_matmul_argmax(_arr(x), _arr(w), _arr(scales), _arr(biases), group_size, bits,
                                             _mode(mode), _arr(logits), ia, _stream(x)))
-    return idx.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    if idx is not None:
+        return idx
+    return out.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
 
 
 def topk(logits: torch.Tensor, k: int, values: bool = True):

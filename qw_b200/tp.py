@@ -159,6 +159,66 @@ class LinearStack:
         return self.matmul(h, self.lm_head, False)
 
 
+# ---------------------------------------------------------------- greedy token
+# A row's best logit as one integer key: the fp16 value made order-preserving
+# (its float32 bits, sign-folded) above, 2^32 - 1 - (global index) below, so
+# the largest key is the largest logit and, among equal logits, the lowest
+# global index -- the rule of argmax_last_axis (lib.rs:2055) over the whole
+# vocabulary.  The library's decode-kernel epilogue and qw_allreduce_argmax
+# use the same key; the helpers below are its host-side statement (for the
+# NCCL exchange and the CPU tests).
+_SIGN64 = 1 << 63
+
+
+def greedy_keys(logits, index_base: int = 0):
+    """uint64 key of the best logit of each row of fp16 logits [..., N]
+    whose first column is vocabulary row index_base (numpy)."""
+    import numpy as np
+    a = np.asarray(logits, dtype=np.float16)
+    N = a.shape[-1]
+    b = a.reshape(-1, N).astype(np.float32).view(np.uint32).astype(np.uint64)
+    ordered = np.where(b & 0x80000000, (~b) & 0xFFFFFFFF, b | 0x80000000)
+    low = np.uint64(0xFFFFFFFF) - (np.uint64(index_base) + np.arange(N, dtype=np.uint64))
+    return ((ordered << np.uint64(32)) | low[None, :]).max(axis=1).reshape(a.shape[:-1])
+
+
+def key_index(keys):
+    """Global index held in greedy keys (numpy uint64 or torch int64 of
+    signed_keys)."""
+    if hasattr(keys, "new_empty"):  # torch: signed keys
+        return (0xFFFFFFFF - (keys & 0xFFFFFFFF)).to(keys.dtype)
+    import numpy as np
+    return (np.uint64(0xFFFFFFFF) - (np.asarray(keys, np.uint64) & np.uint64(0xFFFFFFFF))).astype(np.int64)
+
+
+def signed_keys(keys):
+    """uint64 keys as int64 that compare the same way (for an int64 MAX
+    all-reduce, which NCCL and gloo provide)."""
+    import numpy as np
+    return (np.asarray(keys, np.uint64) ^ np.uint64(_SIGN64)).view(np.int64)
+
+
+def greedy_keys_torch(logits, index_base: int = 0):
+    """signed_keys(greedy_keys(...)) of torch fp16 logits [..., N], on their device."""
+    import torch
+    N = logits.shape[-1]
+    b = logits.reshape(-1, N).float().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    ordered = torch.where((b & 0x80000000) != 0, (~b) & 0xFFFFFFFF, b | 0x80000000)
+    low = 0xFFFFFFFF - (index_base + torch.arange(N, device=logits.device, dtype=torch.int64))
+    # bit 63 flipped before the signed max: signed order = the keys' unsigned order
+    k = (((ordered << 32) | low) ^ (-_SIGN64)).max(dim=1).values
+    return k.reshape(logits.shape[:-1])
+
+
+def exchange_greedy_keys(keys_signed, group=None):
+    """The global greedy token of each row from every rank's signed keys: an
+    int64 MAX all-reduce over `group` (torch.distributed, any backend), then
+    the index."""
+    import torch.distributed as dist
+    dist.all_reduce(keys_signed, op=dist.ReduceOp.MAX, group=group)
+    return key_index(keys_signed)
+
+
 def gate_up_halves(w):
     """(gate, up) triples of a rank's gate_up shard (rows: gate plane, then up)."""
     n = w[0].shape[0] // 2
@@ -218,6 +278,23 @@ class PeerAllreduce:
         self.world, self.rank, self.max_elems = world, rank, int(max_elems)
         self._group = group
         self._device = torch.cuda.current_device()
+
+    def argmax(self, x, w, index_base: int, idx=None, logits=None, group_size: int = 64, bits: int = 4,
+               mode: str = "affine"):
+        """Global greedy token of each row of x over the ranks' vocabulary
+        shards (qw_allreduce_argmax): this rank's shard w = (wq, scales,
+        biases) holds vocabulary rows [index_base, index_base + N).  Returns
+        int64 [M] indices, the same on every rank."""
+        import torch
+
+        from .ops import _arr, _mode, _stream
+        M = x.numel() // x.shape[-1]
+        if idx is None:
+            idx = torch.empty(M, dtype=torch.int32, device=x.device)
+        self._lib.check(self._lib.load().qw_allreduce_argmax(
+            self._comm, _arr(x), _arr(w[0]), _arr(w[1]), _arr(w[2]), group_size, bits, _mode(mode),
+            int(index_base), _arr(logits), _arr(idx), _stream(x)))
+        return idx
 
     def __call__(self, partial, out):
         """out (fp16 or fp32) = sum over ranks of partial (fp32, same numel)."""

@@ -162,3 +162,101 @@ def test_tp_stack_matches_oracle(world, mode):
         assert rel_err(full, single) <= TOL * np.sqrt(n_ops), (world, M)
         ref = ref_stack.forward(x[:M]).astype(np.float32)
         assert rel_err(full, ref) <= TOL * np.sqrt(n_ops), (world, M)
+
+
+ARGMAX_VOCAB, ARGMAX_K = 32768, 512  # one 512-wide chunk: every row's logit is one CTA's, whatever the shard
+
+
+def _argmax_rank(rank, world, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    import torch.distributed as dist
+    import qw_b200
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        lm = tp.StackDims(hidden=ARGMAX_K, vocab=ARGMAX_VOCAB).lm_head()
+        full_np = oracle.quantize(synth.weight_fp16(lm.N, lm.K, seed=4, layer=99, tid=lm.tid))
+        full = tuple(torch.from_numpy(np.ascontiguousarray(a).view(np.int32) if a.dtype == np.uint32 else a).to(dev)
+                     for a in full_np)
+        n = lm.N // world
+        mine = tuple(t[rank * n:(rank + 1) * n].contiguous() for t in full)
+        ar = tp.PeerAllreduce(64)
+        x_all = torch.from_numpy(synth.activations(20, lm.K, seed=8)).to(dev)
+        for M in (1, 4, 16, 20):
+            x = x_all[:M].contiguous()
+            logits = torch.empty(M, n, dtype=torch.float16, device=dev) if M > 16 else None
+            idx = ar.argmax(x, mine, rank * n, logits=logits)
+            full_logits = torch.empty(M, lm.N, dtype=torch.float16, device=dev) if M > 16 else None
+            one = qw_b200.quantized_matmul_argmax(x, *full, logits=full_logits)
+            torch.cuda.synchronize()
+            out_q.put((rank, M, "ok", ((idx.to(torch.int64) & 0xFFFFFFFF).cpu().numpy(), one.cpu().numpy())))
+        # replayed from a CUDA graph: the exchange's epoch advances on the device
+        x = x_all[:1].contiguous()
+        idx = torch.empty(1, dtype=torch.int32, device=dev)
+        s = torch.cuda.Stream(dev)
+        with torch.cuda.stream(s):
+            ar.argmax(x, mine, rank * n, idx=idx)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            ar.argmax(x, mine, rank * n, idx=idx)
+        replays = []
+        for i in range(3):
+            x.copy_(x_all[i + 1:i + 2])
+            torch.cuda.synchronize()
+            with torch.cuda.stream(s):
+                g.replay()
+            s.synchronize()
+            replays.append(((idx.to(torch.int64) & 0xFFFFFFFF).cpu().numpy(),
+                            qw_b200.quantized_matmul_argmax(x, *full).cpu().numpy()))
+        del g
+        out_q.put((rank, -2, "ok", replays))
+        status = qw_b200.device_status(rank, clear=False)
+        ar.close()
+        out_q.put((rank, -3, "ok", status))
+    except Exception as e:  # noqa: BLE001
+        out_q.put((rank, -1, "error", repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_tp_greedy_token_matches_one_gpu(world):
+    """qw_allreduce_argmax over vocabulary shards returns, on every rank, the
+    greedy token one GPU holding the whole LM head returns (fused decode
+    epilogue for M <= 16, logits and a row reduction for M = 20), also when
+    replayed from a CUDA graph.  World size 1 runs the exchange kernel
+    against itself, on a one-GPU machine."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_argmax_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    deadline = time.time() + 300
+    while len(got) < 6 * world and time.time() < deadline:
+        try:
+            r, M, status, payload = q.get(timeout=10)
+        except Exception:
+            continue
+        assert status == "ok", payload
+        got[(r, M)] = payload
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert len(got) == 6 * world
+    for r in range(world):
+        for M in (1, 4, 16, 20):
+            idx, one = got[(r, M)]
+            np.testing.assert_array_equal(idx, one, err_msg=f"rank {r} M={M}")
+        for idx, one in got[(r, -2)]:
+            np.testing.assert_array_equal(idx, one)
+        assert got[(r, -3)] == 0

@@ -76,7 +76,13 @@ def _rank_main(rank, world, port, x, out_q, fail_rank):
         stack = tp.LinearStack(mine, lm_mine, world, rank, _oracle_mm, allreduce,
                                lambda a: a.astype(np.float16), DIMS, swiglu=_oracle_swiglu)
         t0 = time.time()
-        out_q.put((rank, "ok", stack.forward(x), time.time() - t0))
+        logits = stack.forward(x)
+        # greedy token over the vocabulary shards: this rank's keys, then the
+        # int64 MAX exchange (the host-side statement of qw_allreduce_argmax)
+        base = tp.column_shard_rows(DIMS.lm_head(), world, rank, DIMS)[0][0]
+        keys = torch.from_numpy(np.ascontiguousarray(tp.signed_keys(tp.greedy_keys(logits, base))))
+        token = tp.exchange_greedy_keys(keys).numpy()
+        out_q.put((rank, "ok", (logits, token), time.time() - t0))
     except Exception as e:  # noqa: BLE001 - reported to the parent
         out_q.put((rank, "error", repr(e), 0.0))
     finally:
@@ -140,13 +146,76 @@ def test_two_rank_stack_matches_unsharded():
     x, results = _run(2)
     assert set(results) == {0, 1}, results
     ref = _reference_logits(x)
-    shards = []
+    shards, tokens = [], []
     for r in range(2):
         status, payload = results[r]
         assert status == "ok", payload
-        shards.append(payload)
+        shards.append(payload[0])
+        tokens.append(payload[1])
     full = tp.gather_columns(shards, DIMS.lm_head(), DIMS)
     assert rel_err(full.astype(np.float32), ref.astype(np.float32)) <= 1e-2
+    # both ranks hold the greedy token of the whole vocabulary
+    want = oracle.topk(full, 1)[0][:, 0]
+    for t in tokens:
+        np.testing.assert_array_equal(t, want)
+
+
+def _greedy_rank(rank, world, port, logits, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        n = logits.shape[1] // world
+        keys = tp.greedy_keys(logits[:, rank * n:(rank + 1) * n], rank * n)
+        token = tp.exchange_greedy_keys(torch.from_numpy(np.ascontiguousarray(tp.signed_keys(keys))))
+        out_q.put((rank, "ok", token.numpy()))
+    except Exception as e:  # noqa: BLE001
+        out_q.put((rank, "error", repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_greedy_token_exchange_ties_and_signs(world):
+    """The (value, index) key exchange over gloo: equal maxima in different
+    shards go to the lower global index, +0 outranks -0, an all-negative row
+    and a row whose maximum sits in the last shard.  Every rank gets the
+    argmax of the whole row."""
+    rng = np.random.default_rng(3)
+    N = 256 * world
+    lg = (rng.standard_normal((6, N)) * 3).astype(np.float16)
+    lg[0, 5] = lg[0, N - 7] = np.float16(30)           # tie across the first and last shard
+    lg[1, :] = np.float16(0)
+    lg[1, 3] = np.float16(-0.0)                          # index 0 holds +0: the answer
+    lg[2, :] = -np.abs(lg[2, :]) - np.float16(1)          # all negative
+    lg[3, N - 1] = np.float16(60)                        # the very last column
+    lg[4, 256] = lg[4, 257] = np.float16(40)             # tie inside one shard
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_greedy_rank, args=(r, world, port, lg, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    deadline = time.time() + 120
+    while len(got) < world and time.time() < deadline:
+        try:
+            r, status, payload = q.get(timeout=5)
+            assert status == "ok", payload
+            got[r] = payload
+        except Exception as e:  # noqa: BLE001
+            if isinstance(e, AssertionError):
+                raise
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    want = oracle.topk(lg, 1)[0][:, 0]
+    assert list(want[:5]) == [5, 0, int(np.argmax(lg[2])), N - 1, 256]
+    assert len(got) == world
+    for r in range(world):
+        np.testing.assert_array_equal(got[r], want)
 
 
 def test_failed_rank_does_not_hang_its_peer():
