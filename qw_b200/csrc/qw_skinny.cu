@@ -98,8 +98,10 @@ struct SkinnyCfg {
   // One token with 4-bit codes: the 8 groups of a unit are the 8 columns of
   // the MMAs (see the consumer), with B fragments masked per group.
   static constexpr bool COLS = MT == 1 && BITS == 4;
-  static constexpr int WST = BITS == 8 ? (MT == 1 ? 3 : 2) : (MT == 1 ? 5 : (MT <= 8 ? 4 : 3));
-  static constexpr int SST = BITS == 8 ? 2 : (MT == 1 ? (COLS ? 3 : 4) : (MT <= 8 ? 3 : 2));
+  // Ring depths: the one-token 4-bit path measured fastest with two weight
+  // stages (13.4 us at 17408 x 5120 against 13.8 to 14.2 with 3 to 5).
+  static constexpr int WST = BITS == 8 ? (MT == 1 ? 3 : 2) : (MT == 1 ? (COLS ? 2 : 5) : (MT <= 8 ? 4 : 3));
+  static constexpr int SST = BITS == 8 ? 2 : (MT == 1 ? (COLS ? 2 : 4) : (MT <= 8 ? 3 : 2));
   static constexpr int W_BOX = BN * 128;
   static constexpr int SB_BYTES = BN * 16;
   static constexpr int W_STAGE = NBOX * W_BOX + 2 * SB_BYTES;  // W boxes, scales, biases
@@ -803,10 +805,17 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
         // are summed when the row's segment ends.
         const uint32_t stu = smem_u32(sring + sslot * Cfg::S_STAGE);
         float dA[4], dB[4];
+        auto b_addr = [&](int g) { return stu + Cfg::OFF_BF + g * 1024 + lane * 16; };
+        // The next unit's fragments are copied in the unit's second half
+        // (groups 0-7 of the next unit while groups 4-7 of this one compute),
+        // so its data has the longest time to land before the wait.
+        auto roll = [&](int g) {
+          ldmatrix_x4(wb_next + (g / 4) * Cfg::W_BOX + lm_off[g % 4], A[g][0], A[g][1], A[g][2], A[g][3]);
+        };
 #pragma unroll
         for (int gi = 0; gi < 8; ++gi) {
-          const uint4 b0 = lds128(stu + Cfg::OFF_BF + gi * 1024 + lane * 16);
-          const uint4 b1 = lds128(stu + Cfg::OFF_BF + gi * 1024 + 512 + lane * 16);
+          const uint4 b0 = lds128(b_addr(gi));
+          const uint4 b1 = lds128(b_addr(gi) + 512);
           uint32_t e[4][4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -815,11 +824,6 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
             e[1][i] = lop3_and_or(A[gi][i], 0x00F000F0u);
             e[2][i] = lop3_and_or(w8, 0x000F000Fu);
             e[3][i] = lop3_and_or(w8, 0x00F000F0u);
-          }
-          if (has_next) {
-            if (gi == 0 && !*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull))
-              *abort_flag = 1;
-            ldmatrix_x4(wb_next + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
           }
           if (gi == 0) {
             mma_16816_zc(dA, e[0][0], e[0][1], e[0][2], e[0][3], b0.x, b0.y);
@@ -830,6 +834,13 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           }
           mma_16816(dA, e[2][0], e[2][1], e[2][2], e[2][3], b1.x, b1.y);
           mma_16816(dB, e[3][0], e[3][1], e[3][2], e[3][3], b1.z, b1.w);
+          if (has_next && gi >= 4) {
+            // A[0..gi] are expanded: groups 2 (gi - 4) and 2 (gi - 4) + 1 are free
+            if (gi == 4 && !*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull))
+              *abort_flag = 1;
+            roll(2 * (gi - 4));
+            roll(2 * (gi - 4) + 1);
+          }
         }
         // (X, Z) of groups 2 s4 and 2 s4 + 1
         const float4 v = *reinterpret_cast<const float4*>(sring + sslot * Cfg::S_STAGE + Cfg::OFF_XZ + s4 * 16);
