@@ -110,9 +110,11 @@ struct SkinnyCfg {
   static constexpr int X_BYTES = kGroupsPerStage * MT * 128;
   static constexpr int BF_TOK = MT;
   // COLS: per group a 1 KB block [b0 | b1][32 lanes][16 bytes], zero except
-  // the four lanes of MMA column (= group) gi; otherwise per (group, token,
-  // lane column) 32 bytes.
-  static constexpr int BF_BYTES = COLS ? kGroupsPerStage * 1024 : kGroupsPerStage * BF_TOK * 4 * 32;
+  // the four lanes of MMA column (= group) gi.  Otherwise per group
+  // [b0 | b1][token][lane column][16 bytes]: a warp's lanes read consecutive
+  // 16-byte words, free of bank conflicts.
+  static constexpr int BF_GROUP = BF_TOK * 4 * 32;
+  static constexpr int BF_BYTES = COLS ? kGroupsPerStage * 1024 : kGroupsPerStage * BF_GROUP;
   static constexpr int XZ_COLS = 8 * NT;
   static constexpr int XZ_BYTES = kGroupsPerStage * XZ_COLS * 8;
   static constexpr int OFF_X = 0;  // within a small stage (1024-aligned for SW128)
@@ -571,9 +573,9 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               xb[q] = lds64(xbase + line * 128 + (((2 * q + (s >> 1)) ^ (line & 7)) << 4) + 8 * (s & 1));
-            const uint32_t fa = bf + ((gi * Cfg::BF_TOK + n) * 4 + s) * 32;
+            const uint32_t fa = bf + gi * Cfg::BF_GROUP + (n * 4 + s) * 16;
             sts128(fa, make_uint4(xb[0].x, xb[0].y, xb[1].x, xb[1].y));
-            sts128(fa + 16, make_uint4(xb[2].x, xb[2].y, xb[3].x, xb[3].y));
+            sts128(fa + Cfg::BF_GROUP / 2, make_uint4(xb[2].x, xb[2].y, xb[3].x, xb[3].y));
             float xs = 0.f;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -604,9 +606,9 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
             sts128(bf + gi * 1024 + (gi * 4 + s) * 16, f0);
             sts128(bf + gi * 1024 + 512 + (gi * 4 + s) * 16, f1);
           } else {
-            const uint32_t fa = bf + ((gi * Cfg::BF_TOK + n) * 4 + s) * 32;
+            const uint32_t fa = bf + gi * Cfg::BF_GROUP + (n * 4 + s) * 16;
             sts128(fa, f0);
-            sts128(fa + 16, f1);
+            sts128(fa + Cfg::BF_GROUP / 2, f1);
           }
           // sums over even and odd k of the 16 x values this lane holds
           float xe = 0.f, xo = 0.f;
@@ -707,7 +709,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
 #pragma unroll
   for (int tt = 0; tt < NT; ++tt) {
     const int tok = (tt * 8 + r) < p.M ? (tt * 8 + r) : (p.M - 1);
-    bf_off[tt] = Cfg::OFF_BF + (tok * 4 + s4) * 32;
+    bf_off[tt] = Cfg::OFF_BF + (tok * 4 + s4) * 16;
   }
   const uint32_t xz_off = Cfg::OFF_XZ + 2 * s4 * 8;
   const uint32_t wring_u = smem_u32(wring);
@@ -857,9 +859,9 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           uint4 b0[NT], b1[NT];
 #pragma unroll
           for (int tt = 0; tt < NT; ++tt) {
-            const uint4* fb = reinterpret_cast<const uint4*>(stp + bf_off[tt] + gi * (Cfg::BF_TOK * 4 * 32));
-            b0[tt] = fb[0];
-            b1[tt] = fb[1];
+            const uint8_t* fb = stp + bf_off[tt] + gi * Cfg::BF_GROUP;
+            b0[tt] = *reinterpret_cast<const uint4*>(fb);
+            b1[tt] = *reinterpret_cast<const uint4*>(fb + Cfg::BF_GROUP / 2);
           }
           // expanded A registers: e[jj][i] for word i
           uint32_t e[4][4];
