@@ -250,3 +250,25 @@ def test_split_tiles_across_changing_grids():
             x = synth.activations(1, K, seed=rep)
             _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
             assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL, (N, K, rep)
+
+
+@pytest.mark.parametrize("P", [4, 8])
+@pytest.mark.parametrize("M", [1, 16])
+def test_tensor_parallel_shard_shapes(P, M):
+    """Every shard shape of the BASELINE stack at TP=4 and TP=8 on one GPU:
+    column shards (q|k|v, gate|up halves, lm_head) and row shards (o, down)
+    whose K (1536/768, 4352/2176) is not a multiple of 512, so the decode
+    kernel stages their scales and biases with plain loads.  Row shards
+    return fp32 partial sums, as the exchange consumes them."""
+    from qw_b200 import tp
+    for lin in synth.layer_linears() + [synth.LM_HEAD]:
+        N, K = tp.shard_shape(lin, P)
+        if lin.name == "gate_up":
+            N //= 2  # one of the two halves the fused SwiGLU reads
+        wq, s, b = quantized(N, K, seed=N + K + P)
+        x = synth.activations(M, K, seed=P)
+        _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+        if lin.row_parallel:
+            assert rel_err(run_qmm(x, wq, s, b, out_dtype=torch.float32), y_ref) <= 1e-3, (lin.name, N, K)
+        else:
+            assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL, (lin.name, N, K)
