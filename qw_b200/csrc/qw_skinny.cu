@@ -95,13 +95,18 @@ struct SkinnyCfg {
   // boxes of 128 bytes) or 512 bytes of 8-bit codes (four boxes), so 8-bit
   // stages are twice as large and the rings shallower.
   static constexpr int NBOX = BITS == 8 ? 4 : 2;
-  // One token with 4-bit codes: the 8 groups of a unit are the 8 columns of
-  // the MMAs (see the consumer), with B fragments masked per group.
-  static constexpr bool COLS = MT == 1 && BITS == 4;
+  // Column scheme (4-bit codes, one to four tokens): the MMA's 8 columns hold
+  // (token, group) pairs, TPC token columns for each of GPC groups, so one
+  // accumulator chain collects GPC groups and the fold runs once per GPC
+  // groups.  Group gi's B fragment is x in the lanes of its columns and zero
+  // in the others.  One token: 8 groups a chain; up to four: 2 groups a chain.
+  static constexpr bool COLS = BITS == 4 && (MT == 1 || MT == 4);
+  static constexpr int TPC = MT == 4 ? 4 : 1;  // token columns per group
+  static constexpr int GPC = 8 / TPC;          // groups per accumulator chain
   // Ring depths: the one-token 4-bit path measured fastest with two weight
   // stages (13.4 us at 17408 x 5120 against 13.8 to 14.2 with 3 to 5).
-  static constexpr int WST = BITS == 8 ? (MT == 1 ? 3 : 2) : (MT == 1 ? (COLS ? 2 : 5) : (MT <= 8 ? 4 : 3));
-  static constexpr int SST = BITS == 8 ? 2 : (MT == 1 ? (COLS ? 2 : 4) : (MT <= 8 ? 3 : 2));
+  static constexpr int WST = BITS == 8 ? (MT == 1 ? 3 : 2) : (COLS ? 2 : (MT <= 8 ? 4 : 3));
+  static constexpr int SST = BITS == 8 ? 2 : (COLS ? 2 : (MT <= 8 ? 3 : 2));
   static constexpr int W_BOX = BN * 128;
   static constexpr int SB_BYTES = BN * 16;
   static constexpr int W_STAGE = NBOX * W_BOX + 2 * SB_BYTES;  // W boxes, scales, biases
@@ -110,12 +115,13 @@ struct SkinnyCfg {
   static constexpr int X_BYTES = kGroupsPerStage * MT * 128;
   static constexpr int BF_TOK = MT;
   // COLS: per group a 1 KB block [b0 | b1][32 lanes][16 bytes], zero except
-  // the four lanes of MMA column (= group) gi.  Otherwise per group
+  // the lanes of group gi's columns.  Otherwise per group
   // [b0 | b1][token][lane column][16 bytes]: a warp's lanes read consecutive
   // 16-byte words, free of bank conflicts.
   static constexpr int BF_GROUP = BF_TOK * 4 * 32;
   static constexpr int BF_BYTES = COLS ? kGroupsPerStage * 1024 : kGroupsPerStage * BF_GROUP;
-  static constexpr int XZ_COLS = 8 * NT;
+  // (X, Z) per group and token column: with COLS entry (gi, t) is at gi * TPC + t
+  static constexpr int XZ_COLS = COLS ? TPC : 8 * NT;
   static constexpr int XZ_BYTES = kGroupsPerStage * XZ_COLS * 8;
   static constexpr int OFF_X = 0;  // within a small stage (1024-aligned for SW128)
   static constexpr int OFF_BF = align1k(X_BYTES);
@@ -538,7 +544,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
                make_uint4(0u, 0u, 0u, 0u));
     }
     // (X, Z) of token columns >= M stay zero for the whole launch.
-    for (int e = h * 32 + lane; !Cfg::COLS && e < SST * kGroupsPerStage * Cfg::XZ_COLS; e += Cfg::HW * 32) {
+    for (int e = h * 32 + lane; e < SST * kGroupsPerStage * Cfg::XZ_COLS; e += Cfg::HW * 32) {
       const int slot = e / (kGroupsPerStage * Cfg::XZ_COLS);
       const int col = e % Cfg::XZ_COLS;
       if (col >= p.M) {
@@ -602,9 +608,11 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           f1.z = hmul2_rn(prmt(xv0.y, xv0.w, 0x7632), 0x2C002C00u);
           f1.w = hmul2_rn(prmt(xv1.y, xv1.w, 0x7632), 0x2C002C00u);
           if (Cfg::COLS) {
-            // lane (row gi, column s) of group gi's block: MMA column gi
-            sts128(bf + gi * 1024 + (gi * 4 + s) * 16, f0);
-            sts128(bf + gi * 1024 + 512 + (gi * 4 + s) * 16, f1);
+            // lane (row n + TPC (gi % GPC), column s) of group gi's block:
+            // token n's column among the group's
+            const int lr = n + Cfg::TPC * (gi % Cfg::GPC);
+            sts128(bf + gi * 1024 + (lr * 4 + s) * 16, f0);
+            sts128(bf + gi * 1024 + 512 + (lr * 4 + s) * 16, f1);
           } else {
             const uint32_t fa = bf + gi * Cfg::BF_GROUP + (n * 4 + s) * 16;
             sts128(fa, f0);
@@ -624,7 +632,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           xe += __shfl_xor_sync(0xffffffffu, xe, 2);
           xo += __shfl_xor_sync(0xffffffffu, xo, 2);
           if (s == 0)
-            sts_f32x2(xz + (Cfg::COLS ? gi : gi * Cfg::XZ_COLS + n) * 8, xe + xo, 1024.f * xe + 64.f * xo);
+            sts_f32x2(xz + (gi * Cfg::XZ_COLS + n) * 8, xe + xo, 1024.f * xe + 64.f * xo);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&ready[slot]);
@@ -752,9 +760,9 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
     }
   };
   // Scales and biases of this lane's rows: all 8 groups (16 bytes a row), or
-  // with COLS the two groups 2 s4, 2 s4 + 1 of its MMA columns (4 bytes).
+  // for one token the two groups 2 s4, 2 s4 + 1 of its MMA columns (4 bytes).
   auto load_sb = [&](uint32_t wb) {
-    if (Cfg::COLS) {
+    if (Cfg::COLS && Cfg::TPC == 1) {
       sv_lo.x = lds32(wb + Cfg::OFF_WS + sb_off + 4 * s4);
       sv_hi.x = lds32(wb + Cfg::OFF_WS + sb_off + kSbHi + 4 * s4);
       bv_lo.x = lds32(wb + Cfg::OFF_WB + sb_off + 4 * s4);
@@ -798,13 +806,14 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
       // compute against the unit's x fragments, refilling A with the next unit
       if (!*abort_flag && !mbar_wait(&ready[sslot], sphase, p.status, kDevTimeoutFull)) *abort_flag = 1;
       if constexpr (Cfg::COLS) {
-        // One token, 4-bit codes.  MMA column n of a unit is its group n:
-        // group gi's B block is x's fragment in the lanes of column gi and zero
-        // in the others, so one accumulator pair collects all 8 groups, each in
-        // its own column (d = 1024 X_even + 64 X_odd + sum_k x_k q_k of that
-        // group), and the fold runs once per unit: lane (r, s4) folds groups
-        // 2 s4 and 2 s4 + 1 of rows r and r + 8, and the four lanes of a row
-        // are summed when the row's segment ends.
+        // 4-bit codes, one to four tokens.  MMA column c of group gi is token
+        // c % TPC of group gi - gi % GPC + c / TPC: group gi's B block is x's
+        // fragment in the lanes of its TPC columns and zero in the others, so
+        // one accumulator pair collects GPC groups, each in its own columns
+        // (d = 1024 X_even + 64 X_odd + sum_k x_k q_k of that group and
+        // token), and the fold runs once per GPC groups.  Lane (r, s4) folds
+        // columns 2 s4 and 2 s4 + 1 of rows r and r + 8; the lanes of a row
+        // that hold the same tokens are summed when the row's segment ends.
         const uint32_t stu = smem_u32(sring + sslot * Cfg::S_STAGE);
         float dA[4], dB[4];
         auto b_addr = [&](int g) { return stu + Cfg::OFF_BF + g * 1024 + lane * 16; };
@@ -813,6 +822,31 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
         // so its data has the longest time to land before the wait.
         auto roll = [&](int g) {
           ldmatrix_x4(wb_next + (g / 4) * Cfg::W_BOX + lm_off[g % 4], A[g][0], A[g][1], A[g][2], A[g][3]);
+        };
+        auto word = [](const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; };
+        // fold of the chain ending at group block q: y += s (d - Z) + b X
+        auto fold = [&](int q) {
+          // (X, Z) of this lane's two columns: entries 8 q + 2 s4 and 8 q + 2 s4 + 1
+          const float4 v =
+              *reinterpret_cast<const float4*>(sring + sslot * Cfg::S_STAGE + Cfg::OFF_XZ + (q * 8 + 2 * s4) * 8);
+          if constexpr (Cfg::TPC == 1) {
+            // one token: the columns are groups 2 s4 and 2 s4 + 1
+            acc[0][0] = fmaf(half_lo(sv_lo.x), (dA[0] + dB[0]) - v.y, fmaf(half_lo(bv_lo.x), v.x, acc[0][0]));
+            acc[0][0] = fmaf(half_hi(sv_lo.x), (dA[1] + dB[1]) - v.w, fmaf(half_hi(bv_lo.x), v.z, acc[0][0]));
+            acc[0][2] = fmaf(half_lo(sv_hi.x), (dA[2] + dB[2]) - v.y, fmaf(half_lo(bv_hi.x), v.x, acc[0][2]));
+            acc[0][2] = fmaf(half_hi(sv_hi.x), (dA[3] + dB[3]) - v.w, fmaf(half_hi(bv_hi.x), v.z, acc[0][2]));
+          } else {
+            // both columns belong to group GPC q + s4 / 2 (word q of the row's scales)
+            const bool hi = (s4 & 2) != 0;
+            const float s_r = hi ? half_hi(word(sv_lo, q)) : half_lo(word(sv_lo, q));
+            const float s_r8 = hi ? half_hi(word(sv_hi, q)) : half_lo(word(sv_hi, q));
+            const float b_r = hi ? half_hi(word(bv_lo, q)) : half_lo(word(bv_lo, q));
+            const float b_r8 = hi ? half_hi(word(bv_hi, q)) : half_lo(word(bv_hi, q));
+            acc[0][0] = fmaf(s_r, (dA[0] + dB[0]) - v.y, fmaf(b_r, v.x, acc[0][0]));
+            acc[0][1] = fmaf(s_r, (dA[1] + dB[1]) - v.w, fmaf(b_r, v.z, acc[0][1]));
+            acc[0][2] = fmaf(s_r8, (dA[2] + dB[2]) - v.y, fmaf(b_r8, v.x, acc[0][2]));
+            acc[0][3] = fmaf(s_r8, (dA[3] + dB[3]) - v.w, fmaf(b_r8, v.z, acc[0][3]));
+          }
         };
 #pragma unroll
         for (int gi = 0; gi < 8; ++gi) {
@@ -827,7 +861,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
             e[2][i] = lop3_and_or(w8, 0x000F000Fu);
             e[3][i] = lop3_and_or(w8, 0x00F000F0u);
           }
-          if (gi == 0) {
+          if (gi % Cfg::GPC == 0) {
             mma_16816_zc(dA, e[0][0], e[0][1], e[0][2], e[0][3], b0.x, b0.y);
             mma_16816_zc(dB, e[1][0], e[1][1], e[1][2], e[1][3], b0.z, b0.w);
           } else {
@@ -843,13 +877,8 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
             roll(2 * (gi - 4));
             roll(2 * (gi - 4) + 1);
           }
+          if (gi % Cfg::GPC == Cfg::GPC - 1) fold(gi / Cfg::GPC);
         }
-        // (X, Z) of groups 2 s4 and 2 s4 + 1
-        const float4 v = *reinterpret_cast<const float4*>(sring + sslot * Cfg::S_STAGE + Cfg::OFF_XZ + s4 * 16);
-        acc[0][0] = fmaf(half_lo(sv_lo.x), (dA[0] + dB[0]) - v.y, fmaf(half_lo(bv_lo.x), v.x, acc[0][0]));
-        acc[0][0] = fmaf(half_hi(sv_lo.x), (dA[1] + dB[1]) - v.w, fmaf(half_hi(bv_lo.x), v.z, acc[0][0]));
-        acc[0][2] = fmaf(half_lo(sv_hi.x), (dA[2] + dB[2]) - v.y, fmaf(half_lo(bv_hi.x), v.x, acc[0][2]));
-        acc[0][2] = fmaf(half_hi(sv_hi.x), (dA[3] + dB[3]) - v.w, fmaf(half_hi(bv_hi.x), v.z, acc[0][2]));
       } else {
         const uint8_t* stp = sring + sslot * Cfg::S_STAGE;
         const uint32_t svl[4] = {sv_lo.x, sv_lo.y, sv_lo.z, sv_lo.w}, svh[4] = {sv_hi.x, sv_hi.y, sv_hi.z, sv_hi.w};
@@ -950,11 +979,17 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
       }
       if (!seg_end) continue;
       if constexpr (Cfg::COLS) {
-        // a row's groups were folded in its four lanes: every lane gets the sum
+        // a row's groups were folded in the lanes that hold the same tokens:
+        // every one of them gets the sum
+        if constexpr (Cfg::TPC == 1) {
 #pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          acc[0][e] += __shfl_xor_sync(0xffffffffu, acc[0][e], 1);
-          acc[0][e] += __shfl_xor_sync(0xffffffffu, acc[0][e], 2);
+          for (int e = 0; e < 4; e += 2) {
+            acc[0][e] += __shfl_xor_sync(0xffffffffu, acc[0][e], 1);
+            acc[0][e] += __shfl_xor_sync(0xffffffffu, acc[0][e], 2);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[0][e] += __shfl_xor_sync(0xffffffffu, acc[0][e], 2);
         }
       }
       const bool whole = (seg_begin == 0) && (c == 0);
@@ -1349,6 +1384,7 @@ cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStrea
     return launch_cfg<16, 8>(a, scratch, stream, pdl, err);
   }
   if (a.M == 1) return launch_cfg<1, 4>(a, scratch, stream, pdl, err);
+  if (a.M <= 4) return launch_cfg<4, 4>(a, scratch, stream, pdl, err);
   if (a.M <= 8) return launch_cfg<8, 4>(a, scratch, stream, pdl, err);
   return launch_cfg<16, 4>(a, scratch, stream, pdl, err);
 }

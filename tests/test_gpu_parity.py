@@ -90,7 +90,7 @@ def test_every_small_m(M):
 
 
 @pytest.mark.parametrize("N,K", [(1, 64), (129, 64), (130, 576), (1000, 2048), (17, 4160), (512, 5120)])
-@pytest.mark.parametrize("M", [1, 5, 16])
+@pytest.mark.parametrize("M", [1, 3, 5, 16])
 def test_ragged_shapes(M, N, K):
     wq, s, b = quantized(N, K, seed=N + K)
     x = synth.activations(M, K, seed=N)
@@ -253,7 +253,7 @@ def test_split_tiles_across_changing_grids():
 
 
 @pytest.mark.parametrize("P", [4, 8])
-@pytest.mark.parametrize("M", [1, 16])
+@pytest.mark.parametrize("M", [1, 4, 16])
 def test_tensor_parallel_shard_shapes(P, M):
     """Every shard shape of the BASELINE stack at TP=4 and TP=8 on one GPU:
     column shards (q|k|v, gate|up halves, lm_head) and row shards (o, down)
