@@ -190,9 +190,18 @@ class StackRunner:
         # the step's result: the greedy token of every row over the whole vocabulary
         self.token = torch.empty(M, dtype=torch.int32, device=dev)
         self.vocab_base = (torch.distributed.get_rank(group) if P > 1 else 0) * lm[0].shape[0]
-        # per layer 4 matmuls; lm_head + argmax: the fused epilogue's finalize
-        # (1 GPU) or the peer exchange kernel (tensor-parallel)
-        self.launches_per_step = 4 * len(ws) + 2
+        # this library's kernels per step: per layer 4 matmuls (and under
+        # tensor parallelism with the peer exchange 2 allreduce kernels); then
+        # lm_head with the greedy token: the fused epilogue and its finalize
+        # (1 GPU), the matmul and the peer exchange kernel, or the matmul alone
+        # (NCCL: the keys and the all-reduce are torch's and NCCL's kernels)
+        L = len(ws)
+        if P == 1:
+            self.launches_per_step = 4 * L + 2
+        elif ar is not None:
+            self.launches_per_step = 6 * L + 2
+        else:
+            self.launches_per_step = 4 * L + 1
         if self.chain:
             self._build_segments()
 
@@ -227,8 +236,10 @@ class StackRunner:
         flush()
         acts.append(("token", None))
         self.actions = acts
-        self.launches_per_step = sum((len(a[1]) + 23) // 24 if a[0] == "chain" else 1
-                                     for a in acts if a[0] != "reduce") + 1
+        self.launches_per_step = (sum((len(a[1]) + 23) // 24 for a in acts if a[0] == "chain")
+                                  + sum(1 for a in acts if a[0] == "swiglu")
+                                  + sum(1 for a in acts if a[0] == "reduce" and self.ar is not None)
+                                  + (2 if self.P == 1 or self.ar is not None else 1))
 
     def _mm(self, x, w, out):
         self.qw.quantized_matmul(x, w[0], w[1], w[2], out=out)
