@@ -68,7 +68,6 @@ namespace {
 
 constexpr int kGroup = 64;
 constexpr int kGroupsPerStage = 8;
-constexpr int kChunkK = kGroup * kGroupsPerStage;  // 512
 constexpr size_t kMaxCounters = kSkinnyMaxCounters;  // row tiles per launch (N <= 8M rows)
 constexpr size_t kCounterBytes = kSkinnyCounterBytes;
 
@@ -94,7 +93,6 @@ struct SkinnyCfg {
   // A stage's 512-wide chunk is 256 bytes of 4-bit codes per row (two SW128
   // boxes of 128 bytes) or 512 bytes of 8-bit codes (four boxes), so 8-bit
   // stages are twice as large and the rings shallower.
-  static constexpr int NBOX = BITS == 8 ? 4 : 2;
   // Column scheme (4-bit codes, one to four tokens): the MMA's 8 columns hold
   // (token, group) pairs, TPC token columns for each of GPC groups, so one
   // accumulator chain collects GPC groups and the fold runs once per GPC
@@ -103,26 +101,33 @@ struct SkinnyCfg {
   static constexpr bool COLS = BITS == 4 && (MT == 1 || MT == 4);
   static constexpr int TPC = MT == 4 ? 4 : 1;  // token columns per group
   static constexpr int GPC = 8 / TPC;          // groups per accumulator chain
+#ifndef QWV_GPS1
+#define QWV_GPS1 8
+#endif
+  // 64-wide groups per unit (per pipeline stage): the unit is 128 rows x 64 GPS k
+  static constexpr int GPS = (COLS && TPC == 1) ? QWV_GPS1 : 8;
+  static constexpr int CK = kGroup * GPS;       // k per unit
+  static constexpr int NBOX = GPS * kGroup * BITS / 8 / 128;  // 128-byte TMA boxes of a unit's codes
   // Ring depths: the one-token 4-bit path measured fastest with two weight
   // stages (13.4 us at 17408 x 5120 against 13.8 to 14.2 with 3 to 5).
   static constexpr int WST = BITS == 8 ? (MT == 1 ? 3 : 2) : (COLS ? 2 : (MT <= 8 ? 4 : 3));
   static constexpr int SST = BITS == 8 ? 2 : (COLS ? 2 : (MT <= 8 ? 3 : 2));
   static constexpr int W_BOX = BN * 128;
-  static constexpr int SB_BYTES = BN * 16;
+  static constexpr int SB_BYTES = BN * 2 * GPS;
   static constexpr int W_STAGE = NBOX * W_BOX + 2 * SB_BYTES;  // W boxes, scales, biases
   static constexpr int OFF_WS = NBOX * W_BOX;
   static constexpr int OFF_WB = OFF_WS + SB_BYTES;
-  static constexpr int X_BYTES = kGroupsPerStage * MT * 128;
+  static constexpr int X_BYTES = GPS * MT * 128;
   static constexpr int BF_TOK = MT;
   // COLS: per group a 1 KB block [b0 | b1][32 lanes][16 bytes], zero except
   // the lanes of group gi's columns.  Otherwise per group
   // [b0 | b1][token][lane column][16 bytes]: a warp's lanes read consecutive
   // 16-byte words, free of bank conflicts.
   static constexpr int BF_GROUP = BF_TOK * 4 * 32;
-  static constexpr int BF_BYTES = COLS ? kGroupsPerStage * 1024 : kGroupsPerStage * BF_GROUP;
+  static constexpr int BF_BYTES = COLS ? GPS * 1024 : GPS * BF_GROUP;
   // (X, Z) per group and token column: with COLS entry (gi, t) is at gi * TPC + t
   static constexpr int XZ_COLS = COLS ? TPC : 8 * NT;
-  static constexpr int XZ_BYTES = kGroupsPerStage * XZ_COLS * 8;
+  static constexpr int XZ_BYTES = GPS * XZ_COLS * 8;
   static constexpr int OFF_X = 0;  // within a small stage (1024-aligned for SW128)
   static constexpr int OFF_BF = align1k(X_BYTES);
   static constexpr int OFF_XZ = OFF_BF + BF_BYTES;
@@ -367,8 +372,8 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
             for (int bx = 0; bx < Cfg::NBOX; ++bx)
               tma_load_2d_hint(st + bx * Cfg::W_BOX, &op.tm_w, &wfull[slot], cx + bx * 128, t * Cfg::BN, pol_w);
             if (op.sb_tma) {
-              tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
-              tma_load_2d_hint(st + Cfg::OFF_WB, &op.tm_b, &wfull[slot], c * kGroupsPerStage, t * Cfg::BN, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * Cfg::GPS, t * Cfg::BN, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WB, &op.tm_b, &wfull[slot], c * Cfg::GPS, t * Cfg::BN, pol_w);
             }
           } else {
             // 64 gate rows, then the same 64 up rows (boxes of 64 rows; the
@@ -382,100 +387,103 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
               tma_load_2d_hint(st + bx * Cfg::W_BOX + H * 128, &op.tm_w2, &wfull[slot], cx + bx * 128, r0, pol_w);
             }
             if (op.sb_tma) {
-              tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
-              tma_load_2d_hint(st + Cfg::OFF_WS + H * 16, &op.tm_s2, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
-              tma_load_2d_hint(st + Cfg::OFF_WB, &op.tm_b, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
-              tma_load_2d_hint(st + Cfg::OFF_WB + H * 16, &op.tm_b2, &wfull[slot], c * kGroupsPerStage, r0, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WS, &op.tm_s, &wfull[slot], c * Cfg::GPS, r0, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WS + H * 2 * Cfg::GPS, &op.tm_s2, &wfull[slot], c * Cfg::GPS, r0, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WB, &op.tm_b, &wfull[slot], c * Cfg::GPS, r0, pol_w);
+              tma_load_2d_hint(st + Cfg::OFF_WB + H * 2 * Cfg::GPS, &op.tm_b2, &wfull[slot], c * Cfg::GPS, r0, pol_w);
             }
           }
         }
         if (!op.sb_tma) {
           // Scales/biases staged with plain loads (rows not 16-byte strided
-          // when K % 512 != 0; groups of 128, whose scale serves both 64-wide
-          // groups it covers), zero beyond the matrix edge, after the weight
-          // boxes are on their way; the stage's arrival follows them.  The
-          // stage holds 8 halves (16 bytes) per row.
-          __half* ss = reinterpret_cast<__half*>(st + Cfg::OFF_WS);
-          __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_WB);
-          if (op.gsh == 2 && op.K % kChunkK == 0) {
-            // Groups of 128 with 16-byte strided rows: a chunk holds 4 per
-            // row, one 8-byte load per row each for scales and biases (all in
-            // flight together), each value written for both 64-wide groups.
-            uint2 sv4[Cfg::BN / 32], bv4[Cfg::BN / 32];
+          // when K is not a multiple of the unit's k; groups of 128, whose
+          // scale serves both 64-wide groups it covers), zero beyond the
+          // matrix edge, after the weight boxes are on their way; the stage's
+          // arrival follows them.  The stage holds GPS halves per row, filled
+          // eight groups (16 bytes) at a time.
+          for (int sc = 0; sc < Cfg::GPS / kGroupsPerStage; ++sc) {
+            __half* ss = reinterpret_cast<__half*>(st + Cfg::OFF_WS) + sc * kGroupsPerStage;
+            __half* sb = reinterpret_cast<__half*>(st + Cfg::OFF_WB) + sc * kGroupsPerStage;
+            const int g0 = c * Cfg::GPS + sc * kGroupsPerStage;  // first 64-wide group of these eight
+            if (op.gsh == 2 && op.K % Cfg::CK == 0) {
+              // Groups of 128 with 16-byte strided rows: a chunk holds 4 per
+              // row, one 8-byte load per row each for scales and biases (all in
+              // flight together), each value written for both 64-wide groups.
+              uint2 sv4[Cfg::BN / 32], bv4[Cfg::BN / 32];
 #pragma unroll
-            for (int i = 0; i < Cfg::BN / 32; ++i) {
-              const int r = lane + 32 * i;
-              const bool up = op.swiglu && r >= Cfg::BN / 2;
-              const int row = op.swiglu ? t * (Cfg::BN / 2) + (r % (Cfg::BN / 2)) : t * Cfg::BN + r;
-              sv4[i] = bv4[i] = make_uint2(0u, 0u);
-              if (row < op.N) {
-                const size_t off = (size_t)row * Gs + (size_t)c * (kGroupsPerStage / 2);
-                sv4[i] = *reinterpret_cast<const uint2*>((up ? op.scales2 : op.scales) + off);
-                bv4[i] = *reinterpret_cast<const uint2*>((up ? op.biases2 : op.biases) + off);
+              for (int i = 0; i < Cfg::BN / 32; ++i) {
+                const int r = lane + 32 * i;
+                const bool up = op.swiglu && r >= Cfg::BN / 2;
+                const int row = op.swiglu ? t * (Cfg::BN / 2) + (r % (Cfg::BN / 2)) : t * Cfg::BN + r;
+                sv4[i] = bv4[i] = make_uint2(0u, 0u);
+                if (row < op.N) {
+                  const size_t off = (size_t)row * Gs + (size_t)g0 / 2;
+                  sv4[i] = *reinterpret_cast<const uint2*>((up ? op.scales2 : op.scales) + off);
+                  bv4[i] = *reinterpret_cast<const uint2*>((up ? op.biases2 : op.biases) + off);
+                }
               }
-            }
 #pragma unroll
-            for (int i = 0; i < Cfg::BN / 32; ++i) {
-              const int r = lane + 32 * i;
-              // halves (h0 h1 h2 h3) -> (h0 h0 h1 h1 h2 h2 h3 h3)
-              *reinterpret_cast<uint4*>(ss + r * kGroupsPerStage) =
-                  make_uint4(prmt(sv4[i].x, 0u, 0x1010u), prmt(sv4[i].x, 0u, 0x3232u), prmt(sv4[i].y, 0u, 0x1010u),
-                             prmt(sv4[i].y, 0u, 0x3232u));
-              *reinterpret_cast<uint4*>(sb + r * kGroupsPerStage) =
-                  make_uint4(prmt(bv4[i].x, 0u, 0x1010u), prmt(bv4[i].x, 0u, 0x3232u), prmt(bv4[i].y, 0u, 0x1010u),
-                             prmt(bv4[i].y, 0u, 0x3232u));
-            }
-          } else {
-            // One row per lane and step, the loads of all four steps in flight
-            // together: the eight 64-wide groups of the chunk as two 8-byte
-            // loads when the row allows (groups of 64, 8-byte aligned, not past
-            // the row's end), one 8-byte load of four group-128 values written
-            // twice each, or element by element at a ragged edge.
-            uint32_t sw[Cfg::BN / 32][4], bw[Cfg::BN / 32][4];
-#pragma unroll
-            for (int i = 0; i < Cfg::BN / 32; ++i) {
-              const int r = lane + 32 * i;
-              const bool up = op.swiglu && r >= Cfg::BN / 2;
-              const int row = op.swiglu ? t * (Cfg::BN / 2) + (r % (Cfg::BN / 2)) : t * Cfg::BN + r;
-              const __half* srow = (up ? op.scales2 : op.scales) + (size_t)row * Gs;
-              const __half* brow = (up ? op.biases2 : op.biases) + (size_t)row * Gs;
-              const int g0 = c * kGroupsPerStage;  // first 64-wide group of the chunk
-#pragma unroll
-              for (int q = 0; q < 4; ++q) sw[i][q] = bw[i][q] = 0u;
-              if (row >= op.N) continue;
-              if (op.gsh == 1 && g0 + kGroupsPerStage <= G && (((size_t)row * Gs + g0) & 3) == 0) {
-                const uint2 s0 = *reinterpret_cast<const uint2*>(srow + g0);
-                const uint2 s1 = *reinterpret_cast<const uint2*>(srow + g0 + 4);
-                const uint2 b0 = *reinterpret_cast<const uint2*>(brow + g0);
-                const uint2 b1 = *reinterpret_cast<const uint2*>(brow + g0 + 4);
-                sw[i][0] = s0.x; sw[i][1] = s0.y; sw[i][2] = s1.x; sw[i][3] = s1.y;
-                bw[i][0] = b0.x; bw[i][1] = b0.y; bw[i][2] = b1.x; bw[i][3] = b1.y;
-              } else if (op.gsh == 2 && g0 + kGroupsPerStage <= G && (((size_t)row * Gs + g0 / 2) & 3) == 0) {
-                const uint2 s4 = *reinterpret_cast<const uint2*>(srow + g0 / 2);
-                const uint2 b4 = *reinterpret_cast<const uint2*>(brow + g0 / 2);
+              for (int i = 0; i < Cfg::BN / 32; ++i) {
+                const int r = lane + 32 * i;
                 // halves (h0 h1 h2 h3) -> (h0 h0 h1 h1 h2 h2 h3 h3)
-                sw[i][0] = prmt(s4.x, 0u, 0x1010u); sw[i][1] = prmt(s4.x, 0u, 0x3232u);
-                sw[i][2] = prmt(s4.y, 0u, 0x1010u); sw[i][3] = prmt(s4.y, 0u, 0x3232u);
-                bw[i][0] = prmt(b4.x, 0u, 0x1010u); bw[i][1] = prmt(b4.x, 0u, 0x3232u);
-                bw[i][2] = prmt(b4.y, 0u, 0x1010u); bw[i][3] = prmt(b4.y, 0u, 0x3232u);
-              } else {
+                *reinterpret_cast<uint4*>(ss + r * Cfg::GPS) =
+                    make_uint4(prmt(sv4[i].x, 0u, 0x1010u), prmt(sv4[i].x, 0u, 0x3232u), prmt(sv4[i].y, 0u, 0x1010u),
+                               prmt(sv4[i].y, 0u, 0x3232u));
+                *reinterpret_cast<uint4*>(sb + r * Cfg::GPS) =
+                    make_uint4(prmt(bv4[i].x, 0u, 0x1010u), prmt(bv4[i].x, 0u, 0x3232u), prmt(bv4[i].y, 0u, 0x1010u),
+                               prmt(bv4[i].y, 0u, 0x3232u));
+              }
+            } else {
+              // One row per lane and step, the loads of all four steps in flight
+              // together: the eight 64-wide groups of the chunk as two 8-byte
+              // loads when the row allows (groups of 64, 8-byte aligned, not past
+              // the row's end), one 8-byte load of four group-128 values written
+              // twice each, or element by element at a ragged edge.
+              uint32_t sw[Cfg::BN / 32][4], bw[Cfg::BN / 32][4];
 #pragma unroll
-                for (int g = 0; g < kGroupsPerStage; ++g) {
-                  const int grp = g0 + g;
-                  if (grp < G) {
-                    const uint32_t sv = __half_as_ushort(srow[grp / op.gsh]);
-                    const uint32_t bv = __half_as_ushort(brow[grp / op.gsh]);
-                    sw[i][g / 2] |= sv << (16 * (g & 1));
-                    bw[i][g / 2] |= bv << (16 * (g & 1));
+              for (int i = 0; i < Cfg::BN / 32; ++i) {
+                const int r = lane + 32 * i;
+                const bool up = op.swiglu && r >= Cfg::BN / 2;
+                const int row = op.swiglu ? t * (Cfg::BN / 2) + (r % (Cfg::BN / 2)) : t * Cfg::BN + r;
+                const __half* srow = (up ? op.scales2 : op.scales) + (size_t)row * Gs;
+                const __half* brow = (up ? op.biases2 : op.biases) + (size_t)row * Gs;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) sw[i][q] = bw[i][q] = 0u;
+                if (row >= op.N) continue;
+                if (op.gsh == 1 && g0 + kGroupsPerStage <= G && (((size_t)row * Gs + g0) & 3) == 0) {
+                  const uint2 s0 = *reinterpret_cast<const uint2*>(srow + g0);
+                  const uint2 s1 = *reinterpret_cast<const uint2*>(srow + g0 + 4);
+                  const uint2 b0 = *reinterpret_cast<const uint2*>(brow + g0);
+                  const uint2 b1 = *reinterpret_cast<const uint2*>(brow + g0 + 4);
+                  sw[i][0] = s0.x; sw[i][1] = s0.y; sw[i][2] = s1.x; sw[i][3] = s1.y;
+                  bw[i][0] = b0.x; bw[i][1] = b0.y; bw[i][2] = b1.x; bw[i][3] = b1.y;
+                } else if (op.gsh == 2 && g0 + kGroupsPerStage <= G && (((size_t)row * Gs + g0 / 2) & 3) == 0) {
+                  const uint2 s4 = *reinterpret_cast<const uint2*>(srow + g0 / 2);
+                  const uint2 b4 = *reinterpret_cast<const uint2*>(brow + g0 / 2);
+                  // halves (h0 h1 h2 h3) -> (h0 h0 h1 h1 h2 h2 h3 h3)
+                  sw[i][0] = prmt(s4.x, 0u, 0x1010u); sw[i][1] = prmt(s4.x, 0u, 0x3232u);
+                  sw[i][2] = prmt(s4.y, 0u, 0x1010u); sw[i][3] = prmt(s4.y, 0u, 0x3232u);
+                  bw[i][0] = prmt(b4.x, 0u, 0x1010u); bw[i][1] = prmt(b4.x, 0u, 0x3232u);
+                  bw[i][2] = prmt(b4.y, 0u, 0x1010u); bw[i][3] = prmt(b4.y, 0u, 0x3232u);
+                } else {
+#pragma unroll
+                  for (int g = 0; g < kGroupsPerStage; ++g) {
+                    const int grp = g0 + g;
+                    if (grp < G) {
+                      const uint32_t sv = __half_as_ushort(srow[grp / op.gsh]);
+                      const uint32_t bv = __half_as_ushort(brow[grp / op.gsh]);
+                      sw[i][g / 2] |= sv << (16 * (g & 1));
+                      bw[i][g / 2] |= bv << (16 * (g & 1));
+                    }
                   }
                 }
               }
-            }
 #pragma unroll
-            for (int i = 0; i < Cfg::BN / 32; ++i) {
-              const int r = lane + 32 * i;
-              *reinterpret_cast<uint4*>(ss + r * kGroupsPerStage) = make_uint4(sw[i][0], sw[i][1], sw[i][2], sw[i][3]);
-              *reinterpret_cast<uint4*>(sb + r * kGroupsPerStage) = make_uint4(bw[i][0], bw[i][1], bw[i][2], bw[i][3]);
+              for (int i = 0; i < Cfg::BN / 32; ++i) {
+                const int r = lane + 32 * i;
+                *reinterpret_cast<uint4*>(ss + r * Cfg::GPS) = make_uint4(sw[i][0], sw[i][1], sw[i][2], sw[i][3]);
+                *reinterpret_cast<uint4*>(sb + r * Cfg::GPS) = make_uint4(bw[i][0], bw[i][1], bw[i][2], bw[i][3]);
+              }
             }
           }
           __syncwarp();
@@ -498,7 +506,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
   if (warp == 1) {
     // ------------------------------------------------------- x producer
     if (lane == 0) {
-      const uint32_t x_bytes = kGroupsPerStage * 128 * p.M;
+      const uint32_t x_bytes = Cfg::GPS * 128 * p.M;
       pdl_wait();  // x is the previous kernel's output
       int slot = 0, issued = 0;
       uint32_t phase = 0;
@@ -519,7 +527,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           }
           if (*abort_flag) break;
           mbar_arrive_expect_tx(&sfull[slot], x_bytes);
-          tma_load_3d(sring + slot * Cfg::S_STAGE + Cfg::OFF_X, &op.tm_x, &sfull[slot], 0, 0, c * kGroupsPerStage);
+          tma_load_3d(sring + slot * Cfg::S_STAGE + Cfg::OFF_X, &op.tm_x, &sfull[slot], 0, 0, c * Cfg::GPS);
           if (++slot == SST) {
             slot = 0;
             phase ^= 1u;
@@ -544,11 +552,11 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
                make_uint4(0u, 0u, 0u, 0u));
     }
     // (X, Z) of token columns >= M stay zero for the whole launch.
-    for (int e = h * 32 + lane; e < SST * kGroupsPerStage * Cfg::XZ_COLS; e += Cfg::HW * 32) {
-      const int slot = e / (kGroupsPerStage * Cfg::XZ_COLS);
+    for (int e = h * 32 + lane; e < SST * Cfg::GPS * Cfg::XZ_COLS; e += Cfg::HW * 32) {
+      const int slot = e / (Cfg::GPS * Cfg::XZ_COLS);
       const int col = e % Cfg::XZ_COLS;
       if (col >= p.M) {
-        const int gi = (e / Cfg::XZ_COLS) % kGroupsPerStage;
+        const int gi = (e / Cfg::XZ_COLS) % Cfg::GPS;
         sts_f32x2(smem_u32(sring + slot * Cfg::S_STAGE + Cfg::OFF_XZ) + (gi * Cfg::XZ_COLS + col) * 8, 0.f, 0.f);
       }
     }
@@ -564,7 +572,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
         const uint32_t bf = smem_u32(st + Cfg::OFF_BF);
         const uint32_t xz = smem_u32(st + Cfg::OFF_XZ);
         // task = ((gi * M + n) * 4 + s): lanes 4k..4k+3 share one (group, token)
-        for (int base = h * 32; base < 32 * p.M; base += Cfg::HW * 32) {
+        for (int base = h * 32; base < 4 * Cfg::GPS * p.M; base += Cfg::HW * 32) {
           const int task = base + lane;
           const int s = task & 3;
           const int gn = task >> 2;
@@ -708,8 +716,8 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
 #pragma unroll
   for (int g4 = 0; g4 < 4; ++g4) lm_off[g4] = lm_row * 128 + (((g4 * 2 + (lm_mi >> 1)) ^ lm_sw) << 4);
   // scale/bias rows of MMA rows r and r+8 of this warp, all 8 groups (16 bytes each)
-  const uint32_t sb_off = (wrow + r) * 16;
-  constexpr uint32_t kSbHi = (Cfg::BN / 2) * 16;
+  const uint32_t sb_off = (wrow + r) * 2 * Cfg::GPS;
+  constexpr uint32_t kSbHi = (Cfg::BN / 2) * 2 * Cfg::GPS;
   // B fragments: a lane whose token column is >= M reads token M-1's (a
   // shared-memory broadcast).  MMA output columns depend only on their own B
   // column, so those columns are never mixed into a written result.
@@ -748,7 +756,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
   // computed, and the slot is released once the last group's loads are
   // issued.
   constexpr bool kRoll = BITS == 4 && MT <= 8;
-  uint32_t A[BITS == 8 ? 4 : 8][4];
+  uint32_t A[BITS == 8 ? 4 : Cfg::GPS][4];
   uint4 sv_lo, sv_hi, bv_lo, bv_hi;
   uint32_t wb_cur = 0;  // 8-bit: the slot of the unit being computed
   auto release_wslot = [&]() {
@@ -763,10 +771,17 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
   // for one token the two groups 2 s4, 2 s4 + 1 of its MMA columns (4 bytes).
   auto load_sb = [&](uint32_t wb) {
     if (Cfg::COLS && Cfg::TPC == 1) {
+      // word q (q < GPS / 8) of each: groups 8 q + 2 s4 and 8 q + 2 s4 + 1
       sv_lo.x = lds32(wb + Cfg::OFF_WS + sb_off + 4 * s4);
       sv_hi.x = lds32(wb + Cfg::OFF_WS + sb_off + kSbHi + 4 * s4);
       bv_lo.x = lds32(wb + Cfg::OFF_WB + sb_off + 4 * s4);
       bv_hi.x = lds32(wb + Cfg::OFF_WB + sb_off + kSbHi + 4 * s4);
+      if (Cfg::GPS > 8) {
+        sv_lo.y = lds32(wb + Cfg::OFF_WS + sb_off + 16 + 4 * s4);
+        sv_hi.y = lds32(wb + Cfg::OFF_WS + sb_off + kSbHi + 16 + 4 * s4);
+        bv_lo.y = lds32(wb + Cfg::OFF_WB + sb_off + 16 + 4 * s4);
+        bv_hi.y = lds32(wb + Cfg::OFF_WB + sb_off + kSbHi + 16 + 4 * s4);
+      }
     } else {
       sv_lo = lds128(wb + Cfg::OFF_WS + sb_off);
       sv_hi = lds128(wb + Cfg::OFF_WS + sb_off + kSbHi);
@@ -784,7 +799,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
         ldmatrix_x4(wb + lm_off[li], A[li][0], A[li][1], A[li][2], A[li][3]);
     } else {
 #pragma unroll
-      for (int gi = 0; gi < 8; ++gi)
+      for (int gi = 0; gi < Cfg::GPS; ++gi)
         ldmatrix_x4(wb + (gi / 4) * Cfg::W_BOX + lm_off[gi % 4], A[gi][0], A[gi][1], A[gi][2], A[gi][3]);
     }
     load_sb(wb);
@@ -815,7 +830,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
         // columns 2 s4 and 2 s4 + 1 of rows r and r + 8; the lanes of a row
         // that hold the same tokens are summed when the row's segment ends.
         const uint32_t stu = smem_u32(sring + sslot * Cfg::S_STAGE);
-        float dA[4], dB[4];
+        float dA[4] = {0.f, 0.f, 0.f, 0.f}, dB[4] = {0.f, 0.f, 0.f, 0.f};  // set by each chain's first MMAs
         auto b_addr = [&](int g) { return stu + Cfg::OFF_BF + g * 1024 + lane * 16; };
         // The next unit's fragments are copied in the unit's second half
         // (groups 0-7 of the next unit while groups 4-7 of this one compute),
@@ -830,11 +845,12 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           const float4 v =
               *reinterpret_cast<const float4*>(sring + sslot * Cfg::S_STAGE + Cfg::OFF_XZ + (q * 8 + 2 * s4) * 8);
           if constexpr (Cfg::TPC == 1) {
-            // one token: the columns are groups 2 s4 and 2 s4 + 1
-            acc[0][0] = fmaf(half_lo(sv_lo.x), (dA[0] + dB[0]) - v.y, fmaf(half_lo(bv_lo.x), v.x, acc[0][0]));
-            acc[0][0] = fmaf(half_hi(sv_lo.x), (dA[1] + dB[1]) - v.w, fmaf(half_hi(bv_lo.x), v.z, acc[0][0]));
-            acc[0][2] = fmaf(half_lo(sv_hi.x), (dA[2] + dB[2]) - v.y, fmaf(half_lo(bv_hi.x), v.x, acc[0][2]));
-            acc[0][2] = fmaf(half_hi(sv_hi.x), (dA[3] + dB[3]) - v.w, fmaf(half_hi(bv_hi.x), v.z, acc[0][2]));
+            // one token: the columns are groups 8 q + 2 s4 and 8 q + 2 s4 + 1
+            const uint32_t sl = word(sv_lo, q), sh = word(sv_hi, q), bl = word(bv_lo, q), bh = word(bv_hi, q);
+            acc[0][0] = fmaf(half_lo(sl), (dA[0] + dB[0]) - v.y, fmaf(half_lo(bl), v.x, acc[0][0]));
+            acc[0][0] = fmaf(half_hi(sl), (dA[1] + dB[1]) - v.w, fmaf(half_hi(bl), v.z, acc[0][0]));
+            acc[0][2] = fmaf(half_lo(sh), (dA[2] + dB[2]) - v.y, fmaf(half_lo(bh), v.x, acc[0][2]));
+            acc[0][2] = fmaf(half_hi(sh), (dA[3] + dB[3]) - v.w, fmaf(half_hi(bh), v.z, acc[0][2]));
           } else {
             // both columns belong to group GPC q + s4 / 2 (word q of the row's scales)
             const bool hi = (s4 & 2) != 0;
@@ -849,7 +865,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           }
         };
 #pragma unroll
-        for (int gi = 0; gi < 8; ++gi) {
+        for (int gi = 0; gi < Cfg::GPS; ++gi) {
           const uint4 b0 = lds128(b_addr(gi));
           const uint4 b1 = lds128(b_addr(gi) + 512);
           uint32_t e[4][4];
@@ -870,12 +886,13 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
           }
           mma_16816(dA, e[2][0], e[2][1], e[2][2], e[2][3], b1.x, b1.y);
           mma_16816(dB, e[3][0], e[3][1], e[3][2], e[3][3], b1.z, b1.w);
-          if (has_next && gi >= 4) {
-            // A[0..gi] are expanded: groups 2 (gi - 4) and 2 (gi - 4) + 1 are free
-            if (gi == 4 && !*abort_flag && !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull))
+          if (has_next && gi >= Cfg::GPS / 2) {
+            // A[0..gi] are expanded: groups 2 (gi - GPS/2) and 2 (gi - GPS/2) + 1 are free
+            if (gi == Cfg::GPS / 2 && !*abort_flag &&
+                !mbar_wait(&wfull[wslot], wphase, p.status, kDevTimeoutFull))
               *abort_flag = 1;
-            roll(2 * (gi - 4));
-            roll(2 * (gi - 4) + 1);
+            roll(2 * (gi - Cfg::GPS / 2));
+            roll(2 * (gi - Cfg::GPS / 2) + 1);
           }
           if (gi % Cfg::GPC == Cfg::GPC - 1) fold(gi / Cfg::GPC);
         }
@@ -1169,13 +1186,13 @@ bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
   using Cfg = SkinnyCfg<MT, BITS>;
   op->N = (int)a.N;
   op->K = (int)a.K;
-  op->C = (int)((a.K + kChunkK - 1) / kChunkK);
+  op->C = (int)((a.K + Cfg::CK - 1) / Cfg::CK);
   // a SwiGLU tile holds 64 output rows (64 gate + 64 up weight rows)
   const int tile_rows = a.swiglu ? Cfg::BN / 2 : Cfg::BN;
   op->T = (int)((a.N + tile_rows - 1) / tile_rows);
   op->U = (long long)op->T * op->C;
   op->gsh = a.group_size / kGroup;
-  op->sb_tma = (a.K % kChunkK == 0 && op->gsh == 1) ? 1 : 0;
+  op->sb_tma = (a.K % Cfg::CK == 0 && op->gsh == 1) ? 1 : 0;
   op->y_f32 = a.y_f32 ? 1 : 0;
   op->swiglu = a.swiglu ? 1 : 0;
   op->y = a.y;
@@ -1202,7 +1219,7 @@ bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
     // x viewed as [K/64 groups][M tokens][64 halves]: one box = 8 groups x M tokens
     const uint64_t dims[3] = {(uint64_t)kGroup, (uint64_t)a.M, (uint64_t)(a.K / kGroup)};
     const uint64_t strides[2] = {(uint64_t)(a.x_ld ? a.x_ld : a.K) * 2, (uint64_t)kGroup * 2};
-    const uint32_t box[3] = {(uint32_t)kGroup, (uint32_t)a.M, (uint32_t)kGroupsPerStage};
+    const uint32_t box[3] = {(uint32_t)kGroup, (uint32_t)a.M, (uint32_t)Cfg::GPS};
     if (!encode_tmap_3d(&op->tm_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_128B, err))
       return false;
@@ -1214,7 +1231,7 @@ bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
     CUtensorMap* maps[4] = {&op->tm_s, &op->tm_b, &op->tm_s2, &op->tm_b2};
     for (int i = 0; i < (a.swiglu ? 4 : 2); ++i)
       if (!encode_tmap_2d(maps[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, srcs[i], G64, (uint64_t)a.N, G64 * 2,
-                          kGroupsPerStage, tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE, err))
+                          Cfg::GPS, tile_rows, CU_TENSOR_MAP_SWIZZLE_NONE, err))
         return false;
   }
   return true;
