@@ -18,9 +18,11 @@ Extra keys report the single-matrix qmv (M=1) and verify qmm (M=16) GB/s with
 L2 defeated by rotating weight copies, and the M=16 stack.
 
 With torchrun (N > 1) the stack is tensor-parallel: q/k/v/gate/up/lm_head
-column-sharded, o/down row-sharded, their fp32 partials summed by the
-library's one-shot NVLink peer allreduce with the fp16 cast fused
-(`--tp-allreduce nccl`: ncclAllReduce then a cast, for comparison).  Rank 0 prints
+column-sharded, o/down row-sharded.  With the library's peer exchange (the
+default) o and down are qw_allreduce_matmul calls: each 128-row tile's fp32
+products go to every rank over NVLink from the decode kernel's epilogue and
+are summed there, one launch per projection (`--tp-allreduce nccl`: the
+matmul, ncclAllReduce and a cast, for comparison).  Rank 0 prints
 one JSON line.  `--impl reference` times the reference's CPU path (the oracle
 restatement of MLX's affine quantized_matmul; the reference itself cannot be
 built here) on the host cores.
@@ -190,16 +192,18 @@ class StackRunner:
         # the step's result: the greedy token of every row over the whole vocabulary
         self.token = torch.empty(M, dtype=torch.int32, device=dev)
         self.vocab_base = (torch.distributed.get_rank(group) if P > 1 else 0) * lm[0].shape[0]
-        # this library's kernels per step: per layer 4 matmuls (and under
-        # tensor parallelism with the peer exchange 2 allreduce kernels); then
-        # lm_head with the greedy token: the fused epilogue and its finalize
-        # (1 GPU), the matmul and the peer exchange kernel, or the matmul alone
-        # (NCCL: the keys and the all-reduce are torch's and NCCL's kernels)
+        # this library's kernels per step: per layer 4 matmuls (under tensor
+        # parallelism with the peer exchange, o and down sum over the ranks in
+        # their own epilogue for M <= 16, else an allreduce kernel follows
+        # each); then lm_head with the greedy token: the fused epilogue and its
+        # finalize (1 GPU), the matmul and the peer exchange kernel, or the
+        # matmul alone (NCCL: the keys and the all-reduce are torch's and
+        # NCCL's kernels)
         L = len(ws)
         if P == 1:
             self.launches_per_step = 4 * L + 2
         elif ar is not None:
-            self.launches_per_step = 6 * L + 2
+            self.launches_per_step = (4 if M <= 16 else 6) * L + 2
         else:
             self.launches_per_step = 4 * L + 1
         if self.chain:
@@ -255,9 +259,11 @@ class StackRunner:
     def _rowpar(self, x, w, out16):
         if self.P == 1:
             self._mm(x, w, out16)
-            return
-        self._mm(x, w, self.part)
-        self._reduce(out16)
+        elif self.ar is not None:
+            self.ar.matmul(x, w, out16)  # the sum over ranks fused (qw_allreduce_matmul)
+        else:
+            self._mm(x, w, self.part)
+            self._reduce(out16)
 
     def _swiglu(self, x, l, out):
         self.qw.quantized_matmul_swiglu(x, *self.halves[l], out=out)
@@ -639,7 +645,9 @@ def stack_config(args, world):
     compare the two lines)."""
     return {"workload": f"decode linear stack M=1, {args.layers} layers (qkv/o/gate_up+SwiGLU/down) + lm_head",
             "M": 1, "layers": args.layers, "hidden": synth.HIDDEN, "vocab": synth.VOCAB,
-            "parallelism": (f"tp{world}, {args.tp_allreduce} allreduce" if world > 1 else "single"),
+            "parallelism": ((f"tp{world}, o/down summed over ranks in the matmul epilogue (NVLink peer stores)"
+                             if args.tp_allreduce == "peer" else f"tp{world}, nccl allreduce")
+                            if world > 1 else "single"),
             "l2": "inputs larger than L2 (weights %.2f GB per step)" % (synth.stack_bytes(1, args.layers) / 1e9),
             "graph": "one CUDA graph per step, programmatic dependent launch"}
 

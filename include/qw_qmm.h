@@ -217,6 +217,26 @@ int qw_allreduce_connect(qw_allreduce* comm, const unsigned char* handles);
 int qw_allreduce_sum(qw_allreduce* comm, const qw_array* partial, qw_array* y, void* stream);
 int qw_allreduce_destroy(qw_allreduce* comm);
 
+/* Row-parallel projection of a tensor-parallel layer (the o and down
+ * projections), the matmul and the sum over ranks in one call: y (f16 or
+ * f32 [M, N]) = sum over ranks r of x_r @ dequantize(w_r).T, where this rank
+ * holds x_r [M, K_r] and w_r (scales, biases as in qw_quantized_matmul) [N,
+ * K_r] of a K-split (the same N on every rank).  Every rank receives the
+ * fp32 products summed in rank order and rounded once: bit for bit
+ * qw_quantized_matmul into f32 then qw_allreduce_sum.  For M <= 16 the
+ * exchange runs in the decode kernel's epilogue (each tile stored into every
+ * rank's slot, flagged, waited for and summed by the CTA that finished it):
+ * one launch instead of two.  Larger M runs the matmul into the
+ * communicator's fp32 buffer and then the allreduce kernel.  A collective
+ * call of the same sequence as qw_allreduce_sum (all ranks, same order, same
+ * M and N); M * N <= max_elems.
+ * Replaces: the o and down projections of a layer split over GPUs
+ * (crates/runtime/src/qwen3_next.rs:142-160, 458-487 run them on one
+ * device) followed by ncclAllReduce(float32, sum) and a cast. */
+int qw_allreduce_matmul(qw_allreduce* comm, const qw_array* x, const qw_array* w, const qw_array* scales,
+                        const qw_array* biases, int group_size, int bits, const char* mode, qw_array* y,
+                        void* stream);
+
 /* Greedy token of a vocabulary-sharded LM head under tensor parallelism:
  * this rank holds rows [index_base, index_base + N) of the head (w, scales,
  * biases as in qw_quantized_matmul_argmax) and every rank receives in idx

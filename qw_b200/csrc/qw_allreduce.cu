@@ -2,37 +2,26 @@
 // partials across the GPUs of one node, over NVLink peer memory, with the
 // fp16 rounding of the sum fused (the o and down projections of a
 // tensor-parallel layer: each rank holds y_r = x_r W_r^T over its K-slice,
-// and y = fp16(sum_r y_r)).
+// and y = fp16(sum_r y_r)), and the greedy-token exchange of a vocabulary-
+// sharded LM head.  The buffers, epochs and flags are qw_exchange.cuh's.
 //
-// Each rank owns one buffer that every rank maps (CUDA IPC):
-//   [flags: 2 parities x 8 ranks x 1024 chunks of uint32]
-//   [data:  2 parities x P ranks x n_max floats]
 // CTA b of every rank handles chunk b of the vector (every rank launches the
 // same grid for the same n), so the exchange is per chunk and needs no
 // grid-wide step.  CTA b with epoch e (parity e & 1):
 //   1. stores its chunk of the local partial into slot (parity, rank) of
 //      every rank's buffer (plain stores over NVLink), then, after a CTA
-//      barrier, writes flag (parity, rank, b) = e into every rank's buffer
-//      with system-scope release semantics;
+//      barrier, writes flag (parity, rank, b) = e into every rank's buffer;
 //   2. waits, bounded, until flags (parity, r, b) of its own buffer reach e
-//      for every rank r (acquire), then sums its chunk over the P slots in
-//      rank order (every rank gets identical y) and writes fp16 (or fp32).
-// Every chunk of a call uses the same epoch e (parity e & 1): the call's
-// number, kept in device memory and advanced by the last CTA of the call to
-// finish, so a call captured in a CUDA graph advances on every replay, and
-// every rank runs the same sequence of calls, so the epochs agree without a
-// host exchange.  The grid, and so each chunk's range, depends on n, so
-// calls of different sizes cut the vector differently; a call-wide parity
-// keeps that safe.  Two parities make the reuse safe: a rank stores call
-// e + 2 only after its own call e + 1 completed, which needed every rank's
-// flag of call e + 1 for some chunk, and a rank flags call e + 1 only after
-// its whole call e completed (a call reads its epoch after the previous
-// kernel of the stream completed).
-// No multicast, no NVLS: plain loads and stores to mapped peer memory.  A
-// rank whose peers never flag gives up after the wait bound, records a
-// status and returns (its output is then incomplete).
+//      for every rank r, then sums its chunk over the P slots in rank order
+//      (every rank gets identical y) and writes fp16 (or fp32).
+// The grid, and so each chunk's range, depends on n, so calls of different
+// sizes cut the vector differently; the call-wide epoch and parity keep that
+// safe.  No multicast, no NVLS: plain loads and stores to mapped peer
+// memory.  A rank whose peers never flag gives up after the wait bound,
+// records a status and returns (its output is then incomplete).
 #include <cuda_fp16.h>
 
+#include "qw_exchange.cuh"
 #include "qw_internal.h"
 #include "qw_ptx.cuh"
 
@@ -41,35 +30,15 @@ namespace qw {
 namespace {
 
 constexpr int kArThreads = 256;
-constexpr int kArVec = 4;         // floats per thread per step
-constexpr int kArMaxChunks = 1024;
-constexpr size_t kArFlagBytes = (size_t)2 * kArMaxRanks * kArMaxChunks * sizeof(unsigned int);
+constexpr int kArVec = 4;  // floats per thread per step
 
-struct ArParams {
-  float* data[kArMaxRanks];       // each rank's data area (mapped here)
-  unsigned int* flags[kArMaxRanks];
-  unsigned int* epochs;           // local: [0] the last finished call's epoch, [1] CTAs done in this call
-  unsigned int* status;
-  int P, rank;
-  long long n_max;
-};
-
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// --- the exchange protocol, shared by the sum and the greedy-token kernels.
+// --- the exchange protocol for kernels whose whole CTA takes part.
 // A call's epoch: every CTA reads it before it counts itself done in
 // ar_finish, and the last CTA to count writes the next one, so all CTAs of
 // a call see the same.
 __device__ __forceinline__ unsigned int ar_epoch(const ArParams& p) {
   __shared__ unsigned int s_e;
-  if (threadIdx.x == 0) s_e = *(volatile unsigned int*)p.epochs + 1u;
+  if (threadIdx.x == 0) s_e = ar_next_epoch(p);
   __syncthreads();
   return s_e;
 }
@@ -78,45 +47,22 @@ __device__ __forceinline__ unsigned int ar_epoch(const ArParams& p) {
 __device__ __forceinline__ void ar_flag(const ArParams& p, int par, int b, unsigned int e) {
   if (threadIdx.x < p.P) {
     __threadfence_system();
-    st_release_sys(p.flags[threadIdx.x] + ((size_t)par * kArMaxRanks + p.rank) * kArMaxChunks + b, e);
+    st_release_sys(ar_flag_ptr(p, threadIdx.x, par, p.rank, b), e);
   }
 }
 // Waits, bounded, for every rank's flag of chunk b in this rank's buffer.
-// Once a call has given up (a peer missing), later calls do not wait again:
-// the status stays set until the host clears it, and every call returns at
-// once, so a broken job ends in its own time instead of 2 s per call.
 // Returns (to every thread) whether the chunk's slots may be read.
 __device__ __forceinline__ bool ar_wait(const ArParams& p, int par, int b, unsigned int e) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
-  if (threadIdx.x < p.P && *(volatile unsigned int*)p.status == kDevTimeoutPeer) s_ok = 0;
-  __syncthreads();
-  if (threadIdx.x < p.P && s_ok) {
-    const unsigned int* f = p.flags[p.rank] + ((size_t)par * kArMaxRanks + threadIdx.x) * kArMaxChunks + b;
-    if ((int)(ld_acquire_sys(f) - e) < 0) {
-      const uint64_t t0 = globaltimer_ns();
-      while ((int)(ld_acquire_sys(f) - e) < 0) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          record_status(p.status, kDevTimeoutPeer);
-          s_ok = 0;
-          break;
-        }
-      }
-    }
-  }
+  if (threadIdx.x < p.P && !ar_wait_flag(p, ar_flag_ptr(p, p.rank, par, threadIdx.x, b), e)) s_ok = 0;
   __syncthreads();
   return s_ok != 0;
 }
 // Counts this CTA done; the call's last CTA publishes its epoch.
 __device__ __forceinline__ void ar_finish(const ArParams& p, unsigned int e) {
-  if (threadIdx.x == 0) {
-    __threadfence();  // this CTA's read of the epoch precedes its count
-    if (atomicAdd(p.epochs + 1, 1u) == gridDim.x - 1) {
-      p.epochs[1] = 0u;
-      *(volatile unsigned int*)p.epochs = e;
-    }
-  }
+  if (threadIdx.x == 0) ar_count_done(p, e);
 }
 
 template <bool OUT_F32>
@@ -142,11 +88,11 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p,
     if (vec_ok) {
       const float4 x = *reinterpret_cast<const float4*>(partial + i);
       for (int r = 0; r < p.P; ++r)
-        *reinterpret_cast<float4*>(p.data[r] + ((long long)par * p.P + p.rank) * p.n_max + i) = x;
+        *reinterpret_cast<float4*>(ar_slot(p, r, par, p.rank) + i) = x;
     } else {
       for (int j = 0; j < kArVec && i + j < n; ++j) {
         const float x = partial[i + j];
-        for (int r = 0; r < p.P; ++r) p.data[r][((long long)par * p.P + p.rank) * p.n_max + i + j] = x;
+        for (int r = 0; r < p.P; ++r) ar_slot(p, r, par, p.rank)[i + j] = x;
       }
     }
   }
@@ -155,7 +101,7 @@ __global__ void __launch_bounds__(kArThreads) allreduce_kernel(const ArParams p,
 
   // 2. wait for every rank's flag of this chunk, then sum it
   if (ar_wait(p, par, b, e)) {
-    const float* mine = p.data[p.rank] + (long long)par * p.P * p.n_max;
+    const float* mine = ar_slot(p, p.rank, par, 0);
     for (long long v = v0 + threadIdx.x; v < v1; v += kArThreads) {
       const long long i = v * kArVec;
       if (vec_ok) {
@@ -205,12 +151,12 @@ __global__ void __launch_bounds__(kArThreads) argmax_exchange_kernel(const ArPar
   for (int m = threadIdx.x; m < M; m += kArThreads) {
     const unsigned long long k = keys[m] - index_base;
     for (int r = 0; r < p.P; ++r)
-      reinterpret_cast<unsigned long long*>(p.data[r] + ((long long)par * p.P + p.rank) * p.n_max)[m] = k;
+      reinterpret_cast<unsigned long long*>(ar_slot(p, r, par, p.rank))[m] = k;
   }
   __syncthreads();
   ar_flag(p, par, 0, e);
   if (ar_wait(p, par, 0, e)) {
-    const float* mine = p.data[p.rank] + (long long)par * p.P * p.n_max;
+    const float* mine = ar_slot(p, p.rank, par, 0);
     for (int m = threadIdx.x; m < M; m += kArThreads) {
       unsigned long long best = 0ull;
       for (int r = 0; r < p.P; ++r) {
@@ -231,21 +177,6 @@ size_t allreduce_buffer_bytes(int P, int64_t n_max) {
 
 size_t allreduce_epoch_bytes() { return 2 * sizeof(unsigned int); }
 
-namespace {
-ArParams ar_params(const ArComm& c) {
-  ArParams p{};
-  for (int r = 0; r < c.P; ++r) {
-    p.data[r] = reinterpret_cast<float*>(static_cast<uint8_t*>(c.peer_bufs[r]) + kArFlagBytes);
-    p.flags[r] = static_cast<unsigned int*>(c.peer_bufs[r]);
-  }
-  p.epochs = c.counters;
-  p.status = c.status;
-  p.P = c.P;
-  p.rank = c.rank;
-  p.n_max = c.n_max;
-  return p;
-}
-}  // namespace
 
 cudaError_t launch_argmax_exchange(const ArComm& c, const unsigned long long* keys, int64_t index_base,
                                    uint32_t* idx, int64_t M, cudaStream_t stream) {

@@ -863,6 +863,7 @@ struct qw_allreduce {
   bool opened[kArMaxRanks] = {};       // peer buffers mapped through IPC
   int sm_count = 0;
   unsigned long long* keys = nullptr;  // greedy-token keys of this rank's shard, n_max / 2 rows
+  float* partial = nullptr;            // this rank's fp32 product where the exchange is not fused, n_max
 };
 
 int qw_allreduce_init(int world, int rank, int64_t max_elems, qw_allreduce** out, unsigned char* handle) {
@@ -889,7 +890,8 @@ int qw_allreduce_init(int world, int rank, int64_t max_elems, qw_allreduce** out
   if ((ce = cudaMalloc(&c->own, bytes)) != cudaSuccess || (ce = cudaMemset(c->own, 0, bytes)) != cudaSuccess ||
       (ce = cudaMalloc(reinterpret_cast<void**>(&c->comm.counters), allreduce_epoch_bytes())) != cudaSuccess ||
       (ce = cudaMemset(c->comm.counters, 0, allreduce_epoch_bytes())) != cudaSuccess ||
-      (ce = cudaMalloc(reinterpret_cast<void**>(&c->keys), (size_t)(c->comm.n_max / 2 + 1) * 8)) != cudaSuccess) {
+      (ce = cudaMalloc(reinterpret_cast<void**>(&c->keys), (size_t)(c->comm.n_max / 2 + 1) * 8)) != cudaSuccess ||
+      (ce = cudaMalloc(reinterpret_cast<void**>(&c->partial), (size_t)c->comm.n_max * sizeof(float))) != cudaSuccess) {
     cudaGetLastError();
     qw_allreduce_destroy(c);
     return cuda_fail(ce, "allreduce buffer allocation");
@@ -922,16 +924,29 @@ int qw_allreduce_connect(qw_allreduce* c, const unsigned char* handles) {
   return QW_OK;
 }
 
-int qw_allreduce_sum(qw_allreduce* c, const qw_array* partial, qw_array* y, void* stream) {
-  set_error("");
-  int rc;
+}  // extern "C"
+
+namespace {
+// A communicator call runs on the communicator's device, once every rank's
+// buffer is mapped.
+int check_comm_ready(const qw_allreduce* c) {
   if (!c) return fail(QW_EINVAL, "comm is null");
-  if ((rc = check_array(partial, "partial")) || (rc = check_array(y, "y"))) return rc;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev != c->device)
     return fail(QW_EINVAL, "the current device is not the communicator's (device " + std::to_string(c->device) + ")");
   for (int r = 0; r < c->comm.P; ++r)
     if (!c->comm.peer_bufs[r]) return fail(QW_EINVAL, "rank " + std::to_string(r) + " is not connected");
+  return QW_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int qw_allreduce_sum(qw_allreduce* c, const qw_array* partial, qw_array* y, void* stream) {
+  set_error("");
+  int rc;
+  if ((rc = check_comm_ready(c))) return rc;
+  if ((rc = check_array(partial, "partial")) || (rc = check_array(y, "y"))) return rc;
   if (partial->dtype != QW_F32) return fail(QW_EINVAL, "partial must be float32");
   if (y->dtype != QW_F16 && y->dtype != QW_F32) return fail(QW_EINVAL, "y must be float16 or float32");
   const int64_t n = numel(partial);
@@ -946,20 +961,55 @@ int qw_allreduce_sum(qw_allreduce* c, const qw_array* partial, qw_array* y, void
   return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "allreduce launch");
 }
 
+int qw_allreduce_matmul(qw_allreduce* c, const qw_array* x, const qw_array* w, const qw_array* scales,
+                        const qw_array* biases, int group_size, int bits, const char* mode, qw_array* y,
+                        void* stream) {
+  set_error("");
+  int rc;
+  if ((rc = check_comm_ready(c))) return rc;
+  SkinnyArgs sa;
+  if ((rc = check_qmm_call(x, w, scales, biases, 1, group_size, bits, mode, y, &sa))) return rc;
+  const int64_t n = sa.M * sa.N;
+  if (n > c->comm.n_max)
+    return fail(QW_EINVAL, std::to_string(n) + " output elements exceed the communicator's " +
+                               std::to_string(c->comm.n_max));
+  if (n == 0) return QW_OK;  // nothing is launched, on every rank alike
+  cudaStream_t st = as_stream(stream);
+  sa.ar = &c->comm;
+  if (skinny_config(group_size, bits) && skinny_exchange_fits(sa)) {
+    DeviceRes* res = nullptr;
+    std::string err;
+    if (!device_res(c->device, &res, &err)) return fail(QW_ENOMEM, err);
+    sa.status = res->status;
+    Scratch sc;
+    if (!scratch_for(c->device, st, skinny_scratch_bytes(sa, c->device), &sc, &err)) return fail(QW_ENOMEM, err);
+    const cudaError_t ce = launch_skinny(sa, sc, st, pdl_enabled(), &err);
+    if (ce != cudaSuccess) return err.empty() ? cuda_fail(ce, "skinny launch") : fail(QW_ECUDA, err);
+    return QW_OK;
+  }
+  // Larger shapes: this rank's fp32 product, then the allreduce kernel.
+  qw_array part{};
+  part.data = c->partial;
+  part.dtype = QW_F32;
+  part.ndim = 2;
+  part.shape[0] = sa.M;
+  part.shape[1] = sa.N;
+  if ((rc = run_qmm(x, w, scales, biases, 1, group_size, bits, mode, &part, stream))) return rc;
+  const bool y32 = y->dtype == QW_F32;
+  const bool vec = n % 4 == 0 && aligned(y->data, y32 ? 16 : 8);
+  const cudaError_t ce = launch_allreduce(c->comm, c->partial, y->data, y32, vec, n, c->sm_count, st);
+  return ce == cudaSuccess ? QW_OK : cuda_fail(ce, "allreduce launch");
+}
+
 int qw_allreduce_argmax(qw_allreduce* c, const qw_array* x, const qw_array* w, const qw_array* scales,
                         const qw_array* biases, int group_size, int bits, const char* mode, int64_t index_base,
                         qw_array* logits, qw_array* idx, void* stream) {
   set_error("");
-  if (!c) return fail(QW_EINVAL, "comm is null");
+  int rc;
+  if ((rc = check_comm_ready(c))) return rc;
   WeightDims d;
   int64_t M = 0, x_ld = 0;
-  int rc = check_argmax_call(x, w, scales, biases, group_size, bits, mode, logits, idx, &d, &M, &x_ld);
-  if (rc != QW_OK) return rc;
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev != c->device)
-    return fail(QW_EINVAL, "the current device is not the communicator's (device " + std::to_string(c->device) + ")");
-  for (int r = 0; r < c->comm.P; ++r)
-    if (!c->comm.peer_bufs[r]) return fail(QW_EINVAL, "rank " + std::to_string(r) + " is not connected");
+  if ((rc = check_argmax_call(x, w, scales, biases, group_size, bits, mode, logits, idx, &d, &M, &x_ld))) return rc;
   if (index_base < 0 || index_base + d.N > (int64_t)0xFFFFFFFF)
     return fail(QW_EINVAL, "the shard's rows [index_base, index_base + N) must lie below 2^32 - 1");
   if (2 * M > c->comm.n_max)
@@ -986,6 +1036,7 @@ int qw_allreduce_destroy(qw_allreduce* c) {
   if (c->own) cudaFree(c->own);
   if (c->comm.counters) cudaFree(c->comm.counters);
   if (c->keys) cudaFree(c->keys);
+  if (c->partial) cudaFree(c->partial);
   cudaGetLastError();
   cudaSetDevice(prev);
   delete c;

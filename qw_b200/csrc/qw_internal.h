@@ -39,6 +39,8 @@ struct Scratch {
 };
 
 // Skinny path (M <= 16): stream-K over (row tile, 512-wide k chunk) units.
+struct ArComm;
+
 struct SkinnyArgs {
   const void* x;         // fp16 [M][K], rows x_ld apart
   const uint32_t* w;     // [N][K/8]
@@ -60,7 +62,14 @@ struct SkinnyArgs {
   const uint32_t* w2 = nullptr;
   const void* scales2 = nullptr;
   const void* biases2 = nullptr;
+  // Row-parallel projection under tensor parallelism (M <= 16, not SwiGLU,
+  // no greedy keys): y = the sum over the communicator's ranks of every
+  // rank's x W^T, exchanged through the communicator's buffers in the
+  // kernel's epilogue.  Null: y is this rank's product alone.
+  const ArComm* ar = nullptr;
 };
+// Whether a skinny launch can fuse the row-parallel exchange for this shape.
+bool skinny_exchange_fits(const SkinnyArgs& a);
 // Skinny-path scratch layout: split-tile counters (zero between launches) at
 // the start, then the partial-sum slots.
 constexpr size_t kSkinnyMaxCounters = 1u << 16;  // row tiles per launch

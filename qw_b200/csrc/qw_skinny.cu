@@ -37,7 +37,17 @@
 // One token with 4-bit codes: the 8 groups of a unit are the 8 columns of
 // the MMAs (group gi's B fragment is x in the lanes of column gi and zero in
 // the others), so one accumulator pair collects the whole unit and the fold
-// below runs once per unit instead of once per group.
+// below runs once per unit instead of once per group.  This path also comes
+// with 16-group units (1024 k, four boxes a stage, a fold per 8 groups):
+// 512 contiguous bytes per weight row per stage and half the units, chosen
+// per shape by the host.
+//
+// Row-parallel exchange (a separate instantiation, XCHG): the launch is one
+// rank's K-slice of a tensor-parallel projection, and y is the sum over the
+// ranks.  Finished tiles go to this rank's slot of the communicator's buffer
+// (qw_exchange.cuh); after its last unit a CTA copies its tiles into every
+// peer's buffer, flags them, waits (bounded) for every rank's flags of the
+// same tiles, and sums them in rank order into y.
 //
 // Consumer arithmetic (no per-element dequantisation): a packed word w holds
 // nibbles q0..q7 (k ascending).  lop3(w & 0x000F000F | 0x64006400) is the fp16
@@ -59,6 +69,7 @@
 
 #include <mutex>
 
+#include "qw_exchange.cuh"
 #include "qw_internal.h"
 #include "qw_ptx.cuh"
 
@@ -83,7 +94,11 @@ constexpr int align1k(int v) { return (v + 1023) / 1024 * 1024; }
 //     kernel's bytes-in-flight budget against HBM latency.
 //   small ring (SST stages): the unit's x box and what the helper warps derive
 //     from it (MMA B fragments, per-group X / Z sums).  x comes from L2.
-template <int MT, int BITS = 4>
+// WIDE: 16 groups (1024 k) per unit instead of 8, for the one-token 4-bit
+// column scheme: 512 contiguous bytes per weight row per stage, half the
+// units and so half the per-unit fixed costs.  The host picks it per shape
+// (launch_skinny), since larger units leave a short launch less balanced.
+template <int MT, int BITS = 4, bool WIDE = false>
 struct SkinnyCfg {
   static constexpr int NT = (MT + 7) / 8;       // n8 MMA column tiles
   static constexpr int MPAD_ = 8 * NT;
@@ -101,11 +116,9 @@ struct SkinnyCfg {
   static constexpr bool COLS = BITS == 4 && (MT == 1 || MT == 4);
   static constexpr int TPC = MT == 4 ? 4 : 1;  // token columns per group
   static constexpr int GPC = 8 / TPC;          // groups per accumulator chain
-#ifndef QWV_GPS1
-#define QWV_GPS1 8
-#endif
+  static_assert(!WIDE || (COLS && TPC == 1), "16-group units are built for the one-token column scheme");
   // 64-wide groups per unit (per pipeline stage): the unit is 128 rows x 64 GPS k
-  static constexpr int GPS = (COLS && TPC == 1) ? QWV_GPS1 : 8;
+  static constexpr int GPS = WIDE ? 16 : 8;
   static constexpr int CK = kGroup * GPS;       // k per unit
   static constexpr int NBOX = GPS * kGroup * BITS / 8 / 128;  // 128-byte TMA boxes of a unit's codes
   // Ring depths: the one-token 4-bit path measured fastest with two weight
@@ -143,7 +156,11 @@ struct SkinnyCfg {
   static constexpr int OFF_RECV = OFF_COMB + COMB_BYTES;
   static constexpr int OFF_BAR = OFF_RECV + RECV_BYTES;
   static constexpr int NBAR = 2 * WST + 3 * SST + 1;  // wfull, wempty | sfull, ready, sempty | recv
-  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  // after the barriers: MISC_INTS words (abort, two finish flags, exchange
+  // tile count, epoch, status), then the tiles this CTA exchanges
+  static constexpr int MISC_INTS = 8;
+  static constexpr int XLIST_MAX = 32;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + (MISC_INTS + XLIST_MAX) * 4 + 1024;
   static constexpr int THREADS = (2 + HW + CW) * 32;
   // registers per thread: the whole register file over the CTA's warps
   static constexpr int MAXREG = (65536 / THREADS) & ~7;
@@ -196,6 +213,7 @@ struct SkinnyLaunch {
   unsigned int* gbar;     // [n_ops]: CTAs done with each matmul, zero at launch (n_ops > 1)
   unsigned long long* amax;  // one matmul only, may be null: [M] greedy-token keys (atomicMax)
   unsigned int* status;   // device status word
+  ArParams ar;            // one matmul only: ar.P > 0 sums y over the ranks in the epilogue
 };
 
 __device__ __forceinline__ long long unit_begin(long long i, long long U, int G) { return (i * U) / G; }
@@ -266,10 +284,14 @@ __device__ __forceinline__ bool wait_matmuls_done(const unsigned int* gbar, unsi
   return true;
 }
 
-template <int MT, int OPS_MAX, int BITS>
-__global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__((SkinnyCfg<MT, BITS>::MAXREG))
-    qmm_skinny_kernel(const __grid_constant__ SkinnyLaunch<OPS_MAX> p) {
-  using Cfg = SkinnyCfg<MT, BITS>;
+// XCHG: the row-parallel exchange in the epilogue (p.ar); a separate
+// instantiation, so the plain kernel carries none of its code.
+template <int MT, int OPS_MAX, int BITS, bool WIDE, bool XCHG>
+__global__ void __launch_bounds__((SkinnyCfg<MT, BITS, WIDE>::THREADS), 1)
+    __maxnreg__((SkinnyCfg<MT, BITS, WIDE>::MAXREG))
+        qmm_skinny_kernel(const __grid_constant__ SkinnyLaunch<OPS_MAX> p) {
+  using Cfg = SkinnyCfg<MT, BITS, WIDE>;
+  static_assert(!XCHG || OPS_MAX == 1, "the exchange takes single-matmul launches");
   constexpr int NT = Cfg::NT;
   constexpr int WST = Cfg::WST;
   constexpr int SST = Cfg::SST;
@@ -286,6 +308,10 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
   uint64_t* recv_bar = sempty + SST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + Cfg::NBAR);
   volatile int* fin_flag = abort_flag + 1;  // [2]: tile+1 to finish per partial slot, 0 = none
+  volatile int* xcount = abort_flag + 3;    // row-parallel exchange: tiles this CTA stored
+  volatile unsigned int* xepoch = reinterpret_cast<volatile unsigned int*>(abort_flag + 4);
+  volatile int* xok = abort_flag + 5;       // the exchange may go on (no abort, no peer timeout)
+  volatile int* xlist = abort_flag + Cfg::MISC_INTS;
   uint8_t* wring = smem + Cfg::OFF_WRING;
   uint8_t* sring = smem + Cfg::OFF_SRING;
 
@@ -316,6 +342,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
     *abort_flag = 0;
     fin_flag[0] = 0;
     fin_flag[1] = 0;
+    *xcount = 0;
     fence_barrier_init();
   }
   if (p.split > 1) {
@@ -661,6 +688,13 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
   const int wrow = cw * 8;
   const int r = lane / 4, s4 = lane % 4;
   pdl_wait();
+  // Row-parallel exchange: this call's epoch, read once the previous kernel
+  // of the stream (the previous call's last CTA included) has completed;
+  // kept in shared memory, not in registers across the main loop.
+  if constexpr (XCHG) {
+    if (cw == 0 && lane == 0) *xepoch = ar_next_epoch(p.ar);
+    asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+  }
 
   float acc[NT][4];
 #pragma unroll
@@ -690,6 +724,9 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
         }
       return;
     }
+    // row-parallel exchange: this rank's fp32 product goes to its own slot
+    // (parity, rank) first; the final phase pushes it to the peers
+    float* const yx = XCHG ? ar_slot(p.ar, p.ar.rank, (int)(*xepoch & 1u), p.ar.rank) : nullptr;
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
@@ -698,12 +735,19 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
         const int row = tile * Cfg::BN + wrow + r + ((e & 2) ? Cfg::BN / 2 : 0);
         if (n < p.M && row < op.N) {
           const size_t idx = (size_t)n * op.N + row;
-          if (!op.y) {
+          if (yx) {
+            yx[idx] = v[tt][e];
+          } else if (!op.y) {
           } else if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = v[tt][e];
           else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(v[tt][e]);
           if (p.amax) best[tt][e & 1] = umax64(best[tt][e & 1], amax_key(v[tt][e], row));
         }
       }
+    if (XCHG && cw == 0 && lane == 0) {
+      const int c = *xcount;
+      if (c < Cfg::XLIST_MAX) xlist[c] = tile;
+      *xcount = c + 1;
+    }
   };
 
   // ldmatrix lane addressing: matrix mi = lane/8 covers rows 8*(mi&1).. of
@@ -1150,6 +1194,85 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS>::THREADS), 1) __maxnreg__
       asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
     }
   }
+  if constexpr (XCHG) {
+    // Row-parallel exchange.  Every tile this CTA stored is in slot
+    // (parity, rank) of this rank's buffer: copy it into the same slot of
+    // every other rank's buffer, flag the tiles in every rank's buffer (tile
+    // t is chunk t), wait for every rank's flags of the same tiles in this
+    // rank's buffer, and sum each tile over the ranks in rank order (every
+    // rank gets identical y).  A CTA flags all its tiles before it waits on
+    // any, so no CTA waits on one that is itself waiting.  Every rank runs
+    // the same grid over the same tiles, so each tile is flagged once by
+    // every rank whichever CTA finished it.
+    const SkinnyOp& op = p.op[0];
+    const unsigned int xe = *xepoch;
+    const int xpar = (int)(xe & 1u);
+    if (cw == 0 && lane == 0) *xok = *abort_flag ? 0 : 1;
+    // every consumer's slot stores precede the flags
+    asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+    int nx = *xcount;
+    if (nx > Cfg::XLIST_MAX) nx = Cfg::XLIST_MAX;
+    if (*xok) {
+      if (p.ar.P > 1) {
+        // the tiles' rows, 16 bytes a thread (a tile row of one token is 512
+        // contiguous bytes); N % 4 == 0 keeps them aligned, else 4 bytes
+        const float* mine = ar_slot(p.ar, p.ar.rank, xpar, p.ar.rank);
+        const bool v4 = (op.N & 3) == 0;
+        const int per_tile = v4 ? p.M * (Cfg::BN / 4) : p.M * Cfg::BN;
+        for (int q = cw * 32 + lane; q < nx * per_tile; q += Cfg::CW * 32) {
+          const int tile = xlist[q / per_tile];
+          const int qi = q % per_tile;
+          if (v4) {
+            const int n = qi / (Cfg::BN / 4);
+            const int row = tile * Cfg::BN + (qi % (Cfg::BN / 4)) * 4;
+            if (row >= op.N) continue;
+            const size_t idx = (size_t)n * op.N + row;
+            const float4 val = __ldcg(reinterpret_cast<const float4*>(mine + idx));
+            for (int d = 1; d < p.ar.P; ++d) {
+              const int dst = (p.ar.rank + d) % p.ar.P;
+              *reinterpret_cast<float4*>(ar_slot(p.ar, dst, xpar, p.ar.rank) + idx) = val;
+            }
+          } else {
+            const int n = qi / Cfg::BN;
+            const int row = tile * Cfg::BN + qi % Cfg::BN;
+            if (row >= op.N) continue;
+            const size_t idx = (size_t)n * op.N + row;
+            const float val = __ldcg(mine + idx);
+            for (int d = 1; d < p.ar.P; ++d) {
+              const int dst = (p.ar.rank + d) % p.ar.P;
+              ar_slot(p.ar, dst, xpar, p.ar.rank)[idx] = val;
+            }
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+      }
+      if (cw == 0 && lane < p.ar.P) {
+        __threadfence_system();
+        for (int i = 0; i < nx; ++i) st_release_sys(ar_flag_ptr(p.ar, lane, xpar, p.ar.rank, xlist[i]), xe);
+        bool ok = true;
+        for (int i = 0; i < nx && ok; ++i) ok = ar_wait_flag(p.ar, ar_flag_ptr(p.ar, p.ar.rank, xpar, lane, xlist[i]), xe);
+        if (!ok) *xok = 0;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
+      if (*xok) {
+        const float* slots = ar_slot(p.ar, p.ar.rank, xpar, 0);
+        for (int i = 0; i < nx; ++i) {
+          const int tile = xlist[i];
+          for (int q = cw * 32 + lane; q < p.M * Cfg::BN; q += Cfg::CW * 32) {
+            const int n = q / Cfg::BN;
+            const int row = tile * Cfg::BN + q % Cfg::BN;
+            if (row >= op.N) continue;
+            const size_t idx = (size_t)n * op.N + row;
+            float sum = 0.f;
+            for (int rr = 0; rr < p.ar.P; ++rr) sum += __ldcg(slots + (size_t)rr * p.ar.n_max + idx);
+            if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = sum;
+            else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(sum);
+          }
+        }
+      }
+    }
+    if (cw == 0 && lane == 0) ar_count_done(p.ar, xe);
+  }
   if (p.amax) {
     // Greedy token: reduce the keys over the warp (lanes of one s4 share
     // tokens), then over the consumer warps through shared memory (the
@@ -1181,9 +1304,9 @@ constexpr size_t kGbarBytes = 256;
 static_assert(kSkinnyChainMax * sizeof(unsigned int) <= kGbarBytes, "per-matmul tallies fit");
 
 // One matmul's descriptor: tensor maps and schedule-independent sizes.
-template <int MT, int BITS>
+template <int MT, int BITS, bool WIDE>
 bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
-  using Cfg = SkinnyCfg<MT, BITS>;
+  using Cfg = SkinnyCfg<MT, BITS, WIDE>;
   op->N = (int)a.N;
   op->K = (int)a.K;
   op->C = (int)((a.K + Cfg::CK - 1) / Cfg::CK);
@@ -1237,59 +1360,79 @@ bool make_op(const SkinnyArgs& a, SkinnyOp* op, std::string* err) {
   return true;
 }
 
-template <int MT, int OPS_MAX, int BITS>
+template <int MT, int OPS_MAX, int BITS, bool WIDE, bool XCHG>
 cudaError_t set_smem_attr(int dev) {
   static thread_local int configured_dev = -1;
   // cudaFuncSetAttribute is per device; cheap enough to repeat on change.
   if (configured_dev != dev) {
-    cudaError_t e = cudaFuncSetAttribute(qmm_skinny_kernel<MT, OPS_MAX, BITS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SkinnyCfg<MT, BITS>::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(qmm_skinny_kernel<MT, OPS_MAX, BITS, WIDE, XCHG>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SkinnyCfg<MT, BITS, WIDE>::SMEM);
     if (e != cudaSuccess) return e;
     configured_dev = dev;
   }
   return cudaSuccess;
 }
 
-template <int MT, int BITS>
+// Schedule of one matmul: with fewer row tiles than SMs, each tile gets
+// `split` CTAs (a thread-block cluster reducing through distributed shared
+// memory; one CTA per tile when split == 1).  Otherwise stream-K over all
+// SMs.  With 16 tokens (clusters of at most 2) stream-K also takes the
+// small-T shapes where it gives the busiest CTA fewer units: 5120 x 17408
+// runs in 32.3 us instead of 43.2 (17 chunks per CTA in pairs, 10 units
+// under stream-K).  With up to 8 tokens clusters of 3-4 stayed faster even
+// where stream-K's busiest CTA has fewer units (5120 x 17408 at M=1: 17.0 us
+// in clusters of 3, 19.0 us under stream-K).
+struct SkinnyPlan {
+  long long G;        // CTAs
+  int split;          // CTAs per tile (1: stream-K, or one CTA per tile)
+  long long busiest;  // units of the busiest CTA
+};
+
+template <int MT, int BITS, bool WIDE>
+SkinnyPlan plan_cfg(const SkinnyArgs& a, int sm_count) {
+  using Cfg = SkinnyCfg<MT, BITS, WIDE>;
+  const long long tile_rows = a.swiglu ? Cfg::BN / 2 : Cfg::BN;
+  const long long T = (a.N + tile_rows - 1) / tile_rows;
+  const long long C = (a.K + Cfg::CK - 1) / Cfg::CK;
+  const long long U = T * C;
+  SkinnyPlan pl{sm_count, 1, 0};
+  if (a.max_ctas > 0 && pl.G > a.max_ctas) pl.G = a.max_ctas;
+  if (T <= pl.G) {
+    long long split = pl.G / T;
+    if (split > Cfg::SPLIT_MAX) split = Cfg::SPLIT_MAX;
+    if (split > C) split = C;
+    if (split < 1) split = 1;
+    const long long cluster_span = (C + split - 1) / split;  // chunks of the busiest CTA
+    const long long sk_span = (U + pl.G - 1) / pl.G;          // units of the busiest stream-K CTA
+    if (MT < 16 || sk_span >= cluster_span) {
+      pl.split = (int)split;
+      pl.G = T * split;
+    }
+  }
+  if (pl.G > U) pl.G = U;
+  pl.busiest = pl.split > 1 ? (C + pl.split - 1) / pl.split : (U + pl.G - 1) / pl.G;
+  return pl;
+}
+
+template <int MT, int BITS, bool WIDE>
 cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                        std::string* err) {
-  using Cfg = SkinnyCfg<MT, BITS>;
+  using Cfg = SkinnyCfg<MT, BITS, WIDE>;
   int dev = 0;
   cudaGetDevice(&dev);
   const DeviceInfo& di = device_info(dev);
-  cudaError_t e = set_smem_attr<MT, 1, BITS>(dev);
+  const bool xchg = a.ar != nullptr;
+  cudaError_t e = xchg ? set_smem_attr<MT, 1, BITS, WIDE, true>(dev) : set_smem_attr<MT, 1, BITS, WIDE, false>(dev);
   if (e != cudaSuccess) return e;
   SkinnyLaunch<1> p{};
-  if (!make_op<MT, BITS>(a, &p.op[0], err)) return cudaErrorInvalidValue;
+  if (!make_op<MT, BITS, WIDE>(a, &p.op[0], err)) return cudaErrorInvalidValue;
   p.n_ops = 1;
   p.M = (int)a.M;
   const SkinnyOp& op = p.op[0];
-  // Schedule: with fewer row tiles than SMs, each tile gets `split` CTAs (a
-  // thread-block cluster reducing through distributed shared memory; one
-  // CTA per tile when split == 1).  Otherwise stream-K over all SMs.
-  // With 16 tokens (clusters of at most 2) stream-K also takes the small-T
-  // shapes where it gives the busiest CTA fewer units: 5120 x 17408 runs in
-  // 32.3 us instead of 43.2 (17 chunks per CTA in pairs, 10 units under
-  // stream-K).  With up to 8 tokens clusters of 3-4 stayed faster even where
-  // stream-K's busiest CTA has fewer units (5120 x 17408 at M=1: 17.0 us in
-  // clusters of 3, 19.0 us under stream-K).
-  long long G = (long long)di.sm_count;
-  if (a.max_ctas > 0 && G > a.max_ctas) G = a.max_ctas;
-  p.split = 1;
-  if (op.T <= G) {
-    int split = (int)(G / op.T);
-    if (split > Cfg::SPLIT_MAX) split = Cfg::SPLIT_MAX;
-    if (split > op.C) split = op.C;
-    if (split < 1) split = 1;
-    const long long cluster_span = (op.C + split - 1) / split;  // chunks of the busiest CTA
-    const long long sk_span = (op.U + G - 1) / G;              // units of the busiest stream-K CTA
-    if (MT < 16 || sk_span >= cluster_span) {
-      p.split = split;
-      G = (long long)op.T * split;
-    }
-  }
-  if (G > op.U) G = op.U;
-  p.G = (int)G;
+  const SkinnyPlan pl = plan_cfg<MT, BITS, WIDE>(a, di.sm_count);
+  p.split = pl.split;
+  p.G = (int)pl.G;
   p.op[0].G = p.G;
   const size_t need = kGbarBytes + kCounterBytes + (size_t)p.G * 2 * Cfg::PART * sizeof(float);
   if (scratch.bytes < need || scratch.base == nullptr) {
@@ -1302,6 +1445,18 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   p.part = reinterpret_cast<float*>(base + kGbarBytes + kCounterBytes);
   p.status = a.status;
   p.amax = a.amax;
+  if (xchg) {
+    // Each CTA lists the tiles it stores: one under a cluster split, else
+    // at most the tiles its range of units touches.
+    const long long span = (op.U + p.G - 1) / p.G;
+    const long long tiles_per_cta = p.split > 1 ? 1 : (span + op.C - 1) / op.C + 1;
+    if (!skinny_exchange_fits(a) || tiles_per_cta > Cfg::XLIST_MAX || a.M * a.N > a.ar->n_max ||
+        a.ar->P < 1 || a.ar->P > kArMaxRanks) {
+      *err = "this shape cannot fuse the row-parallel exchange into the decode kernel";
+      return cudaErrorInvalidValue;
+    }
+    p.ar = ar_params(*a.ar);
+  }
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.G);
@@ -1324,7 +1479,8 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   }
   cfg.attrs = attr;
   cfg.numAttrs = nattr;
-  return cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, 1, BITS>, p);
+  return xchg ? cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, 1, BITS, WIDE, true>, p)
+              : cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, 1, BITS, WIDE, false>, p);
 }
 
 // A chain of up to kSkinnyChainMax matmuls in one cooperative launch of one
@@ -1332,18 +1488,18 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
 template <int MT>
 cudaError_t launch_chain_cfg(const SkinnyArgs* ops, int n, const Scratch& scratch, cudaStream_t stream,
                              std::string* err) {
-  using Cfg = SkinnyCfg<MT, 4>;  // chains take 4-bit codes
+  using Cfg = SkinnyCfg<MT, 4, false>;  // chains take 4-bit codes in 8-group units
   int dev = 0;
   cudaGetDevice(&dev);
   const DeviceInfo& di = device_info(dev);
-  cudaError_t e = set_smem_attr<MT, kSkinnyChainMax, 4>(dev);
+  cudaError_t e = set_smem_attr<MT, kSkinnyChainMax, 4, false, false>(dev);
   if (e != cudaSuccess) return e;
   static SkinnyLaunch<kSkinnyChainMax> p;  // large: build it outside the stack (copied at launch)
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
   p = SkinnyLaunch<kSkinnyChainMax>{};
   for (int i = 0; i < n; ++i)
-    if (!make_op<MT, 4>(ops[i], &p.op[i], err)) return cudaErrorInvalidValue;
+    if (!make_op<MT, 4, false>(ops[i], &p.op[i], err)) return cudaErrorInvalidValue;
   p.n_ops = n;
   p.M = (int)ops[0].M;
   p.G = di.sm_count;
@@ -1374,7 +1530,7 @@ cudaError_t launch_chain_cfg(const SkinnyArgs* ops, int n, const Scratch& scratc
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, kSkinnyChainMax, 4>, p);
+  return cudaLaunchKernelEx(&cfg, qmm_skinny_kernel<MT, kSkinnyChainMax, 4, false, false>, p);
 }
 
 }  // namespace
@@ -1384,6 +1540,12 @@ size_t skinny_scratch_bytes(const SkinnyArgs& a, int device) {
   const int mpad = a.M <= 8 ? 8 : 16;
   const int BN = 128;
   return kGbarBytes + kCounterBytes + (size_t)di.sm_count * 2 * BN * mpad * sizeof(float);
+}
+
+bool skinny_exchange_fits(const SkinnyArgs& a) {
+  // one flag chunk per 128-row tile
+  return a.M >= 1 && a.M <= 16 && !a.swiglu && !a.amax && a.y != nullptr &&
+         (a.N + SkinnyCfg<1>::BN - 1) / SkinnyCfg<1>::BN <= kArMaxChunks;
 }
 
 size_t skinny_zeroed_bytes(const SkinnyArgs& a) {
@@ -1396,14 +1558,28 @@ size_t skinny_zeroed_bytes(const SkinnyArgs& a) {
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                           std::string* err) {
   if (a.bits == 8) {
-    if (a.M == 1) return launch_cfg<1, 8>(a, scratch, stream, pdl, err);
-    if (a.M <= 8) return launch_cfg<8, 8>(a, scratch, stream, pdl, err);
-    return launch_cfg<16, 8>(a, scratch, stream, pdl, err);
+    if (a.M == 1) return launch_cfg<1, 8, false>(a, scratch, stream, pdl, err);
+    if (a.M <= 8) return launch_cfg<8, 8, false>(a, scratch, stream, pdl, err);
+    return launch_cfg<16, 8, false>(a, scratch, stream, pdl, err);
   }
-  if (a.M == 1) return launch_cfg<1, 4>(a, scratch, stream, pdl, err);
-  if (a.M <= 4) return launch_cfg<4, 4>(a, scratch, stream, pdl, err);
-  if (a.M <= 8) return launch_cfg<8, 4>(a, scratch, stream, pdl, err);
-  return launch_cfg<16, 4>(a, scratch, stream, pdl, err);
+  if (a.M == 1) {
+    // 16-group units unless they leave the busiest CTA with more than 10%
+    // more k to stream than 8-group units (8192 x 5120: 3 units of 1024 k
+    // per CTA in pairs against 5 of 512; there the wide units ran 11.3 us
+    // against 10.5).  Where both give the same k the wide units were faster:
+    // 17408 x 5120 13.3 against 13.8 us, 5120 x 17408 15.4 against 16.4,
+    // lm_head (151936 x 5120, 1% more k) 76.2 against 86.2.
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sm = device_info(dev).sm_count;
+    const SkinnyPlan p8 = plan_cfg<1, 4, false>(a, sm), p16 = plan_cfg<1, 4, true>(a, sm);
+    const long long k8 = p8.busiest * SkinnyCfg<1, 4, false>::CK, k16 = p16.busiest * SkinnyCfg<1, 4, true>::CK;
+    if (k16 * 10 <= k8 * 11) return launch_cfg<1, 4, true>(a, scratch, stream, pdl, err);
+    return launch_cfg<1, 4, false>(a, scratch, stream, pdl, err);
+  }
+  if (a.M <= 4) return launch_cfg<4, 4, false>(a, scratch, stream, pdl, err);
+  if (a.M <= 8) return launch_cfg<8, 4, false>(a, scratch, stream, pdl, err);
+  return launch_cfg<16, 4, false>(a, scratch, stream, pdl, err);
 }
 
 cudaError_t launch_skinny_chain(const SkinnyArgs* ops, int n, const Scratch& scratch, cudaStream_t stream,

@@ -126,21 +126,26 @@ class LinearStack:
     fp16; `swiglu(x, (wq, s, b))` (optional) returns silu(gate) * up of the
     rank's gate_up shard, whose first half of rows is its gate plane and
     second half the matching up rows, so the activation needs no exchange
-    between ranks.  Row-parallel shards need every rank to run the same
-    sequence of collectives, which this fixed order guarantees.
+    between ranks; `rowpar(x, (wq, s, b))` (optional) runs a row-parallel
+    projection with its sum over ranks in one call and returns fp16 (the
+    library's qw_allreduce_matmul) in place of matmul, allreduce and to_half.
+    Row-parallel shards need every rank to run the same sequence of
+    collectives, which this fixed order guarantees.
     """
 
     def __init__(self, layers: Sequence[Dict[str, tuple]], lm_head: tuple, P: int, rank: int,
                  matmul: Callable, allreduce: Callable, to_half: Callable, dims: StackDims = BASELINE,
-                 swiglu: Callable = None):
+                 swiglu: Callable = None, rowpar: Callable = None):
         self.layers, self.lm_head = layers, lm_head
         self.P, self.rank, self.dims = P, rank, dims
         self.matmul, self.allreduce, self.to_half = matmul, allreduce, to_half
-        self.swiglu = swiglu
+        self.swiglu, self.rowpar = swiglu, rowpar
 
     def _rowpar(self, x, w):
         if self.P == 1:
             return self.matmul(x, w, False)
+        if self.rowpar is not None:
+            return self.rowpar(x, w)
         return self.to_half(self.allreduce(self.matmul(x, w, True)))
 
     def layer(self, h, w):
@@ -295,6 +300,17 @@ class PeerAllreduce:
             self._comm, _arr(x), _arr(w[0]), _arr(w[1]), _arr(w[2]), group_size, bits, _mode(mode),
             int(index_base), _arr(logits), _arr(idx), _stream(x)))
         return idx
+
+    def matmul(self, x, w, out, group_size: int = 64, bits: int = 4, mode: str = "affine"):
+        """Row-parallel projection (qw_allreduce_matmul): out (fp16 or fp32
+        [M, N]) = the sum over ranks of each rank's x @ dequantize(w).T over
+        its K-slice, summed in rank order and rounded once.  For M <= 16 the
+        exchange runs in the decode kernel's epilogue (one launch)."""
+        from .ops import _arr, _mode, _stream
+        self._lib.check(self._lib.load().qw_allreduce_matmul(
+            self._comm, _arr(x), _arr(w[0]), _arr(w[1]), _arr(w[2]), group_size, bits, _mode(mode), _arr(out),
+            _stream(x)))
+        return out
 
     def __call__(self, partial, out):
         """out (fp16 or fp32) = sum over ranks of partial (fp32, same numel)."""

@@ -229,4 +229,8 @@ def test_allreduce_init_bounds():
     assert L.qw_allreduce_init(2, 2, 1024, ctypes.byref(comm), h) == _lib.QW_EINVAL
     assert L.qw_allreduce_init(2, 0, 0, ctypes.byref(comm), h) == _lib.QW_EINVAL
     assert L.qw_allreduce_sum(None, _arr([4], _lib.QW_F32), _arr([4], _lib.QW_F16), None) == _lib.QW_EINVAL
+    assert L.qw_allreduce_matmul(None, _arr([1, 64], _lib.QW_F16), _arr([8, 8], _lib.QW_U32),
+                                 _arr([8, 1], _lib.QW_F16), _arr([8, 1], _lib.QW_F16), 64, 4, b"affine",
+                                 _arr([1, 8], _lib.QW_F16), None) == _lib.QW_EINVAL
+    assert b"comm is null" in L.qw_last_error()
     assert L.qw_allreduce_destroy(None) == _lib.QW_OK

@@ -1,6 +1,8 @@
 """Tensor-parallel linear stack on P GPUs, the o/down partial sums exchanged
-by NCCL (fp32 allreduce, then a cast) or by the library's one-shot peer
-allreduce (qw_allreduce_sum, fp16 rounding fused).
+by NCCL (fp32 allreduce, then a cast), by the library's one-shot peer
+allreduce (qw_allreduce_sum, fp16 rounding fused), or inside the o/down
+matmul itself (qw_allreduce_matmul: the decode kernel's epilogue for up to
+16 rows, the matmul and the allreduce kernel above).
 
 Checked two ways: against the same stack unsharded on one GPU (isolates the
 sharding and the allreduce: only fp32 summation order differs), and against
@@ -68,7 +70,8 @@ def _rank_main(rank, world, port, x, out_q, mode="nccl"):
         def mm(xx, w, out_f32):
             return qw_b200.quantized_matmul(xx, *w, out_dtype=torch.float32 if out_f32 else torch.float16)
 
-        if mode == "peer":
+        rowpar = None
+        if mode in ("peer", "fused"):
             ar = tp.PeerAllreduce(64 * DIMS.hidden)
 
             def allreduce(t):  # fp32 partials in, fp16 sums out
@@ -81,7 +84,12 @@ def _rank_main(rank, world, port, x, out_q, mode="nccl"):
         def swiglu(xx, w):
             return qw_b200.quantized_matmul_swiglu(xx, *[t for half in tp.gate_up_halves(w) for t in half])
 
-        stack = tp.LinearStack(mine, lm_mine, world, rank, mm, allreduce, lambda t: t.half(), DIMS, swiglu=swiglu)
+        if mode == "fused":
+            def rowpar(xx, w):
+                return ar.matmul(xx, w, torch.empty(xx.shape[0], w[0].shape[0], dtype=torch.float16, device=dev))
+
+        stack = tp.LinearStack(mine, lm_mine, world, rank, mm, allreduce, lambda t: t.half(), DIMS, swiglu=swiglu,
+                               rowpar=rowpar)
         torch.cuda.synchronize()
         for M in (1, 16, 64):
             y = stack.forward(torch.from_numpy(x[:M]).to(dev))
@@ -93,7 +101,7 @@ def _rank_main(rank, world, port, x, out_q, mode="nccl"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["nccl", "peer"])
+@pytest.mark.parametrize("mode", ["nccl", "peer", "fused"])
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_stack_matches_oracle(world, mode):
     if torch.cuda.device_count() < world:
