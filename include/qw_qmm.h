@@ -201,7 +201,8 @@ int qw_quantized_matmul_static_scratch(const qw_array* x, const qw_array* w, con
  * ncclAllReduce(float32, sum) + fp16 cast of the tensor-parallel stack.
  *
  * Set-up: qw_allreduce_init on every rank (allocates and zeroes this rank's
- * buffer for up to max_elems floats per call and returns its IPC handle,
+ * buffer for up to max_elems floats per call, 64 KiB + 8 P max_elems +
+ * 16 P min(max_elems, 2^21) bytes, and returns its IPC handle,
  * QW_IPC_HANDLE_BYTES bytes); exchange the handles (any host transport);
  * qw_allreduce_connect with all ranks' handles in rank order; then a
  * barrier across ranks before the first qw_allreduce_sum.  Peers store into
@@ -223,13 +224,14 @@ int qw_allreduce_destroy(qw_allreduce* comm);
  * holds x_r [M, K_r] and w_r (scales, biases as in qw_quantized_matmul) [N,
  * K_r] of a K-split (the same N on every rank).  Every rank receives the
  * fp32 products summed in rank order and rounded once: bit for bit
- * qw_quantized_matmul into f32 then qw_allreduce_sum.  For M <= 16 the
- * exchange runs in the decode kernel's epilogue (each tile stored into every
- * rank's slot, flagged, waited for and summed by the CTA that finished it):
- * one launch instead of two.  Larger M runs the matmul into the
- * communicator's fp32 buffer and then the allreduce kernel.  A collective
- * call of the same sequence as qw_allreduce_sum (all ranks, same order, same
- * M and N); M * N <= max_elems.
+ * qw_quantized_matmul into f32 then qw_allreduce_sum.  For M <= 16 and
+ * M * N <= min(max_elems, 2^21) the exchange runs in the decode kernel: each
+ * finished value goes to every rank as one 64-bit word tagged with the
+ * call's epoch, and a few extra CTAs of the same launch wait for every
+ * rank's words and sum them; one launch instead of two.  Otherwise the call
+ * runs the matmul into the communicator's fp32 buffer and then the allreduce
+ * kernel.  A collective call of the same sequence as qw_allreduce_sum (all
+ * ranks, same order, same M and N); M * N <= max_elems.
  * Replaces: the o and down projections of a layer split over GPUs
  * (crates/runtime/src/qwen3_next.rs:142-160, 458-487 run them on one
  * device) followed by ncclAllReduce(float32, sum) and a cast. */

@@ -172,8 +172,11 @@ __global__ void __launch_bounds__(kArThreads) argmax_exchange_kernel(const ArPar
 }  // namespace
 
 size_t allreduce_buffer_bytes(int P, int64_t n_max) {
-  return kArFlagBytes + (size_t)2 * P * (size_t)n_max * sizeof(float);
+  return kArFlagBytes + (size_t)2 * P * (size_t)n_max * sizeof(float) +
+         (size_t)2 * P * (size_t)ar_ll_elems(n_max) * sizeof(unsigned long long);
 }
+
+int64_t allreduce_ll_elems(int64_t n_max) { return ar_ll_elems(n_max); }
 
 size_t allreduce_epoch_bytes() { return 2 * sizeof(unsigned int); }
 

@@ -976,7 +976,7 @@ int qw_allreduce_matmul(qw_allreduce* c, const qw_array* x, const qw_array* w, c
   if (n == 0) return QW_OK;  // nothing is launched, on every rank alike
   cudaStream_t st = as_stream(stream);
   sa.ar = &c->comm;
-  if (skinny_config(group_size, bits) && skinny_exchange_fits(sa)) {
+  if (skinny_config(group_size, bits) && skinny_exchange_fits(sa) && n <= allreduce_ll_elems(c->comm.n_max)) {
     DeviceRes* res = nullptr;
     std::string err;
     if (!device_res(c->device, &res, &err)) return fail(QW_ENOMEM, err);

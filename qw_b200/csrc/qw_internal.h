@@ -68,7 +68,8 @@ struct SkinnyArgs {
   // kernel's epilogue.  Null: y is this rank's product alone.
   const ArComm* ar = nullptr;
 };
-// Whether a skinny launch can fuse the row-parallel exchange for this shape.
+// Whether a skinny launch can fuse the row-parallel exchange for this shape
+// (the communicator's ll slots must also hold M N values).
 bool skinny_exchange_fits(const SkinnyArgs& a);
 // Skinny-path scratch layout: split-tile counters (zero between launches) at
 // the start, then the partial-sum slots.
@@ -140,6 +141,8 @@ struct ArComm {
   int64_t n_max = 0;
 };
 size_t allreduce_buffer_bytes(int P, int64_t n_max);
+// Outputs a fused row-parallel exchange can carry (the ll slots' length).
+int64_t allreduce_ll_elems(int64_t n_max);
 size_t allreduce_epoch_bytes();
 // idx[m] = the global greedy token of row m over every rank's vocabulary
 // shard: keys[m] is this rank's best (value, local index) key and its shard

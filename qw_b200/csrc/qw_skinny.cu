@@ -156,11 +156,10 @@ struct SkinnyCfg {
   static constexpr int OFF_RECV = OFF_COMB + COMB_BYTES;
   static constexpr int OFF_BAR = OFF_RECV + RECV_BYTES;
   static constexpr int NBAR = 2 * WST + 3 * SST + 1;  // wfull, wempty | sfull, ready, sempty | recv
-  // after the barriers: MISC_INTS words (abort, two finish flags, exchange
-  // tile count, epoch, status), then the tiles this CTA exchanges
-  static constexpr int MISC_INTS = 8;
-  static constexpr int XLIST_MAX = 32;
-  static constexpr int SMEM = OFF_BAR + NBAR * 8 + (MISC_INTS + XLIST_MAX) * 4 + 1024;
+  // after the barriers: MISC_INTS words (abort, two finish flags, the
+  // exchange's epoch)
+  static constexpr int MISC_INTS = 4;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + MISC_INTS * 4 + 1024;
   static constexpr int THREADS = (2 + HW + CW) * 32;
   // registers per thread: the whole register file over the CTA's warps
   static constexpr int MAXREG = (65536 / THREADS) & ~7;
@@ -308,10 +307,7 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS, WIDE>::THREADS), 1)
   uint64_t* recv_bar = sempty + SST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + Cfg::NBAR);
   volatile int* fin_flag = abort_flag + 1;  // [2]: tile+1 to finish per partial slot, 0 = none
-  volatile int* xcount = abort_flag + 3;    // row-parallel exchange: tiles this CTA stored
-  volatile unsigned int* xepoch = reinterpret_cast<volatile unsigned int*>(abort_flag + 4);
-  volatile int* xok = abort_flag + 5;       // the exchange may go on (no abort, no peer timeout)
-  volatile int* xlist = abort_flag + Cfg::MISC_INTS;
+  volatile unsigned int* xepoch = reinterpret_cast<volatile unsigned int*>(abort_flag + 3);  // exchange epoch
   uint8_t* wring = smem + Cfg::OFF_WRING;
   uint8_t* sring = smem + Cfg::OFF_SRING;
 
@@ -342,7 +338,6 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS, WIDE>::THREADS), 1)
     *abort_flag = 0;
     fin_flag[0] = 0;
     fin_flag[1] = 0;
-    *xcount = 0;
     fence_barrier_init();
   }
   if (p.split > 1) {
@@ -724,9 +719,9 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS, WIDE>::THREADS), 1)
         }
       return;
     }
-    // row-parallel exchange: this rank's fp32 product goes to its own slot
-    // (parity, rank) first; the final phase pushes it to the peers
-    float* const yx = XCHG ? ar_slot(p.ar, p.ar.rank, (int)(*xepoch & 1u), p.ar.rank) : nullptr;
+    // row-parallel exchange: this rank's fp32 products go, each with the
+    // call's epoch, into ll slot (parity, rank) of every rank
+    const unsigned int xe = XCHG ? *xepoch : 0u;
 #pragma unroll
     for (int tt = 0; tt < NT; ++tt)
 #pragma unroll
@@ -735,19 +730,15 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS, WIDE>::THREADS), 1)
         const int row = tile * Cfg::BN + wrow + r + ((e & 2) ? Cfg::BN / 2 : 0);
         if (n < p.M && row < op.N) {
           const size_t idx = (size_t)n * op.N + row;
-          if (yx) {
-            yx[idx] = v[tt][e];
+          if (XCHG) {
+            for (int q = 0; q < p.ar.P; ++q)
+              ar_ll_store(ar_ll_slot(p.ar, q, (int)(xe & 1u), p.ar.rank) + idx, v[tt][e], xe);
           } else if (!op.y) {
           } else if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = v[tt][e];
           else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(v[tt][e]);
           if (p.amax) best[tt][e & 1] = umax64(best[tt][e & 1], amax_key(v[tt][e], row));
         }
       }
-    if (XCHG && cw == 0 && lane == 0) {
-      const int c = *xcount;
-      if (c < Cfg::XLIST_MAX) xlist[c] = tile;
-      *xcount = c + 1;
-    }
   };
 
   // ldmatrix lane addressing: matrix mi = lane/8 covers rows 8*(mi&1).. of
@@ -1195,79 +1186,57 @@ __global__ void __launch_bounds__((SkinnyCfg<MT, BITS, WIDE>::THREADS), 1)
     }
   }
   if constexpr (XCHG) {
-    // Row-parallel exchange.  Every tile this CTA stored is in slot
-    // (parity, rank) of this rank's buffer: copy it into the same slot of
-    // every other rank's buffer, flag the tiles in every rank's buffer (tile
-    // t is chunk t), wait for every rank's flags of the same tiles in this
-    // rank's buffer, and sum each tile over the ranks in rank order (every
-    // rank gets identical y).  A CTA flags all its tiles before it waits on
-    // any, so no CTA waits on one that is itself waiting.  Every rank runs
-    // the same grid over the same tiles, so each tile is flagged once by
-    // every rank whichever CTA finished it.
+    // Row-parallel exchange.  A worker CTA (blockIdx < op.G) stored every
+    // value it finished, with the call's epoch, into every rank's ll slot
+    // as it wrote its tiles; it exits without waiting, so its SM is free for
+    // the next kernel's weight stream.  The grid's last F CTAs are
+    // finishers with no units: finisher f reads the rows of tiles
+    // [f T / F, (f + 1) T / F) of every token from every rank's slot in this
+    // rank's buffer,
+    // waiting (bounded) on each word until it carries the epoch, and sums
+    // them in rank order into y (every rank gets identical y).  Workers
+    // never wait on finishers, so the grid completes whether or not the
+    // finishers are resident from the start.
     const SkinnyOp& op = p.op[0];
     const unsigned int xe = *xepoch;
-    const int xpar = (int)(xe & 1u);
-    if (cw == 0 && lane == 0) *xok = *abort_flag ? 0 : 1;
-    // every consumer's slot stores precede the flags
-    asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
-    int nx = *xcount;
-    if (nx > Cfg::XLIST_MAX) nx = Cfg::XLIST_MAX;
-    if (*xok) {
-      if (p.ar.P > 1) {
-        // the tiles' rows, 16 bytes a thread (a tile row of one token is 512
-        // contiguous bytes); N % 4 == 0 keeps them aligned, else 4 bytes
-        const float* mine = ar_slot(p.ar, p.ar.rank, xpar, p.ar.rank);
-        const bool v4 = (op.N & 3) == 0;
-        const int per_tile = v4 ? p.M * (Cfg::BN / 4) : p.M * Cfg::BN;
-        for (int q = cw * 32 + lane; q < nx * per_tile; q += Cfg::CW * 32) {
-          const int tile = xlist[q / per_tile];
-          const int qi = q % per_tile;
-          if (v4) {
-            const int n = qi / (Cfg::BN / 4);
-            const int row = tile * Cfg::BN + (qi % (Cfg::BN / 4)) * 4;
-            if (row >= op.N) continue;
-            const size_t idx = (size_t)n * op.N + row;
-            const float4 val = __ldcg(reinterpret_cast<const float4*>(mine + idx));
-            for (int d = 1; d < p.ar.P; ++d) {
-              const int dst = (p.ar.rank + d) % p.ar.P;
-              *reinterpret_cast<float4*>(ar_slot(p.ar, dst, xpar, p.ar.rank) + idx) = val;
-            }
+    if ((int)blockIdx.x >= op.G) {
+      const int xpar = (int)(xe & 1u);
+      const int F = (int)gridDim.x - op.G, f = (int)blockIdx.x - op.G;
+      const int t0 = (int)((long long)f * op.T / F), t1 = (int)((long long)(f + 1) * op.T / F);
+      const int R = (t1 - t0) * Cfg::BN;  // rows [t0 BN, t1 BN) of a token are contiguous
+      const unsigned long long* slots = ar_ll_slot(p.ar, p.ar.rank, xpar, 0);
+      if ((op.N & 1) == 0 && (reinterpret_cast<uintptr_t>(op.y) & (op.y_f32 ? 7u : 3u)) == 0) {
+        // pairs of outputs (R and N even: a pair never straddles a token;
+        // y aligned for the pair's store)
+        for (int q = 2 * (cw * 32 + lane); q < p.M * R; q += 2 * Cfg::CW * 32) {
+          const int n = q / R;
+          const int row = t0 * Cfg::BN + q % R;
+          if (row >= op.N) continue;
+          const size_t idx = (size_t)n * op.N + row;
+          float s0, s1;
+          if (!ar_ll_sum2(p.ar, slots + idx, p.ar.n_ll, xe, &s0, &s1)) break;
+          if (op.y_f32) {
+            *reinterpret_cast<float2*>(reinterpret_cast<float*>(op.y) + idx) = make_float2(s0, s1);
           } else {
-            const int n = qi / Cfg::BN;
-            const int row = tile * Cfg::BN + qi % Cfg::BN;
-            if (row >= op.N) continue;
-            const size_t idx = (size_t)n * op.N + row;
-            const float val = __ldcg(mine + idx);
-            for (int d = 1; d < p.ar.P; ++d) {
-              const int dst = (p.ar.rank + d) % p.ar.P;
-              ar_slot(p.ar, dst, xpar, p.ar.rank)[idx] = val;
-            }
+            *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(op.y) + idx) = __floats2half2_rn(s0, s1);
           }
         }
-        asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
-      }
-      if (cw == 0 && lane < p.ar.P) {
-        __threadfence_system();
-        for (int i = 0; i < nx; ++i) st_release_sys(ar_flag_ptr(p.ar, lane, xpar, p.ar.rank, xlist[i]), xe);
+      } else {
         bool ok = true;
-        for (int i = 0; i < nx && ok; ++i) ok = ar_wait_flag(p.ar, ar_flag_ptr(p.ar, p.ar.rank, xpar, lane, xlist[i]), xe);
-        if (!ok) *xok = 0;
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::CW * 32) : "memory");
-      if (*xok) {
-        const float* slots = ar_slot(p.ar, p.ar.rank, xpar, 0);
-        for (int i = 0; i < nx; ++i) {
-          const int tile = xlist[i];
-          for (int q = cw * 32 + lane; q < p.M * Cfg::BN; q += Cfg::CW * 32) {
-            const int n = q / Cfg::BN;
-            const int row = tile * Cfg::BN + q % Cfg::BN;
-            if (row >= op.N) continue;
-            const size_t idx = (size_t)n * op.N + row;
-            float sum = 0.f;
-            for (int rr = 0; rr < p.ar.P; ++rr) sum += __ldcg(slots + (size_t)rr * p.ar.n_max + idx);
-            if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = sum;
-            else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(sum);
+        for (int q = cw * 32 + lane; q < p.M * R && ok; q += Cfg::CW * 32) {
+          const int n = q / R;
+          const int row = t0 * Cfg::BN + q % R;
+          if (row >= op.N) continue;
+          const size_t idx = (size_t)n * op.N + row;
+          float sum = 0.f;
+          for (int rr = 0; rr < p.ar.P && ok; ++rr) {
+            float v = 0.f;
+            ok = ar_ll_load(p.ar, slots + (size_t)rr * p.ar.n_ll + idx, xe, &v);
+            sum += v;
           }
+          if (!ok) break;
+          if (op.y_f32) reinterpret_cast<float*>(op.y)[idx] = sum;
+          else reinterpret_cast<__half*>(op.y)[idx] = __float2half_rn(sum);
         }
       }
     }
@@ -1446,20 +1415,29 @@ cudaError_t launch_cfg(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t
   p.status = a.status;
   p.amax = a.amax;
   if (xchg) {
-    // Each CTA lists the tiles it stores: one under a cluster split, else
-    // at most the tiles its range of units touches.
-    const long long span = (op.U + p.G - 1) / p.G;
-    const long long tiles_per_cta = p.split > 1 ? 1 : (span + op.C - 1) / op.C + 1;
-    if (!skinny_exchange_fits(a) || tiles_per_cta > Cfg::XLIST_MAX || a.M * a.N > a.ar->n_max ||
-        a.ar->P < 1 || a.ar->P > kArMaxRanks) {
+    if (!skinny_exchange_fits(a) || a.M * a.N > ar_ll_elems(a.ar->n_max) || a.ar->P < 1 ||
+        a.ar->P > kArMaxRanks) {
       *err = "this shape cannot fuse the row-parallel exchange into the decode kernel";
       return cudaErrorInvalidValue;
     }
     p.ar = ar_params(*a.ar);
   }
+  // Exchange finishers: about one CTA per 512 outputs (a pair of outputs
+  // per consumer thread), at most the SMs the workers leave idle, whole
+  // clusters under a cluster split.
+  long long grid = p.G;
+  if (xchg) {
+    long long F = (a.M * a.N + 511) / 512;
+    const long long idle = di.sm_count - p.G;
+    if (F > idle) F = idle;
+    if (F > op.T) F = op.T;
+    if (F < 1) F = 1;
+    F = (F + p.split - 1) / p.split * p.split;
+    grid += F;
+  }
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)p.G);
+  cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(Cfg::THREADS);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = stream;
@@ -1543,9 +1521,7 @@ size_t skinny_scratch_bytes(const SkinnyArgs& a, int device) {
 }
 
 bool skinny_exchange_fits(const SkinnyArgs& a) {
-  // one flag chunk per 128-row tile
-  return a.M >= 1 && a.M <= 16 && !a.swiglu && !a.amax && a.y != nullptr &&
-         (a.N + SkinnyCfg<1>::BN - 1) / SkinnyCfg<1>::BN <= kArMaxChunks;
+  return a.M >= 1 && a.M <= 16 && !a.swiglu && !a.amax && a.y != nullptr;
 }
 
 size_t skinny_zeroed_bytes(const SkinnyArgs& a) {
@@ -1566,15 +1542,19 @@ cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStrea
     // 16-group units unless they leave the busiest CTA with more than 10%
     // more k to stream than 8-group units (8192 x 5120: 3 units of 1024 k
     // per CTA in pairs against 5 of 512; there the wide units ran 11.3 us
-    // against 10.5).  Where both give the same k the wide units were faster:
+    // against 10.5), or lose the TMA path for scales and biases that 8-group
+    // units have (K a multiple of 512 but not of 1024, as the down shard at
+    // TP=2).  Where both give the same k the wide units were faster:
     // 17408 x 5120 13.3 against 13.8 us, 5120 x 17408 15.4 against 16.4,
     // lm_head (151936 x 5120, 1% more k) 76.2 against 86.2.
     int dev = 0;
     cudaGetDevice(&dev);
     const int sm = device_info(dev).sm_count;
+    constexpr int CK8 = SkinnyCfg<1, 4, false>::CK, CK16 = SkinnyCfg<1, 4, true>::CK;
     const SkinnyPlan p8 = plan_cfg<1, 4, false>(a, sm), p16 = plan_cfg<1, 4, true>(a, sm);
-    const long long k8 = p8.busiest * SkinnyCfg<1, 4, false>::CK, k16 = p16.busiest * SkinnyCfg<1, 4, true>::CK;
-    if (k16 * 10 <= k8 * 11) return launch_cfg<1, 4, true>(a, scratch, stream, pdl, err);
+    const long long k8 = p8.busiest * CK8, k16 = p16.busiest * CK16;
+    const bool tma_sb8 = a.K % CK8 == 0 && a.group_size == kGroup, tma_sb16 = a.K % CK16 == 0 && a.group_size == kGroup;
+    if (k16 * 10 <= k8 * 11 && (tma_sb16 || !tma_sb8)) return launch_cfg<1, 4, true>(a, scratch, stream, pdl, err);
     return launch_cfg<1, 4, false>(a, scratch, stream, pdl, err);
   }
   if (a.M <= 4) return launch_cfg<4, 4, false>(a, scratch, stream, pdl, err);
