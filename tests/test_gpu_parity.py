@@ -98,6 +98,18 @@ def test_ragged_shapes(M, N, K):
     assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL
 
 
+@pytest.mark.parametrize("N,K", [(300, 2112), (5000, 2176), (4000, 3648)])
+def test_one_token_wide_units_ragged(N, K):
+    """One token on shapes where the host takes 16-group (1024-wide) units
+    although K is not a multiple of 1024: a partial last chunk, scales and
+    biases staged with plain loads, and a ragged last row tile."""
+    wq, s, b = quantized(N, K, seed=N ^ K)
+    x = synth.activations(1, K, seed=K)
+    _, y_ref = oracle.quantized_matmul(x, wq, s, b, want_f32=True)
+    assert rel_err(run_qmm(x, wq, s, b), y_ref) <= TOL
+    assert rel_err(run_qmm(x, wq, s, b, out_dtype=torch.float32), y_ref) <= 1e-3
+
+
 @pytest.mark.parametrize("M", [1, 4, 16])
 def test_single_config_full_size(M):
     """BASELINE config: W [17408, 5120] 4-bit group 64, x ~ N(0, 1)."""
