@@ -736,6 +736,90 @@ def run_case(args):
                       "TFLOPs": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 2)}), flush=True)
 
 
+def run_tp_calls(args):
+    """Per-call device time of the tensor-parallel row-parallel patterns on
+    this world's shards (torchrun, N > 1): the o and down shards as a matmul
+    alone, as a matmul into fp32 plus qw_allreduce_sum, and fused
+    (qw_allreduce_matmul); the q|k|v and lm_head shards as matmuls.  Each
+    pattern is a CUDA graph over 8 weight copies (more than L2 for the
+    row-parallel shards), replayed 20 times after a barrier; max over ranks.
+    Rank 0 prints one JSON line."""
+    import torch
+    import torch.distributed as dist
+    import qw_b200 as qw
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev)
+    ar = tp.PeerAllreduce(2048 * synth.HIDDEN)
+    copies, iters = 8, 20
+    s = torch.cuda.Stream(dev)
+
+    def timed(calls):
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                for f in calls:
+                    f()
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for f in calls:
+                f()
+        with torch.cuda.stream(s):
+            g.replay()
+        s.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            for _ in range(iters):
+                g.replay()
+            e1.record(s)
+        s.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) * 1000.0 / (iters * len(calls))], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del g
+        return round(t.item(), 2)
+
+    out = {"metric": "per-call device time of TP shards (us, max over ranks)", "n_gpus": world, "M": 1}
+    lins = {l.name: l for l in synth.layer_linears()}
+    for name in ("o", "down"):
+        N, K = tp.shard_shape(lins[name], world)
+        sets = [make_weights(torch, qw, N, K, seed=100 * i + rank, dev=dev) for i in range(copies)]
+        x = torch.randn(1, K, device=dev).half()
+        y = torch.empty(1, N, dtype=torch.float16, device=dev)
+        part = torch.empty(1, N, dtype=torch.float32, device=dev)
+
+        def mm(w):
+            return lambda: qw.quantized_matmul(x, *w, out=y)
+
+        def two(w):
+            return lambda: (qw.quantized_matmul(x, *w, out=part), ar(part, y))
+
+        def fused(w):
+            return lambda: ar.matmul(x, w, y)
+
+        out[f"{name}_{N}x{K}"] = {"matmul": timed([mm(w) for w in sets]),
+                                  "matmul_then_allreduce": timed([two(w) for w in sets]),
+                                  "fused": timed([fused(w) for w in sets])}
+        del sets
+    for name, lin in (("qkv", lins["qkv"]), ("lm_head", synth.LM_HEAD)):
+        N, K = tp.shard_shape(lin, world)
+        sets = [make_weights(torch, qw, N, K, seed=100 * i + rank, dev=dev) for i in range(4 if name == "lm_head" else copies)]
+        x = torch.randn(1, K, device=dev).half()
+        y = torch.empty(1, N, dtype=torch.float16, device=dev)
+        out[f"{name}_{N}x{K}"] = {"matmul": timed([(lambda w=w: qw.quantized_matmul(x, *w, out=y)) for w in sets])}
+        del sets
+    out["device_status"] = qw.device_status(local, clear=False)
+    dist.barrier()
+    ar.close()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -750,10 +834,14 @@ def main():
     ap.add_argument("--case", default=None,
                     help="M,N,K | swiglu:M,I,K | b8:M,N,K | topk:M,N,k: time one kernel on one shape only "
                          "(small device footprint, for ncu)")
+    ap.add_argument("--tp-calls", action="store_true",
+                    help="under torchrun: per-call times of the tensor-parallel shards and exchanges")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.case:
+    if args.tp_calls:
+        run_tp_calls(args)
+    elif args.case:
         run_case(args)
     elif args.impl == "reference":
         run_reference(args)
