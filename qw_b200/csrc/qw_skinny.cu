@@ -1379,6 +1379,15 @@ SkinnyPlan plan_cfg(const SkinnyArgs& a, int sm_count) {
       pl.G = T * split;
     }
   }
+  if (pl.split == 1 && T > pl.G) {
+    // Whole tiles per CTA where that keeps the busiest CTA's units: no split
+    // tiles, so no partial sums, counters or end-of-launch fix-ups.  The
+    // fused SwiGLU gate|up at one token (272 tiles of 5 units: 2 tiles on
+    // each of 136 CTAs, against 9 or 10 units on each of 148 under stream-K)
+    // went from 25.5 to 21.4 us, the 64-layer stack from 3.69 to 3.47 ms.
+    const long long tpc = (T + pl.G - 1) / pl.G;
+    if (T % tpc == 0 && tpc * C <= (U + pl.G - 1) / pl.G) pl.G = T / tpc;
+  }
   if (pl.G > U) pl.G = U;
   pl.busiest = pl.split > 1 ? (C + pl.split - 1) / pl.split : (U + pl.G - 1) / pl.G;
   return pl;
