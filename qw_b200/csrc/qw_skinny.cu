@@ -1380,13 +1380,15 @@ SkinnyPlan plan_cfg(const SkinnyArgs& a, int sm_count) {
     }
   }
   if (pl.split == 1 && T > pl.G) {
-    // Whole tiles per CTA where that keeps the busiest CTA's units: no split
-    // tiles, so no partial sums, counters or end-of-launch fix-ups.  The
-    // fused SwiGLU gate|up at one token (272 tiles of 5 units: 2 tiles on
-    // each of 136 CTAs, against 9 or 10 units on each of 148 under stream-K)
-    // went from 25.5 to 21.4 us, the 64-layer stack from 3.69 to 3.47 ms.
+    // Whole tiles per CTA where that gives the busiest CTA at most 10% more
+    // units: no split tiles, so no partial sums, counters or end-of-launch
+    // fix-ups.  The fused SwiGLU gate|up (272 tiles, 2 on each of 136 CTAs)
+    // went from 25.5 to 21.4 us at one token (10 units a CTA either way),
+    // from 28.9 to 25.4 at four and from 45.9 to 43.3 at sixteen (20 units
+    // against 19 under stream-K); the one-token 64-layer stack from 3.69 to
+    // 3.47 ms.
     const long long tpc = (T + pl.G - 1) / pl.G;
-    if (T % tpc == 0 && tpc * C <= (U + pl.G - 1) / pl.G) pl.G = T / tpc;
+    if (T % tpc == 0 && tpc * C * 10 <= (U + pl.G - 1) / pl.G * 11) pl.G = T / tpc;
   }
   if (pl.G > U) pl.G = U;
   pl.busiest = pl.split > 1 ? (C + pl.split - 1) / pl.split : (U + pl.G - 1) / pl.G;

@@ -32,10 +32,11 @@ SIZES = [5120, 5121, 16 * 5120, 3]
 MIXED = [64 * 5120, 5120, 64 * 5120, 16 * 5120, 3, 5121, 64 * 5120, 16 * 5120, 5120] * 3
 # Row-parallel matmuls (M, N, K per rank, bits): the o and down shards of the
 # 27B layer at TP 8 and 2 (clusters of 2 and 3 CTAs per 128-row tile), 313
-# tiles over 148 CTAs (stream-K, split tiles), 136 tiles (one CTA each),
-# ragged N and M, 8-bit codes, and M = 17 (the matmul and the allreduce kernel).
+# tiles over 148 CTAs (stream-K, split tiles), 296 tiles two to a CTA (whole
+# tiles), 136 tiles (one CTA each), ragged N and M, 8-bit codes, and M = 17
+# (the matmul and the allreduce kernel).
 MATMULS = [(1, 5120, 768, 4), (1, 5120, 2176, 4), (4, 5120, 3072, 4), (16, 5120, 8704, 4), (1, 40000, 2048, 4),
-           (3, 1000, 512, 4), (8, 17408, 1024, 4), (2, 5120, 1024, 8), (17, 5120, 1024, 4)]
+           (1, 37888, 1024, 4), (3, 1000, 512, 4), (8, 17408, 1024, 4), (2, 5120, 1024, 8), (17, 5120, 1024, 4)]
 MM_MAX = max(m * n for m, n, _, _ in MATMULS)
 
 
