@@ -7,11 +7,13 @@ is the partition BASELINE asks for, Megatron style:
   holds rows [r*N/P, (r+1)*N/P) of every plane of a fused matrix (q|k|v and
   gate|up are sharded plane by plane, then re-fused per rank), with their
   scales and biases;
-* row-parallel (fp32 allreduce): o and down.  Each rank holds input columns
-  [r*K/P, (r+1)*K/P) of the packed weight, on group boundaries so that every
-  quantization group (and its scale/bias) lies wholly in one shard; the rank's
-  matmul returns fp32 partial sums that an allreduce adds before the single
-  fp16 rounding.
+* row-parallel (fp32 sum over ranks): o and down.  Each rank holds input
+  columns [r*K/P, (r+1)*K/P) of the packed weight, on group boundaries so that
+  every quantization group (and its scale/bias) lies wholly in one shard; the
+  ranks' fp32 products are added before the single fp16 rounding, inside the
+  decode kernel (PeerAllreduce.matmul, the library's qw_allreduce_matmul), by
+  the library's allreduce kernel after a matmul into fp32 (PeerAllreduce), or
+  by NCCL.
 
 Everything here is slicing and works on numpy arrays or torch tensors.
 """
