@@ -129,6 +129,8 @@ unsafe extern "C" {
     pub fn qw_allreduce_sum(comm: *mut QwAllreduce, partial: *const QwArray, y: *mut QwArray,
         stream: *mut c_void) -> c_int;
     pub fn qw_allreduce_destroy(comm: *mut QwAllreduce) -> c_int;
+    pub fn qw_decode_schedule(m: i64, n: i64, k: i64, bits: c_int, group_size: c_int, swiglu: c_int,
+        sm_count: c_int, out: *mut i64) -> c_int;
     pub fn qw_allreduce_matmul(comm: *mut QwAllreduce, x: *const QwArray, w: *const QwArray,
         scales: *const QwArray, biases: *const QwArray, group_size: c_int, bits: c_int,
         mode: *const c_char, y: *mut QwArray, stream: *mut c_void) -> c_int;

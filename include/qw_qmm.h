@@ -301,6 +301,17 @@ const char* qw_last_error(void);
  * nothing. */
 int qw_device_status(int device, unsigned int* status, int clear);
 
+/* The decode kernel's configuration and schedule for a matmul of m rows of x
+ * (1..16) against an n x k weight (for a SwiGLU call, n gate rows), on a GPU
+ * with sm_count SMs: the choice the matmul entry points make, computed on the
+ * host without touching a device.  out (int64 [5]) receives the rows of x
+ * the configuration takes (1, 4, 8 or 16), k per unit (512 or 1024), the
+ * CTAs that take units, the CTAs per row tile under a cluster split (1:
+ * stream-K or whole tiles per CTA) and the units of the busiest CTA.  For
+ * tests and tuning; no counterpart in the reference. */
+int qw_decode_schedule(int64_t m, int64_t n, int64_t k, int bits, int group_size, int swiglu, int sm_count,
+                       int64_t* out);
+
 /* QW_ABI_VERSION of the loaded library. */
 int qw_abi_version(void);
 

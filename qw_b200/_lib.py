@@ -57,6 +57,8 @@ SIGNATURES = {
     "qw_allreduce_connect": ([ctypes.c_void_p, ctypes.c_char_p], _I),
     "qw_allreduce_sum": ([ctypes.c_void_p, _PA, _PA, _P], _I),
     "qw_allreduce_destroy": ([ctypes.c_void_p], _I),
+    "qw_decode_schedule": ([ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _I, _I, _I, _I,
+                            ctypes.POINTER(ctypes.c_int64)], _I),
     "qw_allreduce_matmul": ([ctypes.c_void_p, _PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, _PA, _P], _I),
     "qw_allreduce_argmax": ([ctypes.c_void_p, _PA, _PA, _PA, _PA, _I, _I, ctypes.c_char_p, ctypes.c_int64, _PA, _PA,
                              _P], _I),

@@ -1164,6 +1164,32 @@ int qw_device_status(int device, unsigned int* status, int clear) {
   return v ? QW_ETIMEOUT : QW_OK;
 }
 
+int qw_decode_schedule(int64_t m, int64_t n, int64_t k, int bits, int group_size, int swiglu, int sm_count,
+                       int64_t* out) {
+  set_error("");
+  if (!out) return fail(QW_EINVAL, "out is null");
+  if (m < 1 || m > 16) return fail(QW_EINVAL, "the decode kernel takes 1 to 16 rows of x");
+  if (!skinny_config(group_size, bits))
+    return fail(QW_EUNSUPPORTED, "the decode kernel takes bits 4 or 8 in groups of 64 or 128");
+  if (n < 1 || k < 1 || k % group_size != 0 || n > ((int64_t)1 << 30) || k > ((int64_t)1 << 28))
+    return fail(QW_EINVAL, "n and k must be positive, k a multiple of group_size");
+  if (sm_count < 1) return fail(QW_EINVAL, "sm_count must be positive");
+  SkinnyArgs a{};
+  a.M = m;
+  a.N = n;
+  a.K = k;
+  a.bits = bits;
+  a.group_size = group_size;
+  a.swiglu = swiglu != 0;
+  const SkinnySchedule sc = skinny_schedule(a, sm_count);
+  out[0] = sc.tokens;
+  out[1] = sc.unit_k;
+  out[2] = sc.ctas;
+  out[3] = sc.split;
+  out[4] = sc.busiest_units;
+  return QW_OK;
+}
+
 int qw_abi_version(void) { return QW_ABI_VERSION; }
 
 }  // extern "C"

@@ -68,6 +68,16 @@ struct SkinnyArgs {
   // kernel's epilogue.  Null: y is this rank's product alone.
   const ArComm* ar = nullptr;
 };
+// The decode kernel's configuration and schedule for a matmul (the choice
+// launch_skinny makes, computed without touching a device).
+struct SkinnySchedule {
+  int tokens;               // rows of x the configuration takes (1, 4, 8 or 16)
+  int unit_k;               // k per unit (512 or 1024)
+  long long ctas;           // CTAs that take units
+  int split;                // CTAs per row tile under a cluster split (1: stream-K or whole tiles)
+  long long busiest_units;  // units of the busiest CTA
+};
+SkinnySchedule skinny_schedule(const SkinnyArgs& a, int sm_count);
 // Whether a skinny launch can fuse the row-parallel exchange for this shape
 // (the communicator's ll slots must also hold M N values).
 bool skinny_exchange_fits(const SkinnyArgs& a);

@@ -1542,6 +1542,49 @@ size_t skinny_zeroed_bytes(const SkinnyArgs& a) {
   return kGbarBytes + (tiles < kMaxCounters ? tiles : kMaxCounters) * sizeof(unsigned int);
 }
 
+namespace {
+// One token with 4-bit codes: 16-group units unless they leave the busiest
+// CTA with more than 10% more k to stream than 8-group units (8192 x 5120: 3
+// units of 1024 k per CTA in pairs against 5 of 512; there the wide units
+// ran 11.3 us against 10.5), or lose the TMA path for scales and biases that
+// 8-group units have (K a multiple of 512 but not of 1024, as the down shard
+// at TP=2).  Where both give the same k the wide units were faster: 17408 x
+// 5120 13.3 against 13.8 us, 5120 x 17408 15.4 against 16.4, lm_head
+// (151936 x 5120, 1% more k) 76.2 against 86.2.
+bool one_token_wide(const SkinnyArgs& a, int sm) {
+  constexpr int CK8 = SkinnyCfg<1, 4, false>::CK, CK16 = SkinnyCfg<1, 4, true>::CK;
+  const SkinnyPlan p8 = plan_cfg<1, 4, false>(a, sm), p16 = plan_cfg<1, 4, true>(a, sm);
+  const long long k8 = p8.busiest * CK8, k16 = p16.busiest * CK16;
+  const bool tma_sb8 = a.K % CK8 == 0 && a.group_size == kGroup, tma_sb16 = a.K % CK16 == 0 && a.group_size == kGroup;
+  return k16 * 10 <= k8 * 11 && (tma_sb16 || !tma_sb8);
+}
+
+template <int MT, int BITS, bool WIDE>
+SkinnySchedule schedule_of(const SkinnyArgs& a, int sm) {
+  const SkinnyPlan pl = plan_cfg<MT, BITS, WIDE>(a, sm);
+  SkinnySchedule sc;
+  sc.tokens = MT;
+  sc.unit_k = SkinnyCfg<MT, BITS, WIDE>::CK;
+  sc.ctas = pl.G;
+  sc.split = pl.split;
+  sc.busiest_units = pl.busiest;
+  return sc;
+}
+}  // namespace
+
+SkinnySchedule skinny_schedule(const SkinnyArgs& a, int sm_count) {
+  if (a.bits == 8) {
+    if (a.M == 1) return schedule_of<1, 8, false>(a, sm_count);
+    if (a.M <= 8) return schedule_of<8, 8, false>(a, sm_count);
+    return schedule_of<16, 8, false>(a, sm_count);
+  }
+  if (a.M == 1)
+    return one_token_wide(a, sm_count) ? schedule_of<1, 4, true>(a, sm_count) : schedule_of<1, 4, false>(a, sm_count);
+  if (a.M <= 4) return schedule_of<4, 4, false>(a, sm_count);
+  if (a.M <= 8) return schedule_of<8, 4, false>(a, sm_count);
+  return schedule_of<16, 4, false>(a, sm_count);
+}
+
 cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStream_t stream, bool pdl,
                           std::string* err) {
   if (a.bits == 8) {
@@ -1550,22 +1593,9 @@ cudaError_t launch_skinny(const SkinnyArgs& a, const Scratch& scratch, cudaStrea
     return launch_cfg<16, 8, false>(a, scratch, stream, pdl, err);
   }
   if (a.M == 1) {
-    // 16-group units unless they leave the busiest CTA with more than 10%
-    // more k to stream than 8-group units (8192 x 5120: 3 units of 1024 k
-    // per CTA in pairs against 5 of 512; there the wide units ran 11.3 us
-    // against 10.5), or lose the TMA path for scales and biases that 8-group
-    // units have (K a multiple of 512 but not of 1024, as the down shard at
-    // TP=2).  Where both give the same k the wide units were faster:
-    // 17408 x 5120 13.3 against 13.8 us, 5120 x 17408 15.4 against 16.4,
-    // lm_head (151936 x 5120, 1% more k) 76.2 against 86.2.
     int dev = 0;
     cudaGetDevice(&dev);
-    const int sm = device_info(dev).sm_count;
-    constexpr int CK8 = SkinnyCfg<1, 4, false>::CK, CK16 = SkinnyCfg<1, 4, true>::CK;
-    const SkinnyPlan p8 = plan_cfg<1, 4, false>(a, sm), p16 = plan_cfg<1, 4, true>(a, sm);
-    const long long k8 = p8.busiest * CK8, k16 = p16.busiest * CK16;
-    const bool tma_sb8 = a.K % CK8 == 0 && a.group_size == kGroup, tma_sb16 = a.K % CK16 == 0 && a.group_size == kGroup;
-    if (k16 * 10 <= k8 * 11 && (tma_sb16 || !tma_sb8)) return launch_cfg<1, 4, true>(a, scratch, stream, pdl, err);
+    if (one_token_wide(a, device_info(dev).sm_count)) return launch_cfg<1, 4, true>(a, scratch, stream, pdl, err);
     return launch_cfg<1, 4, false>(a, scratch, stream, pdl, err);
   }
   if (a.M <= 4) return launch_cfg<4, 4, false>(a, scratch, stream, pdl, err);

@@ -238,6 +238,16 @@ def quantize_weights(w: torch.Tensor, group_size: int = 64, bits: int = 4,
     return wq, s, b
 
 
+def decode_schedule(M: int, N: int, K: int, bits: int = 4, group_size: int = 64, swiglu: bool = False,
+                    sm_count: int = 148) -> dict:
+    """The decode kernel's configuration and schedule for a matmul of M (1..16)
+    rows of x against an N x K weight (qw_decode_schedule; no device access)."""
+    out = (ctypes.c_int64 * 5)()
+    _lib.check(_lib.load().qw_decode_schedule(int(M), int(N), int(K), bits, group_size, int(bool(swiglu)),
+                                              int(sm_count), out))
+    return {"tokens": out[0], "unit_k": out[1], "ctas": out[2], "split": out[3], "busiest_units": out[4]}
+
+
 def device_status(device: int = 0, clear: bool = True) -> int:
     """Device-side status word left by a kernel whose bounded wait ran out (0 = none)."""
     v = ctypes.c_uint(0)

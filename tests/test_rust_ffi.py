@@ -30,6 +30,7 @@ C_TO_RUST = {
     "unsigned char*": "*mut u8",
     "const unsigned char*": "*const u8",
     "unsigned int*": "*mut u32",
+    "int64_t*": "*mut i64",
 }
 
 
